@@ -1,0 +1,188 @@
+/*
+ * qcc_b200.h -- C ABI of the B200 indexed sparse gated-FFN engine.
+ *
+ * Every entry point takes plain device pointers, sizes and a cudaStream_t,
+ * launches on that stream, never synchronises and never allocates memory.
+ * Scratch memory is caller-provided ("workspace"); its size is given by the
+ * matching *_workspace_bytes() query and it must be zero-filled once with
+ * qcc_workspace_init() before first use (each call leaves it zeroed again).
+ * A workspace must not be shared by calls that can overlap on the GPU.
+ *
+ * Return value: QCC_OK (0) or one of the QCC_ERR_* host-side codes below.
+ * Conditions that are only visible on the device (an index out of range, a
+ * bounded wait that ran out) are recorded as QCC_DEV_* bits in the status
+ * word at the start of the workspace; qcc_workspace_status_offset() gives
+ * its byte offset so a caller can read it back when it chooses to sync.
+ *
+ * Packed weight layout (neuron-major, one record per intermediate neuron n):
+ *     record n = [ gate[n, 0:Hp] | up[n, 0:Hp] | down[0:Hp, n] ]
+ * with Hp = hidden rounded up to a multiple of 8 elements, zero padded, and record stride 3 * Hp * sizeof(dtype) bytes (30720 B for
+ * hidden = 5120 bf16).  The reference keeps gate [N,H], up [N,H] and
+ * down [H,N] as separate tensors (runtime/weights.py:89-96 writes only a
+ * separate transposed down); the interleaved record is new and lets one bulk
+ * copy fetch everything a selected neuron needs.
+ */
+#ifndef QCC_B200_H
+#define QCC_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+#include <cuda_runtime.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define QCC_API __attribute__((visibility("default")))
+#else
+#define QCC_API
+#endif
+
+#define QCC_ABI_VERSION 1
+
+/* Element types (weights, x, y, activations). */
+#define QCC_DTYPE_BF16 0
+#define QCC_DTYPE_F16 1
+#define QCC_DTYPE_F32 2
+/* Index types. */
+#define QCC_INDEX_I32 0
+#define QCC_INDEX_I64 1
+
+/* Host-side status codes. */
+#define QCC_OK 0
+#define QCC_ERR_INVALID_ARGUMENT 1 /* null pointer, negative size, bad enum */
+#define QCC_ERR_SHAPE 2            /* inconsistent sizes / strides            */
+#define QCC_ERR_DTYPE 3            /* unsupported dtype combination           */
+#define QCC_ERR_ALIGNMENT 4        /* pointer or stride not 16-byte aligned   */
+#define QCC_ERR_UNSUPPORTED 5      /* size beyond what the kernels handle     */
+#define QCC_ERR_WORKSPACE 6        /* workspace missing or too small          */
+#define QCC_ERR_CUDA 7             /* a CUDA runtime call or launch failed    */
+
+/* Device-side status bits (sticky, OR-ed into the workspace status word). */
+#define QCC_DEV_ID_RANGE 1u /* a selected id was outside [0, n_records)      */
+#define QCC_DEV_TIMEOUT 2u  /* a bounded wait on a bulk copy ran out          */
+
+/* Library version (QCC_ABI_VERSION). */
+QCC_API int qcc_version(void);
+
+/* Human-readable text for a QCC_ERR_* code (static storage). */
+QCC_API const char* qcc_status_string(int status);
+
+/* Text of the last CUDA error seen by this library on the calling thread. */
+QCC_API const char* qcc_last_cuda_error_string(void);
+
+/* Padded segment length Hp for a hidden size and dtype. */
+QCC_API int qcc_hidden_pad(int hidden, int dtype);
+
+/* Record stride in bytes: 3 * Hp * sizeof(dtype). */
+QCC_API int64_t qcc_record_bytes(int hidden, int dtype);
+
+/* ---------------------------------------------------------------------- */
+/* Packing                                                                 */
+/* ---------------------------------------------------------------------- */
+
+/*
+ * Build the neuron-major packed array from the reference's three tensors.
+ * Replaces the layout step of runtime/weights.py:89-96
+ * (save_neuron_major_layout) and the per-call gathers of
+ * runtime/ffn.py:20-23 (gather_weights): the gathers become one bulk copy
+ * per selected record inside qcc_indexed_ffn_decode.
+ *   gate, up : [n_records, hidden] row-major, row stride ld_gu elements
+ *   down     : element (h, n) at down[h * down_stride_h + n * down_stride_n]
+ *              ([hidden, n_records] row-major: (n_records, 1); the
+ *              reference's transposed down_t [n_records, hidden]: (1, hidden))
+ *   packed   : [n_records, 3 * Hp] (stride qcc_record_bytes)
+ */
+QCC_API int qcc_pack_records(const void* gate, const void* up, int64_t ld_gu, const void* down,
+                             int64_t down_stride_h, int64_t down_stride_n, int64_t n_records, int hidden, int dtype,
+                             void* packed, cudaStream_t stream);
+
+/* ---------------------------------------------------------------------- */
+/* Fused indexed gated FFN (decode / small batch)                          */
+/* ---------------------------------------------------------------------- */
+
+/* Largest batch one qcc_indexed_ffn_decode call accepts (4, or 2 when
+ * hidden > 5120 needs two hidden slots per thread); 0 if hidden is too big. */
+QCC_API int qcc_decode_max_batch(int hidden, int dtype);
+
+/* Bytes of workspace qcc_indexed_ffn_decode needs for this batch/hidden. */
+QCC_API size_t qcc_decode_workspace_bytes(int batch, int hidden, int dtype);
+
+/* Byte offset of the device status word inside any qcc workspace (0). */
+QCC_API size_t qcc_workspace_status_offset(void);
+
+/* Zero-fill a workspace on `stream` (cudaMemsetAsync; allocates nothing). */
+QCC_API int qcc_workspace_init(void* workspace, size_t workspace_bytes, cudaStream_t stream);
+
+/*
+ * y[b, :] = sum_j  m[j,b] * silu(G[id_j] . x[b]) * (U[id_j] . x[b]) * D[:, id_j]
+ * for the selected records id_j, j < n_ids, in one launch.
+ *
+ * Replaces runtime/cuda_indexed.py:61-64 (cuda_indexed_ffn ->
+ * indexed_ffn_cuda, two launches: gate_up then down) and
+ * runtime/ffn.py:34-39 (TorchDynamicSparseFFN.forward).  Math follows
+ * runtime/ffn.py:26-31: activation = silu(gate) * up, y = activation @ down.
+ * Accumulation is fp32 throughout; y is rounded once to y_dtype.
+ *
+ *   x          : [batch, hidden] in `dtype`, row stride ldx elements
+ *   packed     : qcc_pack_records layout, n_records records
+ *   ids        : n_ids selected record indices (QCC_INDEX_I32 or _I64); any
+ *                order, duplicates count twice (as index_select does);
+ *                out-of-range ids contribute nothing and raise QCC_DEV_ID_RANGE
+ *   n_ids_dev  : optional device int32 count; when non-null the kernel uses
+ *                min(*n_ids_dev, n_ids) ids (output of qcc_build_union)
+ *   token_mask : optional [n_ids] bytes; bit b set = token b uses record j.
+ *                Null means every token uses every record (the reference's
+ *                one shared 1-D id list, runtime/ffn.py:20-23).
+ *   y_out      : [batch, hidden] in y_dtype (dtype or QCC_DTYPE_F32)
+ *   activation_out : optional [batch, n_ids] in `dtype`, the per-record
+ *                activation (cuda_indexed_parts' first result,
+ *                runtime/cuda_indexed.py:56-59); entries of records a token
+ *                does not use are 0.
+ * batch must be 1..qcc_decode_max_batch(hidden, dtype) per call (a host
+ * wrapper chunks larger batches).
+ */
+QCC_API int qcc_indexed_ffn_decode(const void* x, int64_t ldx, int batch, int hidden, const void* packed, int64_t n_records,
+                           int dtype, const void* ids, int ids_dtype, int n_ids, const int32_t* n_ids_dev,
+                           const uint8_t* token_mask, void* workspace, size_t workspace_bytes, void* y_out,
+                           int64_t ldy, int y_dtype, void* activation_out, int64_t lda, cudaStream_t stream);
+
+/* ---------------------------------------------------------------------- */
+/* Selector                                                                */
+/* ---------------------------------------------------------------------- */
+
+/*
+ * Per row b of scores [batch, n] (fp32, row stride ld_scores): the k largest
+ * scores, ties broken by lower index, -0.0 == +0.0, NaN largest; written as
+ * k ascending unique int32 indices to ids_out[b * ld_ids + 0..k-1].
+ * Replaces torch.topk(scores, k, sorted=False) in runtime/selector.py:24,
+ * runtime/cuda_selector.py:40 and end_to_end/oracle_sparse_mlp.py:75, whose
+ * tie order is unspecified; this is the deterministic order
+ * sort(scores, descending, stable)[:k] then ascending.
+ * n * 4 bytes must fit in shared memory (n <= 53248).
+ */
+QCC_API int qcc_select_topk(const float* scores, int64_t ld_scores, int batch, int n, int k, int32_t* ids_out, int64_t ld_ids,
+                    cudaStream_t stream);
+
+/*
+ * Union of the per-token sorted id lists ids [batch, k] restricted to
+ * [id_begin, id_end), rebased to id_begin: union_ids gets the sorted
+ * distinct local ids, token_mask bit b says token b selected it, and
+ * *count_out (device int32) receives their number.  Capacity of union_ids
+ * and token_mask: min(id_end - id_begin, batch * k).  batch <= 8.
+ * Used for batched decode with per-token selections and for the
+ * intermediate-dimension shard of each rank.  No reference counterpart
+ * (the reference runs batch 1 with one id list, bridge.py:161-176).
+ */
+QCC_API int qcc_build_union(const int32_t* ids, int64_t ld_ids, int batch, int k, int32_t id_begin, int32_t id_end,
+                    int32_t* union_ids, uint8_t* token_mask, int32_t* count_out, cudaStream_t stream);
+
+/* Elementwise cast of n fp32 values to dtype (used after a cross-rank sum). */
+QCC_API int qcc_cast_f32(const float* src, void* dst, int64_t n, int dtype, cudaStream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* QCC_B200_H */

@@ -1,0 +1,163 @@
+// Library-wide C entry points: version, status text, workspace set-up, the
+// neuron-major packer and the fp32 cast used after a cross-rank sum.
+
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <mutex>
+
+#include "qcc_common.cuh"
+#include "qcc_host.h"
+
+namespace qcc {
+
+namespace {
+thread_local cudaError_t g_last_error = cudaSuccess;
+
+// record n = [gate[n, :Hp] | up[n, :Hp] | down[:Hp, n]], zero padded.
+// Grid-stride over (record, element) pairs: consecutive threads of a warp
+// write 32 consecutive elements of one record.  Down element (h, n) is read
+// at h * sh + n * sn (row-major [hidden, n_records] or the transposed copy).
+// Packing runs once per layer, so the strided down reads are not tuned.
+template <typename T>
+__global__ void pack_records_kernel(const T* __restrict__ gate, const T* __restrict__ up, int64_t ld_gu,
+                                    const T* __restrict__ down, int64_t sh, int64_t sn, int64_t n_records,
+                                    int hidden, int hp, T* __restrict__ packed) {
+  const int64_t per = 3ll * hp;
+  const int64_t total = n_records * per;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t n = i / per;
+    const int64_t r = i - n * per;
+    const int part = static_cast<int>(r / hp);
+    const int h = static_cast<int>(r - static_cast<int64_t>(part) * hp);
+    T v = T(0.f);
+    if (h < hidden) {
+      if (part == 0)
+        v = gate[n * ld_gu + h];
+      else if (part == 1)
+        v = up[n * ld_gu + h];
+      else
+        v = down[static_cast<int64_t>(h) * sh + n * sn];
+    }
+    packed[i] = v;
+  }
+}
+
+__global__ void cast_f32_kernel(const float* __restrict__ src, void* dst, int64_t n, int dtype) {
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    store_as(dst, i, dtype, src[i]);
+}
+
+}  // namespace
+
+void record_cuda_error(cudaError_t err) {
+  if (err != cudaSuccess) g_last_error = err;
+}
+
+bool cuda_ok(cudaError_t err) {
+  record_cuda_error(err);
+  return err == cudaSuccess;
+}
+
+const DeviceInfo& device_info(int device) {
+  static std::mutex mu;
+  static DeviceInfo infos[64];
+  static bool ready[64] = {};
+  static DeviceInfo none;
+  if (device < 0 || device >= 64) return none;
+  std::lock_guard<std::mutex> lock(mu);
+  if (!ready[device]) {
+    DeviceInfo d;
+    if (cudaDeviceGetAttribute(&d.num_sms, cudaDevAttrMultiProcessorCount, device) != cudaSuccess ||
+        cudaDeviceGetAttribute(&d.max_smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device) != cudaSuccess)
+      return none;
+    infos[device] = d;
+    ready[device] = true;
+  }
+  return infos[device];
+}
+
+}  // namespace qcc
+
+extern "C" int qcc_version(void) { return QCC_ABI_VERSION; }
+
+extern "C" const char* qcc_status_string(int status) {
+  switch (status) {
+    case QCC_OK:
+      return "ok";
+    case QCC_ERR_INVALID_ARGUMENT:
+      return "invalid argument (null pointer, negative size or unknown enum)";
+    case QCC_ERR_SHAPE:
+      return "inconsistent shape or stride";
+    case QCC_ERR_DTYPE:
+      return "unsupported dtype";
+    case QCC_ERR_ALIGNMENT:
+      return "pointer or stride is not 16-byte aligned";
+    case QCC_ERR_UNSUPPORTED:
+      return "size beyond what the kernels support";
+    case QCC_ERR_WORKSPACE:
+      return "workspace missing or too small";
+    case QCC_ERR_CUDA:
+      return "CUDA runtime error";
+    default:
+      return "unknown status";
+  }
+}
+
+extern "C" const char* qcc_last_cuda_error_string(void) { return cudaGetErrorString(qcc::g_last_error); }
+
+extern "C" int qcc_hidden_pad(int hidden, int dtype) { return qcc::hidden_pad(hidden, dtype); }
+
+extern "C" int64_t qcc_record_bytes(int hidden, int dtype) {
+  if (!qcc::valid_dtype(dtype) || hidden < 1) return 0;
+  return qcc::record_bytes(hidden, dtype);
+}
+
+extern "C" size_t qcc_workspace_status_offset(void) { return 0; }
+
+extern "C" int qcc_workspace_init(void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+  if (workspace == nullptr || workspace_bytes == 0) return QCC_ERR_WORKSPACE;
+  if (!qcc::cuda_ok(cudaMemsetAsync(workspace, 0, workspace_bytes, stream))) return QCC_ERR_CUDA;
+  return QCC_OK;
+}
+
+extern "C" int qcc_pack_records(const void* gate, const void* up, int64_t ld_gu, const void* down,
+                                int64_t down_stride_h, int64_t down_stride_n, int64_t n_records, int hidden,
+                                int dtype, void* packed, cudaStream_t stream) {
+  if (!qcc::valid_dtype(dtype)) return QCC_ERR_DTYPE;
+  if (n_records < 0 || hidden < 1 || ld_gu < hidden || down_stride_h < 1 || down_stride_n < 1) return QCC_ERR_SHAPE;
+  if (n_records == 0) return QCC_OK;
+  if (gate == nullptr || up == nullptr || down == nullptr || packed == nullptr) return QCC_ERR_INVALID_ARGUMENT;
+  if (!qcc::aligned16(packed)) return QCC_ERR_ALIGNMENT;
+  const int hp = qcc::hidden_pad(hidden, dtype);
+  const int64_t total = n_records * 3ll * hp;
+  const int threads = 256;
+  const int64_t blocks = std::min<int64_t>((total + threads - 1) / threads, 148ll * 16);
+#define QCC_PACK(T)                                                                                              \
+  qcc::pack_records_kernel<T><<<static_cast<unsigned>(blocks), threads, 0, stream>>>(                            \
+      static_cast<const T*>(gate), static_cast<const T*>(up), ld_gu, static_cast<const T*>(down), down_stride_h, \
+      down_stride_n, n_records, hidden, hp, static_cast<T*>(packed))
+  if (dtype == QCC_DTYPE_BF16)
+    QCC_PACK(__nv_bfloat16);
+  else if (dtype == QCC_DTYPE_F16)
+    QCC_PACK(__half);
+  else
+    QCC_PACK(float);
+#undef QCC_PACK
+  if (!qcc::cuda_ok(cudaGetLastError())) return QCC_ERR_CUDA;
+  return QCC_OK;
+}
+
+extern "C" int qcc_cast_f32(const float* src, void* dst, int64_t n, int dtype, cudaStream_t stream) {
+  if (!qcc::valid_dtype(dtype)) return QCC_ERR_DTYPE;
+  if (n < 0) return QCC_ERR_SHAPE;
+  if (n == 0) return QCC_OK;
+  if (src == nullptr || dst == nullptr) return QCC_ERR_INVALID_ARGUMENT;
+  const int threads = 256;
+  const int64_t blocks = std::min<int64_t>((n + threads - 1) / threads, 148ll * 8);
+  qcc::cast_f32_kernel<<<static_cast<unsigned>(blocks), threads, 0, stream>>>(src, dst, n, dtype);
+  if (!qcc::cuda_ok(cudaGetLastError())) return QCC_ERR_CUDA;
+  return QCC_OK;
+}

@@ -1,0 +1,46 @@
+// Host-side helpers shared by the qcc_b200 translation units.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include "qcc_b200.h"
+
+namespace qcc {
+
+struct DeviceInfo {
+  int num_sms = 0;
+  int max_smem_optin = 0;  // bytes of dynamic shared memory one block may opt into
+};
+
+// Cached per-device properties (thread-safe).
+const DeviceInfo& device_info(int device);
+
+inline bool valid_dtype(int dtype) {
+  return dtype == QCC_DTYPE_BF16 || dtype == QCC_DTYPE_F16 || dtype == QCC_DTYPE_F32;
+}
+
+inline int dtype_bytes(int dtype) { return dtype == QCC_DTYPE_F32 ? 4 : 2; }
+
+inline int hidden_pad(int hidden, int /*dtype*/) { return (hidden + 7) / 8 * 8; }
+
+inline int64_t record_bytes(int hidden, int dtype) {
+  return 3ll * hidden_pad(hidden, dtype) * dtype_bytes(dtype);
+}
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Remembers the error text for qcc_last_cuda_error_string(); true on success.
+bool cuda_ok(cudaError_t err);
+void record_cuda_error(cudaError_t err);
+
+int decode_max_batch(int hidden, int dtype);
+size_t decode_workspace_bytes(int batch, int hidden, int dtype);
+
+int indexed_ffn_decode(const void* x, int64_t ldx, int batch, int hidden, const void* packed, int64_t n_records,
+                       int dtype, const void* ids, int ids_dtype, int n_ids, const int32_t* n_ids_dev,
+                       const uint8_t* token_mask, void* workspace, size_t workspace_bytes, void* y_out, int64_t ldy,
+                       int y_dtype, void* activation_out, int64_t lda, cudaStream_t stream);
+
+}  // namespace qcc

@@ -1,0 +1,117 @@
+"""Deterministic top-K selection and per-token unions on the GPU.
+
+The reference selects with ``torch.topk(scores, k, sorted=False)``
+(runtime/selector.py:24, runtime/cuda_selector.py:40,
+end_to_end/oracle_sparse_mlp.py:75), whose order -- and whose choice among
+tied scores -- is unspecified.  :func:`select_topk` returns the k largest
+scores per row as ascending unique int32 indices with ties broken by lower
+index, -0.0 equal to +0.0 and NaN ranked largest: exactly
+``sort(scores, descending=True, stable=True)[:k]`` sorted ascending, which
+is always one of the answers torch.topk may give.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+
+from .. import _lib
+
+
+def retention_count(width: int, retention: float) -> int:
+    """K = max(1, ceil(width * retention)) (predictor/candidate_reranker.py:9-12)."""
+    if not 0 < retention <= 1:
+        raise ValueError("retention must be in (0, 1]")
+    return max(1, math.ceil(width * retention))
+
+
+def select_topk(scores: torch.Tensor, k: int, out: torch.Tensor | None = None) -> torch.Tensor:
+    """[B, N] or [N] fp32 scores -> [B, k] (or [k]) ascending int32 indices."""
+    squeeze = scores.ndim == 1
+    if squeeze:
+        scores = scores.unsqueeze(0)
+    if scores.ndim != 2:
+        raise ValueError("scores must be [batch, n] or [n]")
+    if scores.dtype != torch.float32:
+        raise TypeError("scores must be float32")
+    device = _lib.require_cuda(scores)
+    if scores.stride(1) != 1:
+        scores = scores.contiguous()
+    batch, n = scores.shape
+    if not 0 <= k <= n:
+        raise ValueError(f"k must be in [0, {n}]")
+    if out is None:
+        out = torch.empty((batch, k), dtype=torch.int32, device=device)
+    elif out.shape != (batch, k) or out.dtype != torch.int32 or out.stride(1) != 1:
+        raise ValueError("out must be a row-contiguous int32 [batch, k] tensor")
+    lib = _lib.library()
+    status = lib.qcc_select_topk(scores.data_ptr(), scores.stride(0), batch, n, k, out.data_ptr(), out.stride(0),
+                                 _lib.stream_handle(device))
+    _lib.check(status, "qcc_select_topk")
+    return out.squeeze(0) if squeeze else out
+
+
+def build_union(ids: torch.Tensor, id_begin: int = 0, id_end: int | None = None, capacity: int | None = None):
+    """Union of per-token sorted id rows [B, k] (B <= 8) restricted to [id_begin, id_end).
+
+    Returns (union_ids int32 [capacity], token_mask uint8 [capacity], count
+    int32 [1] on the device).  Entries past ``count`` are undefined.  Ids are
+    rebased to id_begin (local to an intermediate-dimension shard).
+    """
+    if ids.ndim == 1:
+        ids = ids.unsqueeze(0)
+    if ids.ndim != 2 or ids.dtype != torch.int32 or ids.stride(1) != 1:
+        raise ValueError("ids must be a row-contiguous int32 [batch, k] tensor")
+    device = _lib.require_cuda(ids)
+    batch, k = ids.shape
+    if not 1 <= batch <= 8:
+        raise ValueError("build_union handles 1..8 token rows")
+    if id_end is None:
+        id_end = int(ids.max().item()) + 1 if ids.numel() else id_begin
+    width = id_end - id_begin
+    if width < 0:
+        raise ValueError("id_end must be >= id_begin")
+    cap = min(width, batch * k) if capacity is None else capacity
+    if cap < min(width, batch * k):
+        raise ValueError("capacity below min(id_end - id_begin, batch * k)")
+    union_ids = torch.empty(max(cap, 1), dtype=torch.int32, device=device)
+    token_mask = torch.empty(max(cap, 1), dtype=torch.uint8, device=device)
+    count = torch.empty(1, dtype=torch.int32, device=device)
+    lib = _lib.library()
+    status = lib.qcc_build_union(ids.data_ptr(), ids.stride(0), batch, k, id_begin, id_end, union_ids.data_ptr(),
+                                 token_mask.data_ptr(), count.data_ptr(), _lib.stream_handle(device))
+    _lib.check(status, "qcc_build_union")
+    return union_ids, token_mask, count
+
+
+class TopKSelector:
+    """x-independent part of reference runtime/selector.py:15-24: scores -> ids.
+
+    The score producer (the learned predictor) is outside the hot path; this
+    takes per-neuron scores and applies the retention, returning ascending
+    int32 ids [B, K].
+    """
+
+    def __init__(self, intermediate: int, retention: float = 0.5):
+        self.intermediate = intermediate
+        self.retention = retention
+        self.k = retention_count(intermediate, retention)
+
+    def select(self, scores: torch.Tensor) -> torch.Tensor:
+        if scores.shape[-1] != self.intermediate:
+            raise ValueError(f"expected {self.intermediate} scores per row, got {scores.shape[-1]}")
+        return select_topk(scores.float(), self.k)
+
+
+def selected_set_comparison(reference: torch.Tensor, candidate: torch.Tensor, width: int) -> dict:
+    """Set agreement of two [B, K] id lists (reference runtime/selector.py:51-52)."""
+    ref = torch.zeros((len(reference), width), device=reference.device, dtype=torch.bool)
+    ref.scatter_(-1, reference.long(), True)
+    other = torch.zeros_like(ref).scatter_(-1, candidate.long().to(ref.device), True)
+    intersection = (ref & other).sum(-1).float()
+    changed = (ref ^ other).sum(-1).float()
+    union = (ref | other).sum(-1).float().clamp_min(1)
+    return {"set_equality_fraction": float((changed == 0).float().mean()),
+            "jaccard": float((intersection / union).mean()),
+            "mean_changed_neurons": float(changed.mean()),
+            "p95_changed_neurons": float(changed.quantile(.95))}

@@ -1,0 +1,110 @@
+"""Seeded synthetic workloads (Qwen layer-0 FFN shapes; no real weights here).
+
+Each generator is deterministic for its seed.  Small tensors use a CPU
+``torch.Generator``; the large weight arrays are drawn on the target device
+(a CUDA generator is far faster than drawing 267M values on the host), so
+the same seed gives the same weights on the same GPU/torch build.
+
+* decode (``decode_layer``): hidden 5120, intermediate 17408, weights
+  ~ N(0, 0.02^2) drawn directly in neuron-major packed form (every element is
+  iid, so this is the same distribution as packing three separately drawn
+  matrices), x ~ N(0, 1), ids = sort(randperm(N, seed=1000+token)[:K]).
+* selector (``selector_scores``): fp32 scores ~ Laplace(0, 1) per token; a
+  hot 10% of neurons (seeded permutation) gets boost c*(i+1)^-1.1, c = 8, for
+  the i-th hot neuron (Zipf(1.1)-ranked).
+* oracle layer (``oracle_layer``): hidden 1024, intermediate 3072, fp32,
+  gate/up [N,H] and down [H,N] ~ N(0, 0.02^2) drawn in that order from seed 0,
+  64 tokens x ~ N(0,1) RMS-normalised as x / sqrt(mean(x^2) + 1e-6).
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import torch
+
+DECODE_HIDDEN = 5120
+DECODE_INTERMEDIATE = 17408
+WEIGHT_STD = 0.02
+
+
+def retention_k(intermediate: int, retention: float) -> int:
+    return max(1, math.ceil(intermediate * retention))
+
+
+@dataclass
+class PackedLayer:
+    packed: torch.Tensor   # [N, 3H] neuron-major records
+    hidden: int
+    intermediate: int
+
+    def gate(self) -> torch.Tensor:
+        return self.packed[:, :self.hidden]
+
+    def up(self) -> torch.Tensor:
+        return self.packed[:, self.hidden:2 * self.hidden]
+
+    def down(self) -> torch.Tensor:
+        """[H, N] view of the down projection (the reference's layout)."""
+        return self.packed[:, 2 * self.hidden:3 * self.hidden].t()
+
+
+def decode_layer(hidden: int = DECODE_HIDDEN, intermediate: int = DECODE_INTERMEDIATE,
+                 dtype: torch.dtype = torch.bfloat16, device: str | torch.device = "cuda", seed: int = 0,
+                 record_range: tuple[int, int] | None = None) -> PackedLayer:
+    """Packed layer with iid N(0, 0.02^2) weights.  ``record_range`` draws only
+    records [begin, end) of the full layer (an intermediate-dimension shard):
+    record n is drawn from its own seed block, so shards of one seed agree with
+    the unsharded layer."""
+    if hidden % 8:
+        raise ValueError("decode_layer draws packed records directly and needs hidden % 8 == 0")
+    begin, end = record_range if record_range is not None else (0, intermediate)
+    device = torch.device(device)
+    packed = torch.empty((end - begin, 3 * hidden), dtype=dtype, device=device)
+    block = 1024  # records per seeded block
+    for b0 in range(begin - begin % block, end, block):
+        gen = torch.Generator(device=device).manual_seed(seed * 1_000_003 + b0 // block)
+        rows = torch.randn((block, 3 * hidden), generator=gen, device=device, dtype=torch.float32)
+        rows.mul_(WEIGHT_STD)
+        lo, hi = max(b0, begin), min(b0 + block, end)
+        packed[lo - begin:hi - begin].copy_(rows[lo - b0:hi - b0])
+    return PackedLayer(packed, hidden, end - begin)
+
+
+def decode_x(batch: int = 1, hidden: int = DECODE_HIDDEN, dtype: torch.dtype = torch.bfloat16, seed: int = 1) -> torch.Tensor:
+    gen = torch.Generator().manual_seed(seed)
+    return torch.randn((batch, hidden), generator=gen).to(dtype)
+
+
+def decode_ids(intermediate: int, k: int, token: int = 0) -> torch.Tensor:
+    """sort(randperm(N, seed=1000+token)[:K]) as int32 (CPU)."""
+    gen = torch.Generator().manual_seed(1000 + token)
+    return torch.randperm(intermediate, generator=gen)[:k].sort().values.to(torch.int32)
+
+
+def selector_scores(batch: int, intermediate: int = DECODE_INTERMEDIATE, seed: int = 7, hot_fraction: float = 0.1,
+                    boost: float = 8.0, zipf: float = 1.1) -> torch.Tensor:
+    """[batch, N] fp32 Laplace(0,1) scores with a Zipf-boosted hot subset (CPU)."""
+    gen = torch.Generator().manual_seed(seed)
+    u = torch.rand((batch, intermediate), generator=gen, dtype=torch.float64) - 0.5
+    scores = -torch.sign(u) * torch.log1p(-2 * u.abs())
+    hot = torch.randperm(intermediate, generator=gen)[:max(1, int(round(hot_fraction * intermediate)))]
+    ranks = torch.arange(1, hot.numel() + 1, dtype=torch.float64)
+    scores[:, hot] += boost * ranks.pow(-zipf)
+    return scores.to(torch.float32)
+
+
+def oracle_layer(hidden: int = 1024, intermediate: int = 3072, tokens: int = 64, seed: int = 0):
+    """(gate [N,H], up [N,H], down [H,N], x [T,H]) fp32 on CPU."""
+    gen = torch.Generator().manual_seed(seed)
+    gate = torch.randn((intermediate, hidden), generator=gen) * WEIGHT_STD
+    up = torch.randn((intermediate, hidden), generator=gen) * WEIGHT_STD
+    down = torch.randn((hidden, intermediate), generator=gen) * WEIGHT_STD
+    x = torch.randn((tokens, hidden), generator=gen)
+    x = x / torch.sqrt(x.pow(2).mean(-1, keepdim=True) + 1e-6)
+    return gate, up, down, x
+
+
+def decode_bytes(k: int, hidden: int = DECODE_HIDDEN, esize: int = 2, batch: int = 1, index_bytes: int = 4) -> int:
+    """Algorithmic HBM bytes of one decode call: K records + x + ids + y."""
+    return k * 3 * hidden * esize + batch * hidden * esize + k * index_bytes + batch * hidden * esize
