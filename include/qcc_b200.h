@@ -103,7 +103,8 @@ QCC_API int qcc_pack_records(const void* gate, const void* up, int64_t ld_gu, co
 /* ---------------------------------------------------------------------- */
 
 /* Largest batch one qcc_indexed_ffn_decode call accepts (4, or 2 when
- * hidden > 5120 needs two hidden slots per thread); 0 if hidden is too big. */
+ * 1 when hidden > 5120 needs four hidden slots per thread); 0 if hidden is
+ * beyond 10240. */
 QCC_API int qcc_decode_max_batch(int hidden, int dtype);
 
 /* Bytes of workspace qcc_indexed_ffn_decode needs for this batch/hidden. */

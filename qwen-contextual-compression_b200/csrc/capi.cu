@@ -5,6 +5,8 @@
 
 #include <algorithm>
 #include <mutex>
+#include <set>
+#include <utility>
 
 #include "qcc_common.cuh"
 #include "qcc_host.h"
@@ -57,9 +59,18 @@ void record_cuda_error(cudaError_t err) {
 }
 
 bool cuda_ok(cudaError_t err) {
+  if (err == cudaSuccess) return true;
   record_cuda_error(err);
-  return err == cudaSuccess;
+  (void)cudaGetLastError();  // do not leave a non-sticky error for the next caller to find
+  return false;
 }
+
+bool launch_ok() {
+  const cudaError_t err = cudaGetLastError();
+  return cuda_ok(err);
+}
+
+void clear_stale_error() { (void)cudaGetLastError(); }
 
 const DeviceInfo& device_info(int device) {
   static std::mutex mu;
@@ -77,6 +88,23 @@ const DeviceInfo& device_info(int device) {
     ready[device] = true;
   }
   return infos[device];
+}
+
+bool ensure_max_dynamic_smem(const void* kernel, int device) {
+  static std::mutex mu;
+  static std::set<std::pair<const void*, int>> done;
+  std::lock_guard<std::mutex> lock(mu);
+  const auto key = std::make_pair(kernel, device);
+  if (done.count(key)) return true;
+  const DeviceInfo& info = device_info(device);
+  if (info.max_smem_optin <= 0) return false;
+  cudaFuncAttributes attr;
+  if (!cuda_ok(cudaFuncGetAttributes(&attr, kernel))) return false;
+  const int dynamic_max = info.max_smem_optin - static_cast<int>(attr.sharedSizeBytes);
+  if (!cuda_ok(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, dynamic_max)))
+    return false;
+  done.insert(key);
+  return true;
 }
 
 }  // namespace qcc
@@ -139,6 +167,7 @@ extern "C" int qcc_pack_records(const void* gate, const void* up, int64_t ld_gu,
   qcc::pack_records_kernel<T><<<static_cast<unsigned>(blocks), threads, 0, stream>>>(                            \
       static_cast<const T*>(gate), static_cast<const T*>(up), ld_gu, static_cast<const T*>(down), down_stride_h, \
       down_stride_n, n_records, hidden, hp, static_cast<T*>(packed))
+  qcc::clear_stale_error();
   if (dtype == QCC_DTYPE_BF16)
     QCC_PACK(__nv_bfloat16);
   else if (dtype == QCC_DTYPE_F16)
@@ -146,7 +175,7 @@ extern "C" int qcc_pack_records(const void* gate, const void* up, int64_t ld_gu,
   else
     QCC_PACK(float);
 #undef QCC_PACK
-  if (!qcc::cuda_ok(cudaGetLastError())) return QCC_ERR_CUDA;
+  if (!qcc::launch_ok()) return QCC_ERR_CUDA;
   return QCC_OK;
 }
 
@@ -157,7 +186,8 @@ extern "C" int qcc_cast_f32(const float* src, void* dst, int64_t n, int dtype, c
   if (src == nullptr || dst == nullptr) return QCC_ERR_INVALID_ARGUMENT;
   const int threads = 256;
   const int64_t blocks = std::min<int64_t>((n + threads - 1) / threads, 148ll * 8);
+  qcc::clear_stale_error();
   qcc::cast_f32_kernel<<<static_cast<unsigned>(blocks), threads, 0, stream>>>(src, dst, n, dtype);
-  if (!qcc::cuda_ok(cudaGetLastError())) return QCC_ERR_CUDA;
+  if (!qcc::launch_ok()) return QCC_ERR_CUDA;
   return QCC_OK;
 }

@@ -7,9 +7,11 @@
 // ring with one non-multicast bulk copy per record (mbarrier completion),
 // computes g = G_j.x, u = U_j.x with fp32 accumulation, a_j = silu(g) * u,
 // and accumulates a_j * D_j into a per-thread fp32 slice of y held in
-// registers.  At the end each CTA adds its partial y into an fp32 workspace
-// with vector reductions at L2; the last CTA to finish converts the sum to
-// the output dtype and re-zeroes the workspace for the next call.
+// registers.  At the end every CTA stores its partial y (fp32) to the
+// workspace, a bounded grid-wide barrier (cooperative launch: all CTAs are
+// resident, one per SM) waits for all partials, and each CTA sums one slice
+// of y over all partials in a fixed order and writes it in the output dtype.
+// No atomics touch y, so the result is bit-reproducible for a given grid.
 //
 // Thread t of a CTA owns the 8-element hidden slots v = t + k * blockDim.x
 // (k < VPT): it holds x[b, 8v:8v+8] and the partial y[b, 8v:8v+8] in
@@ -30,9 +32,10 @@ namespace qcc {
 
 namespace {
 
-constexpr int kWorkspaceHeader = 256;  // status word, counter, padding
+constexpr int kWorkspaceHeader = 256;  // status word, arrive / depart counters, padding
+constexpr int kMaxGrid = 160;          // CTAs (one per SM) whose partial rows the workspace holds
 constexpr int kMaxStages = 8;
-constexpr int kMaxThreads = 640;  // 5120 hidden / 8 per thread; caps registers at 96 per thread
+constexpr int kMaxThreads = 320;  // 10 warps; hidden 5120 = two 8-element slots per thread
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s bound on any barrier wait
 
 struct DecodeArgs {
@@ -49,8 +52,9 @@ struct DecodeArgs {
   int n_ids;
   const int32_t* n_ids_dev;
   unsigned int* status;
-  unsigned int* counter;
-  float* y_acc;
+  unsigned int* arrive;   // CTAs that stored their partial y in this launch
+  unsigned int* depart;   // CTAs done reading partials; the last one resets both
+  float* partials;        // [gridDim.x][B * hidden_pad] fp32
   void* y_out;
   int64_t ldy;
   int y_dtype;
@@ -58,6 +62,9 @@ struct DecodeArgs {
   int64_t lda;
   int a_dtype;
   int stages;
+  int id_cap;        // capacity of the shared id cache (>= ids per CTA)
+  int64_t ring_bytes;  // stages * record_bytes (16-byte multiple)
+  int x_vec;           // x rows are 16-byte aligned with hidden % 8 == 0: vector loads
 };
 
 __device__ __forceinline__ int64_t load_id(const DecodeArgs& a, int j) {
@@ -65,20 +72,54 @@ __device__ __forceinline__ int64_t load_id(const DecodeArgs& a, int j) {
                  : static_cast<int64_t>(__ldg(reinterpret_cast<const int32_t*>(a.ids) + j));
 }
 
+__host__ __device__ constexpr int next_pow2(int v) { return v <= 1 ? 1 : 2 * next_pow2((v + 1) / 2); }
+
+// Multi-value warp reduction: V (a power of two <= 32) per-lane values in,
+// the warp total of value (lane / (32 / V)) out.  Each butterfly level halves
+// the number of live values, so V values cost log2(32) + V - 1 shuffles
+// instead of 5 * V.
+template <int V>
+__device__ __forceinline__ float warp_reduce_multi(float (&v)[V], int lane) {
+  static_assert(V >= 1 && V <= 32 && (V & (V - 1)) == 0, "V must be a power of two <= 32");
+  int off = 16;
+#pragma unroll
+  for (int n = V; n > 1; n >>= 1, off >>= 1) {
+    const bool upper = (lane & off) != 0;
+#pragma unroll
+    for (int i = 0; i < n / 2; ++i) {
+      const float send = upper ? v[i] : v[i + n / 2];
+      const float keep = upper ? v[i + n / 2] : v[i];
+      v[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+    }
+  }
+#pragma unroll
+  for (; off >= 1; off >>= 1) v[0] += __shfl_xor_sync(0xffffffffu, v[0], off);
+  return v[0];
+}
+
+// Shared-memory layout after the record ring (host mirrors it in tail_bytes):
+//   mbarriers [kMaxStages] | warp partials [2][VP][32] f32 | flag [4] i32 |
+//   ids [id_cap] i32 | token bits [id_cap] u8
 template <typename T, int B, int VPT, int R>
 __global__ void __launch_bounds__(kMaxThreads, 1) indexed_ffn_decode_kernel(const DecodeArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
+  constexpr int kVals = 2 * R * B;          // partial sums per group: (gate, up) x records x tokens
+  constexpr int VP = next_pow2(kVals);      // padded to a power of two for the butterfly
+  constexpr int kLanesPer = 32 / VP;        // lanes holding one value after the butterfly
   const int tid = threadIdx.x;
   const int lane = tid & 31;
+  const int warp = tid >> 5;
   const int nthreads = blockDim.x;
+  const int nwarps = nthreads >> 5;
   const int S = a.stages;
   const int seg = a.hidden_pad;
   const int nslots = seg >> 3;
-  constexpr int kVals = 2 * R * B;
 
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + static_cast<size_t>(S) * a.record_bytes);
-  float* s_tot = reinterpret_cast<float*>(bars + kMaxStages);  // [3][kVals]
-  int* s_flag = reinterpret_cast<int*>(s_tot + 3 * kVals);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + a.ring_bytes);
+  float* s_red = reinterpret_cast<float*>(bars + kMaxStages);
+  int* s_flag = reinterpret_cast<int*>(s_red + 2 * VP * 32);
+  int32_t* s_ids = s_flag + 4;
+  uint8_t* s_bits = reinterpret_cast<uint8_t*>(s_ids + a.id_cap);
 
   // This CTA's share of the id list.
   int n = a.n_ids;
@@ -87,13 +128,35 @@ __global__ void __launch_bounds__(kMaxThreads, 1) indexed_ffn_decode_kernel(cons
   const int end = static_cast<int>((static_cast<int64_t>(n) * (blockIdx.x + 1)) / gridDim.x);
   const int cnt = end - begin;
 
-  if (tid == 0) {
-    for (int s = 0; s < S; ++s) mbar_init(&bars[s], 1);
-    fence_barrier_init();
-  }
-  for (int i = tid; i < 3 * kVals; i += nthreads) s_tot[i] = 0.f;
+  const uint64_t policy = policy_evict_first();
+  const uint32_t rec_bytes = static_cast<uint32_t>(a.record_bytes);
+  int issued = 0;  // meaningful in thread 0 only
 
-  // x and the partial y live in registers (fp32).
+  auto issue = [&](int i, int stage) {  // thread 0: start the bulk copy of local record i
+    const int32_t id = s_ids[i];
+    uint64_t* bar = &bars[stage];
+    if (id >= 0) {
+      mbar_arrive_expect_tx(bar, rec_bytes);
+      bulk_load(smem + static_cast<size_t>(stage) * a.record_bytes,
+                a.packed + static_cast<int64_t>(id) * a.record_bytes, rec_bytes, bar, policy);
+    } else {
+      mbar_arrive(bar);  // completes the phase with no data; consumers skip the record
+    }
+  };
+  auto cache_id = [&](int i) {  // id (or -1 when out of range) and token bits of local record i
+    const int64_t id = load_id(a, begin + i);
+    const bool in_range = id >= 0 && id < a.n_records;
+    if (!in_range) atomicOr(a.status, QCC_DEV_ID_RANGE);
+    s_ids[i] = in_range ? static_cast<int32_t>(id) : -1;
+    s_bits[i] = a.token_mask ? __ldg(a.token_mask + begin + i) : static_cast<uint8_t>(0xFFu);
+  };
+
+  // Prologue.  Every thread first issues its small global loads -- its x
+  // slots and its share of the id cache -- so that they are in the memory
+  // system before any record copy (loads issued after the copies queue
+  // behind ~30 MB of record traffic).  Thread 0 then fetches the first S ids
+  // itself and starts their copies without waiting for the block barrier.
+  const int pre = min(S, cnt);
   float xr[B][VPT][8];
   float yr[B][VPT][8];
   const T* xg = reinterpret_cast<const T*>(a.x);
@@ -102,181 +165,294 @@ __global__ void __launch_bounds__(kMaxThreads, 1) indexed_ffn_decode_kernel(cons
 #pragma unroll
     for (int k = 0; k < VPT; ++k) {
       const int v = tid + k * nthreads;
+      if (a.x_vec && v < nslots) {
+        float f[8];
+        widen(load_global_pack8<T>(xg + b * a.ldx + 8 * v), f);
 #pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        const int h = 8 * v + e;
-        xr[b][k][e] = (v < nslots && h < a.hidden) ? to_f32<T>(xg[b * a.ldx + h]) : 0.f;
-        yr[b][k][e] = 0.f;
+        for (int e = 0; e < 8; ++e) xr[b][k][e] = f[e];
+      } else {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const int h = 8 * v + e;
+          xr[b][k][e] = (v < nslots && h < a.hidden) ? to_f32<T>(xg[b * a.ldx + h]) : 0.f;
+        }
+      }
+#pragma unroll
+      for (int e = 0; e < 8; ++e) yr[b][k][e] = 0.f;
+    }
+  // Thread 0's first S ids are loaded into registers together with the
+  // cache loads, so one memory latency covers both.
+  int64_t first_ids[kMaxStages];
+  if (tid == 0) {
+#pragma unroll
+    for (int i = 0; i < kMaxStages; ++i) first_ids[i] = i < pre ? load_id(a, begin + i) : -1;
+  }
+  for (int i = tid; i < cnt; i += nthreads) cache_id(i);
+  if (tid == 0) {
+    for (int s = 0; s < S; ++s) mbar_init(&bars[s], 1);
+    fence_barrier_init();
+#pragma unroll
+    for (int i = 0; i < kMaxStages; ++i) {
+      if (i < pre) {
+        const int64_t id = first_ids[i];
+        uint64_t* bar = &bars[i];
+        if (id >= 0 && id < a.n_records) {
+          mbar_arrive_expect_tx(bar, rec_bytes);
+          bulk_load(smem + static_cast<size_t>(i) * a.record_bytes, a.packed + id * a.record_bytes, rec_bytes,
+                    bar, policy);
+        } else {
+          mbar_arrive(bar);
+        }
       }
     }
-  __syncthreads();
-
-  const uint64_t policy = policy_evict_first();
-  const uint32_t rec_bytes = static_cast<uint32_t>(a.record_bytes);
-  int issued = 0;  // meaningful in thread 0 only
-
-  auto issue = [&](int i) {  // thread 0: start the bulk copy of local record i
-    const int64_t id = load_id(a, begin + i);
-    uint64_t* bar = &bars[i % S];
-    if (id >= 0 && id < a.n_records) {
-      mbar_arrive_expect_tx(bar, rec_bytes);
-      bulk_load(smem + static_cast<size_t>(i % S) * a.record_bytes, a.packed + id * a.record_bytes, rec_bytes, bar,
-                policy);
-    } else {
-      atomicOr(a.status, QCC_DEV_ID_RANGE);
-      mbar_arrive(bar);  // completes the phase with no data; consumers skip it
-    }
-  };
-
-  if (tid == 0) {
-    const int pre = min(S, cnt);
-    for (int i = 0; i < pre; ++i) issue(i);
     issued = pre;
   }
+  __syncthreads();
 
-  int group = 0;
+  // Software pipeline, one barrier per group of R records:
+  //   iteration g: wait for group g, partial dot products of group g -> warp
+  //   sums -> s_red[g & 1]; meanwhile finish group g-1 (its block sums are
+  //   complete since the previous barrier): activation and y += a * down,
+  //   with group g-1's down slices already in registers.  After the barrier
+  //   the ring slots of group g are refilled at once.
+  Pack8<T> dn_prev[R][VPT];
+  int rn_prev = 0;
+  int buf = 0;
+  int stage0 = 0;    // ring slot of the group's first record
+  uint32_t phase0 = 0;
   int consumed = 0;
   bool aborted = false;
-  for (int g0 = 0; g0 < cnt; g0 += R, ++group) {
+  for (int g0 = 0;; g0 += R) {
     const int rn = min(R, cnt - g0);
-    float pg[R][B], pu[R][B];
-    Pack8<T> dn[R][VPT];
+    Pack8<T> dn_cur[R][VPT];
     bool ok = true;
+    if (rn > 0) {
+      float part[VP];
 #pragma unroll
-    for (int r = 0; r < R; ++r) {
+      for (int q = 0; q < VP; ++q) part[q] = 0.f;
 #pragma unroll
-      for (int b = 0; b < B; ++b) pg[r][b] = pu[r][b] = 0.f;
-      if (r < rn) {
-        const int i = g0 + r;
-        ok = ok && mbar_wait_bounded(&bars[i % S], (i / S) & 1, kWaitLimitNs);
-        const T* rec = reinterpret_cast<const T*>(smem + static_cast<size_t>(i % S) * a.record_bytes);
+      for (int r = 0; r < R; ++r) {
+        if (r < rn) {
+          int stage = stage0 + r;
+          uint32_t phase = phase0;
+          if (stage >= S) {
+            stage -= S;
+            phase ^= 1u;
+          }
+          ok = ok && mbar_wait_bounded(&bars[stage], phase, kWaitLimitNs);
+          const T* rec = reinterpret_cast<const T*>(smem + static_cast<size_t>(stage) * a.record_bytes);
 #pragma unroll
-        for (int k = 0; k < VPT; ++k) {
-          const int v = tid + k * nthreads;
-          if (v < nslots) {
-            const Pack8<T> gr = load_pack8(rec + 8 * v);
-            const Pack8<T> ur = load_pack8(rec + seg + 8 * v);
-            dn[r][k] = load_pack8(rec + 2 * seg + 8 * v);
-            float gf[8], uf[8];
-            widen(gr, gf);
-            widen(ur, uf);
+          for (int k = 0; k < VPT; ++k) {
+            const int v = tid + k * nthreads;
+            if (v < nslots) {
+              const Pack8<T> gr = load_pack8(rec + 8 * v);
+              const Pack8<T> ur = load_pack8(rec + seg + 8 * v);
+              dn_cur[r][k] = load_pack8(rec + 2 * seg + 8 * v);
+              float gf[8], uf[8];
+              widen(gr, gf);
+              widen(ur, uf);
 #pragma unroll
-            for (int b = 0; b < B; ++b)
+              for (int b = 0; b < B; ++b) {
+                float g0a = 0.f, g1a = 0.f, u0a = 0.f, u1a = 0.f;
 #pragma unroll
-              for (int e = 0; e < 8; ++e) {
-                pg[r][b] = fmaf(xr[b][k][e], gf[e], pg[r][b]);
-                pu[r][b] = fmaf(xr[b][k][e], uf[e], pu[r][b]);
+                for (int e = 0; e < 8; e += 2) {
+                  g0a = fmaf(xr[b][k][e], gf[e], g0a);
+                  g1a = fmaf(xr[b][k][e + 1], gf[e + 1], g1a);
+                  u0a = fmaf(xr[b][k][e], uf[e], u0a);
+                  u1a = fmaf(xr[b][k][e + 1], uf[e + 1], u1a);
+                }
+                part[(r * B + b) * 2 + 0] += g0a + g1a;
+                part[(r * B + b) * 2 + 1] += u0a + u1a;
               }
+            }
           }
         }
       }
+      const float wsum = warp_reduce_multi<VP>(part, lane);
+      if ((lane % kLanesPer) == 0) s_red[(buf * VP + lane / kLanesPer) * 32 + warp] = wsum;
     }
-    // Block-wide sums of the 2*R*B partial dot products.
-    float* tot = s_tot + (group % 3) * kVals;
+    if (rn_prev > 0) {
+      // Block totals of group g-1: value q = lane / kLanesPer summed over warps.
+      const float* redp = s_red + (buf ^ 1) * VP * 32 + (lane / kLanesPer) * 32;
+      float t = 0.f;
+      for (int w = lane % kLanesPer; w < nwarps; w += kLanesPer) t += redp[w];
 #pragma unroll
-    for (int r = 0; r < R; ++r)
+      for (int off = kLanesPer / 2; off >= 1; off >>= 1) t += __shfl_xor_sync(0xffffffffu, t, off);
 #pragma unroll
-      for (int b = 0; b < B; ++b) {
-        const float sg = warp_sum(pg[r][b]);
-        const float su = warp_sum(pu[r][b]);
-        if (lane == 0 && r < rn) {
-          atomicAdd(&tot[(r * B + b) * 2 + 0], sg);
-          atomicAdd(&tot[(r * B + b) * 2 + 1], su);
-        }
-      }
-    if (tid == 0) {
-      float* nxt = s_tot + ((group + 1) % 3) * kVals;
-      for (int q = 0; q < kVals; ++q) nxt[q] = 0.f;
-    }
-    if (__syncthreads_or(!ok)) {
-      aborted = true;
-      consumed = g0;
-      break;
-    }
-    // Every thread has read the staged records of this group: refill them.
-    if (tid == 0) {
-      for (int r = 0; r < rn; ++r) {
-        const int i = g0 + r + S;
-        if (i < cnt) {
-          issue(i);
-          issued = i + 1;
-        }
-      }
-    }
+      for (int r = 0; r < R; ++r) {
+        if (r < rn_prev) {
+          const int i = g0 - R + r;
+          const bool valid = s_ids[i] >= 0;
+          const unsigned bits = s_bits[i];
 #pragma unroll
-    for (int r = 0; r < R; ++r) {
-      if (r < rn) {
-        const int j = begin + g0 + r;
-        const int64_t id = load_id(a, j);
-        const bool valid = id >= 0 && id < a.n_records;
-        const unsigned bits = a.token_mask ? __ldg(a.token_mask + j) : 0xFFu;
+          for (int b = 0; b < B; ++b) {
+            const float g = __shfl_sync(0xffffffffu, t, ((r * B + b) * 2 + 0) * kLanesPer);
+            const float u = __shfl_sync(0xffffffffu, t, ((r * B + b) * 2 + 1) * kLanesPer);
+            const bool use = valid && ((bits >> b) & 1u);
+            const float act = use ? __fdividef(g, 1.f + __expf(-g)) * u : 0.f;
+            if (a.a_out != nullptr && tid == 0) store_as(a.a_out, b * a.lda + begin + i, a.a_dtype, act);
+            if (use) {
 #pragma unroll
-        for (int b = 0; b < B; ++b) {
-          const float g = tot[(r * B + b) * 2 + 0];
-          const float u = tot[(r * B + b) * 2 + 1];
-          const bool use = valid && ((bits >> b) & 1u);
-          const float act = use ? (g / (1.f + expf(-g))) * u : 0.f;
-          if (a.a_out != nullptr && tid == 0) store_as(a.a_out, b * a.lda + j, a.a_dtype, act);
-          if (use) {
+              for (int k = 0; k < VPT; ++k) {
+                const int v = tid + k * nthreads;
+                if (v < nslots) {
+                  float df[8];
+                  widen(dn_prev[r][k], df);
 #pragma unroll
-            for (int k = 0; k < VPT; ++k) {
-              const int v = tid + k * nthreads;
-              if (v < nslots) {
-                float df[8];
-                widen(dn[r][k], df);
-#pragma unroll
-                for (int e = 0; e < 8; ++e) yr[b][k][e] = fmaf(act, df[e], yr[b][k][e]);
+                  for (int e = 0; e < 8; ++e) yr[b][k][e] = fmaf(act, df[e], yr[b][k][e]);
+                }
               }
             }
           }
         }
       }
     }
-  }
-
-  if (aborted) {
-    // Drain this CTA's bulk copies still in flight (bounded) before leaving.
-    if (tid == 0) {
-      atomicOr(a.status, QCC_DEV_TIMEOUT);
-      for (int i = consumed; i < issued; ++i) (void)mbar_wait_bounded(&bars[i % S], (i / S) & 1, kWaitLimitNs);
+    if (rn <= 0) break;
+    if (__syncthreads_or(!ok)) {
+      aborted = true;
+      consumed = g0;
+      break;
     }
-  } else {
-    // Partial y -> fp32 workspace (vector reductions at L2).
-#pragma unroll
-    for (int b = 0; b < B; ++b)
-#pragma unroll
-      for (int k = 0; k < VPT; ++k) {
-        const int v = tid + k * nthreads;
-        if (v < nslots && cnt > 0) {
-          float* dst = a.y_acc + static_cast<int64_t>(b) * seg + 8 * v;
-          red_add_v4(dst, yr[b][k][0], yr[b][k][1], yr[b][k][2], yr[b][k][3]);
-          red_add_v4(dst + 4, yr[b][k][4], yr[b][k][5], yr[b][k][6], yr[b][k][7]);
+    // Every thread has its down slices of this group in registers: refill.
+    if (tid == 0) {
+      for (int r = 0; r < rn; ++r) {
+        const int i = g0 + r + S;
+        if (i < cnt) {
+          int stage = stage0 + r;
+          if (stage >= S) stage -= S;
+          issue(i, stage);
+          issued = i + 1;
         }
       }
-  }
-  __threadfence();
-  __syncthreads();
-  if (tid == 0) *s_flag = (atomicAdd(a.counter, 1u) == gridDim.x - 1);
-  __syncthreads();
-  if (*s_flag) {
-    // Last CTA: every partial is in; emit y and leave the workspace zeroed.
-    __threadfence();
-    for (int idx = tid; idx < B * nslots; idx += nthreads) {
-      const int b = idx / nslots;
-      const int v = idx - b * nslots;
-      float* src = a.y_acc + static_cast<int64_t>(b) * seg + 8 * v;
-      const float4 lo = __ldcg(reinterpret_cast<const float4*>(src));
-      const float4 hi = __ldcg(reinterpret_cast<const float4*>(src + 4));
-      const float vals[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
-#pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        const int h = 8 * v + e;
-        if (h < a.hidden) store_as(a.y_out, b * a.ldy + h, a.y_dtype, vals[e]);
-      }
-      __stcg(reinterpret_cast<float4*>(src), make_float4(0.f, 0.f, 0.f, 0.f));
-      __stcg(reinterpret_cast<float4*>(src + 4), make_float4(0.f, 0.f, 0.f, 0.f));
     }
-    if (tid == 0) *a.counter = 0u;
+#pragma unroll
+    for (int r = 0; r < R; ++r)
+#pragma unroll
+      for (int k = 0; k < VPT; ++k) dn_prev[r][k] = dn_cur[r][k];
+    rn_prev = rn;
+    buf ^= 1;
+    stage0 += R;
+    if (stage0 >= S) {
+      stage0 -= S;
+      phase0 ^= 1u;
+    }
+  }
+
+  if (aborted && tid == 0) {
+    // Drain this CTA's bulk copies still in flight (bounded) before the ring
+    // memory is reused below.
+    atomicOr(a.status, QCC_DEV_TIMEOUT);
+    for (int i = consumed; i < issued; ++i) (void)mbar_wait_bounded(&bars[i % S], (i / S) & 1, kWaitLimitNs);
+  }
+
+  // 1. Every CTA (also one with no records) stores its partial y row.  The
+  //    row has nvec = B * seg / 4 float4 columns; column c belongs to the
+  //    final-sum slice of CTA c / per, and the partials are laid out
+  //    slice-major -- [slice][cta][per] float4 -- so that each CTA later reads
+  //    its slice of all grid rows as one contiguous block.
+  const int row_len = B * seg;
+  const int nvec = row_len / 4;
+  const int grid = gridDim.x;
+  const int per = (nvec + grid - 1) / grid;
+  float4* part4 = reinterpret_cast<float4*>(a.partials);
+  auto part_index = [&](int c) {
+    const int blk = c / per;
+    return (static_cast<int64_t>(blk) * grid + blockIdx.x) * per + (c - blk * per);
+  };
+#pragma unroll
+  for (int b = 0; b < B; ++b)
+#pragma unroll
+    for (int k = 0; k < VPT; ++k) {
+      const int v = tid + k * nthreads;
+      if (v < nslots) {
+        const int c = (b * seg + 8 * v) / 4;
+        __stcg(part4 + part_index(c), make_float4(yr[b][k][0], yr[b][k][1], yr[b][k][2], yr[b][k][3]));
+        __stcg(part4 + part_index(c + 1), make_float4(yr[b][k][4], yr[b][k][5], yr[b][k][6], yr[b][k][7]));
+      }
+    }
+  // 2. Bounded grid barrier: wait until every CTA's row is stored.
+  __syncthreads();
+  if (tid == 0) {
+    __threadfence();
+    atomicAdd(a.arrive, 1u);
+    const volatile unsigned int* arrive = a.arrive;
+    const uint64_t start = global_timer_ns();
+    bool all = true;
+    while (*arrive < gridDim.x) {
+      if (global_timer_ns() - start > kWaitLimitNs) {
+        atomicOr(a.status, QCC_DEV_TIMEOUT);
+        all = false;
+        break;
+      }
+      __nanosleep(64);
+    }
+    __threadfence();
+    *s_flag = all ? 1 : 0;
+  }
+  __syncthreads();
+  // 3. This CTA's slice of y: columns [blockIdx.x * per, ... + width).  Load
+  //    the contiguous [grid][per] block into shared memory (coalesced, all
+  //    loads in flight at once), then one warp per column sums the grid rows
+  //    in a fixed order (lane-strided, then a shuffle tree) and writes the
+  //    four outputs in the output dtype.
+  if (*s_flag) {
+    const int c0 = blockIdx.x * per;
+    const int width = max(0, min(nvec, c0 + per) - c0);
+    if (width > 0) {
+      float4* s_blk = reinterpret_cast<float4*>(smem);  // the ring is idle now
+      const float4* blk = part4 + static_cast<int64_t>(blockIdx.x) * grid * per;
+      // All loads of a round in flight before any is stored (one latency).
+      const int total = grid * per;
+      for (int base = 0; base < total; base += 8 * nthreads) {
+        float4 v[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const int i = base + u * nthreads + tid;
+          if (i < total) v[u] = __ldcg(blk + i);
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const int i = base + u * nthreads + tid;
+          if (i < total) s_blk[i] = v[u];
+        }
+      }
+      __syncthreads();
+      for (int col = warp; col < width; col += nwarps) {
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int row = lane; row < grid; row += 32) {
+          const float4 p = s_blk[row * per + col];
+          acc.x += p.x;
+          acc.y += p.y;
+          acc.z += p.z;
+          acc.w += p.w;
+        }
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1) {
+          acc.x += __shfl_xor_sync(0xffffffffu, acc.x, off);
+          acc.y += __shfl_xor_sync(0xffffffffu, acc.y, off);
+          acc.z += __shfl_xor_sync(0xffffffffu, acc.z, off);
+          acc.w += __shfl_xor_sync(0xffffffffu, acc.w, off);
+        }
+        if (lane == 0) {
+          const int e0 = (c0 + col) * 4;
+          const int b = e0 / seg;
+          const int h0 = e0 - b * seg;
+          const float vals[4] = {acc.x, acc.y, acc.z, acc.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e)
+            if (h0 + e < a.hidden) store_as(a.y_out, b * a.ldy + h0 + e, a.y_dtype, vals[e]);
+        }
+      }
+    }
+  }
+  // 4. The last CTA to finish reading resets the counters for the next launch.
+  __syncthreads();
+  if (tid == 0) {
+    __threadfence();
+    if (atomicAdd(a.depart, 1u) == gridDim.x - 1) {
+      *a.arrive = 0u;
+      *a.depart = 0u;
+    }
   }
 }
 
@@ -286,55 +462,65 @@ __global__ void __launch_bounds__(kMaxThreads, 1) indexed_ffn_decode_kernel(cons
 
 using KernelFn = void (*)(const DecodeArgs);
 
-// One hidden slot per thread (hidden <= 5120): batch 1..4.  Two slots per
-// thread (hidden <= 10240): batch 1..2, which keeps x and y in registers.
-template <typename T, int R>
+// Records per barrier group: two for 16-bit weights and up to two tokens,
+// else one (keeps the down slices of two groups in registers).
+template <typename T, int B>
+constexpr int group_records() {
+  return (sizeof(T) == 2 && B <= 2) ? 2 : 1;
+}
+
+template <typename T, int B, int VPT>
+KernelFn kernel_for() {
+  return indexed_ffn_decode_kernel<T, B, VPT, group_records<T, B>()>;
+}
+
+// Slots of 8 hidden elements per thread: 1, 2 or 4 (hidden <= 2560, 5120,
+// 10240).  Batch per launch: up to 4 tokens with <= 2 slots, 1 with 4.
+template <typename T>
 KernelFn pick_kernel(int batch, int vpt) {
-  if (vpt == 1) {
+  if (vpt == 1 || vpt == 2) {
     switch (batch) {
-      case 1: return indexed_ffn_decode_kernel<T, 1, 1, R>;
-      case 2: return indexed_ffn_decode_kernel<T, 2, 1, R>;
-      case 3: return indexed_ffn_decode_kernel<T, 3, 1, R>;
-      case 4: return indexed_ffn_decode_kernel<T, 4, 1, R>;
+      case 1: return vpt == 1 ? kernel_for<T, 1, 1>() : kernel_for<T, 1, 2>();
+      case 2: return vpt == 1 ? kernel_for<T, 2, 1>() : kernel_for<T, 2, 2>();
+      case 3: return vpt == 1 ? kernel_for<T, 3, 1>() : kernel_for<T, 3, 2>();
+      case 4: return vpt == 1 ? kernel_for<T, 4, 1>() : kernel_for<T, 4, 2>();
       default: return nullptr;
     }
   }
-  switch (batch) {
-    case 1: return indexed_ffn_decode_kernel<T, 1, 2, R>;
-    case 2: return indexed_ffn_decode_kernel<T, 2, 2, R>;
-    default: return nullptr;
-  }
+  if (vpt == 4 && batch == 1) return kernel_for<T, 1, 4>();
+  return nullptr;
 }
 
 int vpt_for(int hidden_pad_) {
   const int nslots = hidden_pad_ / 8;
-  if (nslots <= kMaxThreads) return 1;
-  if (nslots <= 2 * kMaxThreads) return 2;
+  for (int vpt = 1; vpt <= 4; vpt *= 2)
+    if (nslots <= vpt * kMaxThreads) return vpt;
   return 0;
 }
 
-constexpr int records_per_group(int dtype) { return dtype == QCC_DTYPE_F32 ? 1 : 2; }
 
 struct LaunchShape {
   int threads;
   int vpt;
   int stages;
+  size_t ring;
   size_t smem;
 };
 
-size_t tail_bytes(int batch, int group) {
-  return kMaxStages * sizeof(uint64_t) + 3 * 2 * group * batch * sizeof(float) + 16;
+size_t tail_bytes(int id_cap) {
+  // mbarriers, warp partials (at most 2 * 32 values x 32 warps), flag, id cache, token bits
+  return kMaxStages * sizeof(uint64_t) + 2 * 32 * 32 * sizeof(float) + 4 * sizeof(int) +
+         static_cast<size_t>(id_cap) * sizeof(int32_t) + (static_cast<size_t>(id_cap) + 15) / 16 * 16;
 }
 
-bool plan_launch(int batch, int hidden_pad, int64_t record_bytes, int dtype, int max_smem, LaunchShape* out) {
+bool plan_launch(int batch, int hidden_pad, int64_t record_bytes, int max_smem, int id_cap,
+                 LaunchShape* out) {
   const int nslots = hidden_pad / 8;
-  int vpt = 1;
-  if (nslots > kMaxThreads) vpt = 2;
-  if (nslots > 2 * kMaxThreads) return false;
+  const int vpt = vpt_for(hidden_pad);
+  if (vpt == 0) return false;
   const int per = (nslots + vpt - 1) / vpt;
   const int threads = std::max(32, (per + 31) / 32 * 32);
-  const int group = records_per_group(dtype);
-  const size_t tail = tail_bytes(batch, group);
+  const size_t tail = tail_bytes(id_cap);
   if (record_bytes <= 0 || static_cast<size_t>(max_smem) < tail) return false;
   int stages = static_cast<int>((static_cast<size_t>(max_smem) - tail) / static_cast<size_t>(record_bytes));
   stages = std::min(stages, kMaxStages);
@@ -342,8 +528,11 @@ bool plan_launch(int batch, int hidden_pad, int64_t record_bytes, int dtype, int
   out->threads = threads;
   out->vpt = vpt;
   out->stages = stages;
-  out->smem = static_cast<size_t>(stages) * record_bytes + tail;
-  return true;
+  // The ring also holds one final-sum block: at most (nvec + kMaxGrid) float4.
+  const size_t block_bytes = (static_cast<size_t>(batch) * hidden_pad / 4 + kMaxGrid) * 16;
+  out->ring = std::max((static_cast<size_t>(stages) * record_bytes + 15) / 16 * 16, block_bytes);
+  out->smem = out->ring + tail;
+  return out->smem <= static_cast<size_t>(max_smem);
 }
 
 struct OccKey {
@@ -362,8 +551,8 @@ struct OccHash {
   }
 };
 
-// Blocks per SM for a kernel configuration (also raises the kernel's dynamic
-// shared-memory limit once per device).  0 on failure.
+// Blocks per SM for a kernel configuration (after raising the kernel's
+// dynamic shared-memory limit to the device maximum).  0 on failure.
 int blocks_per_sm(KernelFn fn, int device, int threads, size_t smem) {
   static std::mutex mu;
   static std::unordered_map<OccKey, int, OccHash> cache;
@@ -373,9 +562,7 @@ int blocks_per_sm(KernelFn fn, int device, int threads, size_t smem) {
     auto it = cache.find(key);
     if (it != cache.end()) return it->second;
   }
-  if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) !=
-      cudaSuccess)
-    return 0;
+  if (!ensure_max_dynamic_smem(reinterpret_cast<const void*>(fn), device)) return 0;
   int nb = 0;
   if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, fn, threads, smem) != cudaSuccess) return 0;
   std::lock_guard<std::mutex> lock(mu);
@@ -387,13 +574,13 @@ int blocks_per_sm(KernelFn fn, int device, int threads, size_t smem) {
 
 int decode_max_batch(int hidden, int dtype) {
   const int vpt = vpt_for(hidden_pad(hidden, dtype));
-  return vpt == 1 ? 4 : (vpt == 2 ? 2 : 0);
+  return (vpt == 1 || vpt == 2) ? 4 : (vpt == 4 ? 1 : 0);
 }
 
 size_t decode_workspace_bytes(int batch, int hidden, int dtype) {
   const int hp = hidden_pad(hidden, dtype);
-  const size_t y = static_cast<size_t>(batch) * hp * sizeof(float);
-  return kWorkspaceHeader + (y + 255) / 256 * 256;
+  const size_t rows = static_cast<size_t>(kMaxGrid) * batch * hp * sizeof(float);
+  return kWorkspaceHeader + (rows + 255) / 256 * 256;
 }
 
 int indexed_ffn_decode(const void* x, int64_t ldx, int batch, int hidden, const void* packed, int64_t n_records,
@@ -418,24 +605,28 @@ int indexed_ffn_decode(const void* x, int64_t ldx, int batch, int hidden, const 
   const DeviceInfo& info = device_info(device);
   if (info.num_sms <= 0) return QCC_ERR_CUDA;
 
+  // Ids per CTA never exceed ceil(n_ids / min(#SMs, n_ids)): the grid is at
+  // least that large whenever it is smaller than n_ids.
+  const int id_cap = std::max(1, (n_ids + std::min(info.num_sms, std::max(1, n_ids)) - 1) /
+                                     std::min(info.num_sms, std::max(1, n_ids)));
   LaunchShape shape;
-  if (!plan_launch(batch, hp, rec, dtype, info.max_smem_optin, &shape)) return QCC_ERR_UNSUPPORTED;
+  if (!plan_launch(batch, hp, rec, info.max_smem_optin, id_cap, &shape)) return QCC_ERR_UNSUPPORTED;
 
   KernelFn fn = nullptr;
   if (dtype == QCC_DTYPE_BF16)
-    fn = pick_kernel<__nv_bfloat16, records_per_group(QCC_DTYPE_BF16)>(batch, shape.vpt);
+    fn = pick_kernel<__nv_bfloat16>(batch, shape.vpt);
   else if (dtype == QCC_DTYPE_F16)
-    fn = pick_kernel<__half, records_per_group(QCC_DTYPE_F16)>(batch, shape.vpt);
+    fn = pick_kernel<__half>(batch, shape.vpt);
   else
-    fn = pick_kernel<float, records_per_group(QCC_DTYPE_F32)>(batch, shape.vpt);
+    fn = pick_kernel<float>(batch, shape.vpt);
   if (fn == nullptr) return QCC_ERR_UNSUPPORTED;
 
   const int nb = blocks_per_sm(fn, device, shape.threads, shape.smem);
-  if (nb <= 0) {
-    record_cuda_error(cudaGetLastError());
-    return QCC_ERR_CUDA;
-  }
-  int64_t grid = static_cast<int64_t>(info.num_sms) * nb;
+  if (nb <= 0) return QCC_ERR_CUDA;
+  // One CTA per SM (the workspace holds kMaxGrid partial rows); every CTA
+  // must be resident at once for the grid barrier, which the cooperative
+  // launch guarantees.
+  int64_t grid = std::min<int64_t>(info.num_sms, kMaxGrid);
   if (n_ids_dev == nullptr) grid = std::min<int64_t>(grid, std::max(1, n_ids));
 
   DecodeArgs args;
@@ -453,8 +644,9 @@ int indexed_ffn_decode(const void* x, int64_t ldx, int batch, int hidden, const 
   args.n_ids_dev = n_ids_dev;
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   args.status = reinterpret_cast<unsigned int*>(ws);
-  args.counter = reinterpret_cast<unsigned int*>(ws + 4);
-  args.y_acc = reinterpret_cast<float*>(ws + kWorkspaceHeader);
+  args.arrive = reinterpret_cast<unsigned int*>(ws + 4);
+  args.depart = reinterpret_cast<unsigned int*>(ws + 8);
+  args.partials = reinterpret_cast<float*>(ws + kWorkspaceHeader);
   args.y_out = y_out;
   args.ldy = ldy;
   args.y_dtype = y_dtype;
@@ -462,9 +654,22 @@ int indexed_ffn_decode(const void* x, int64_t ldx, int batch, int hidden, const 
   args.lda = lda;
   args.a_dtype = dtype;
   args.stages = shape.stages;
+  args.id_cap = id_cap;
+  args.ring_bytes = static_cast<int64_t>(shape.ring);
+  args.x_vec = (hidden % 8 == 0) && aligned16(x) && ((ldx * dtype_bytes(dtype)) % 16 == 0);
 
-  fn<<<static_cast<unsigned>(grid), shape.threads, shape.smem, stream>>>(args);
-  if (!cuda_ok(cudaGetLastError())) return QCC_ERR_CUDA;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(grid));
+  cfg.blockDim = dim3(static_cast<unsigned>(shape.threads));
+  cfg.dynamicSmemBytes = shape.smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  clear_stale_error();
+  if (!cuda_ok(cudaLaunchKernelEx(&cfg, fn, args))) return QCC_ERR_CUDA;
   return QCC_OK;
 }
 

@@ -107,6 +107,15 @@ __device__ __forceinline__ Pack8<T> load_pack8(const T* p) {
   return r;
 }
 
+// Same 8 elements from global memory through the read-only path (16-byte aligned).
+template <typename T>
+__device__ __forceinline__ Pack8<T> load_global_pack8(const T* p) {
+  Pack8<T> r;
+#pragma unroll
+  for (int i = 0; i < Pack8<T>::kWords; ++i) r.w[i] = __ldg(reinterpret_cast<const uint4*>(p) + i);
+  return r;
+}
+
 __device__ __forceinline__ void bf16x2_to_f32(uint32_t w, float& lo, float& hi) {
   lo = __uint_as_float(w << 16);
   hi = __uint_as_float(w & 0xFFFF0000u);

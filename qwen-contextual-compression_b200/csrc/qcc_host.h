@@ -17,6 +17,12 @@ struct DeviceInfo {
 // Cached per-device properties (thread-safe).
 const DeviceInfo& device_info(int device);
 
+// Raises a kernel's dynamic shared-memory limit to the device maximum, once
+// per (kernel, device) for the whole process (thread-safe).  Raising it to
+// the maximum, rather than to the size of one launch, keeps every later
+// launch of that kernel valid whatever its size.
+bool ensure_max_dynamic_smem(const void* kernel, int device);
+
 inline bool valid_dtype(int dtype) {
   return dtype == QCC_DTYPE_BF16 || dtype == QCC_DTYPE_F16 || dtype == QCC_DTYPE_F32;
 }
@@ -34,6 +40,10 @@ inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 
 // Remembers the error text for qcc_last_cuda_error_string(); true on success.
 bool cuda_ok(cudaError_t err);
 void record_cuda_error(cudaError_t err);
+// Clears a pending error left by earlier runtime calls (so a launch check
+// reports only this library's launch), and checks the launch just made.
+void clear_stale_error();
+bool launch_ok();
 
 int decode_max_batch(int hidden, int dtype);
 size_t decode_workspace_bytes(int batch, int hidden, int dtype);

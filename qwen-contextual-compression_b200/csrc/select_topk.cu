@@ -219,15 +219,11 @@ extern "C" int qcc_select_topk(const float* scores, int64_t ld_scores, int batch
   const size_t static_smem = 8 * 1024;
   if (info.max_smem_optin <= 0 || smem + static_smem > static_cast<size_t>(info.max_smem_optin))
     return QCC_ERR_UNSUPPORTED;
-  static thread_local size_t configured[64] = {};
-  if (device < 64 && configured[device] < smem) {
-    if (!qcc::cuda_ok(cudaFuncSetAttribute(qcc::select_topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           static_cast<int>(smem))))
-      return QCC_ERR_CUDA;
-    configured[device] = smem;
-  }
+  if (!qcc::ensure_max_dynamic_smem(reinterpret_cast<const void*>(qcc::select_topk_kernel), device))
+    return QCC_ERR_CUDA;
+  qcc::clear_stale_error();
   qcc::select_topk_kernel<<<batch, qcc::kSelectThreads, smem, stream>>>(scores, ld_scores, n, k, ids_out, ld_ids);
-  if (!qcc::cuda_ok(cudaGetLastError())) return QCC_ERR_CUDA;
+  if (!qcc::launch_ok()) return QCC_ERR_CUDA;
   return QCC_OK;
 }
 
@@ -243,15 +239,11 @@ extern "C" int qcc_build_union(const int32_t* ids, int64_t ld_ids, int batch, in
   const int width = id_end - id_begin;
   const size_t smem = (static_cast<size_t>(width) + 3) / 4 * 4;
   if (info.max_smem_optin <= 0 || smem + 1024 > static_cast<size_t>(info.max_smem_optin)) return QCC_ERR_UNSUPPORTED;
-  static thread_local size_t configured[64] = {};
-  if (device < 64 && configured[device] < smem) {
-    if (!qcc::cuda_ok(cudaFuncSetAttribute(qcc::build_union_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           static_cast<int>(smem))))
-      return QCC_ERR_CUDA;
-    configured[device] = smem;
-  }
+  if (!qcc::ensure_max_dynamic_smem(reinterpret_cast<const void*>(qcc::build_union_kernel), device))
+    return QCC_ERR_CUDA;
+  qcc::clear_stale_error();
   qcc::build_union_kernel<<<1, qcc::kUnionThreads, smem, stream>>>(ids, ld_ids, batch, k, id_begin, id_end, union_ids,
                                                                    token_mask, count_out);
-  if (!qcc::cuda_ok(cudaGetLastError())) return QCC_ERR_CUDA;
+  if (!qcc::launch_ok()) return QCC_ERR_CUDA;
   return QCC_OK;
 }

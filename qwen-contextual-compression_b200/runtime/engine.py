@@ -7,8 +7,10 @@ chunk of <= 4 tokens,
 
 which is reference runtime/ffn.py:34-39 (``TorchDynamicSparseFFN.forward``)
 and runtime/cuda_indexed.py:61-64 (``cuda_indexed_ffn``) without gathered
-copies.  The fp32 accumulation workspace is owned here, one per CUDA stream,
-zeroed once; the kernel leaves it zeroed after every call.
+copies.  The kernel's scratch (a status word, grid-barrier counters and one
+fp32 partial-y row per CTA) is a device buffer shared by every engine that
+launches on the same CUDA stream -- launches on one stream never overlap --
+zeroed once; the kernel leaves its counters at zero after every call.
 """
 from __future__ import annotations
 
@@ -23,13 +25,11 @@ from .packing import PackedFFNWeights
 class DecodeWorkspace:
     """Zero-initialised scratch for qcc_indexed_ffn_decode on one stream."""
 
-    def __init__(self, device: torch.device, batch: int, hidden: int, dtype: torch.dtype, stream: torch.cuda.Stream):
+    def __init__(self, device: torch.device, nbytes: int, stream: torch.cuda.Stream):
         lib = _lib.library()
-        code = _lib.dtype_code(dtype)
-        self.nbytes = int(lib.qcc_decode_workspace_bytes(batch, hidden, code))
-        if self.nbytes == 0:
-            raise ValueError(f"no decode workspace for batch={batch} hidden={hidden}")
+        self.nbytes = nbytes
         self.buffer = torch.empty(self.nbytes, dtype=torch.uint8, device=device)
+        self.ptr = self.buffer.data_ptr()
         self.status_offset = int(lib.qcc_workspace_status_offset())
         _lib.check(lib.qcc_workspace_init(self.buffer.data_ptr(), self.nbytes, stream.cuda_stream),
                    "qcc_workspace_init")
@@ -41,6 +41,28 @@ class DecodeWorkspace:
         if clear and value:
             word.zero_()
         return value
+
+
+_workspace_lock = threading.Lock()
+_workspaces: dict[tuple[int, int], DecodeWorkspace] = {}
+
+
+def stream_workspace(device: torch.device, stream: torch.cuda.Stream, nbytes: int) -> DecodeWorkspace:
+    """The shared workspace of (device, stream), grown to at least nbytes."""
+    key = (device.index, stream.cuda_stream)
+    ws = _workspaces.get(key)
+    if ws is None or ws.nbytes < nbytes:
+        with _workspace_lock:
+            ws = _workspaces.get(key)
+            if ws is None or ws.nbytes < nbytes:
+                old = ws
+                ws = DecodeWorkspace(device, nbytes, stream)
+                if old is not None:
+                    status = old.read_status(clear=True)  # carry pending device errors over
+                    if status:
+                        ws.buffer[:4].view(torch.int32).fill_(status)
+                _workspaces[key] = ws
+    return ws
 
 
 class IndexedSparseFFN:
@@ -60,8 +82,10 @@ class IndexedSparseFFN:
         self.max_batch = int(lib.qcc_decode_max_batch(weights.hidden, self._code))
         if self.max_batch < 1:
             raise ValueError(f"hidden={weights.hidden} is beyond the decode kernel's limit")
-        self._workspaces: dict[int, DecodeWorkspace] = {}
-        self._lock = threading.Lock()
+        self._workspace_bytes = int(lib.qcc_decode_workspace_bytes(self.max_batch, weights.hidden, self._code))
+        self._streams: set[int] = set()
+        self._streams_ws: dict[int, DecodeWorkspace] = {}
+        self._plans: dict = {}
 
     @property
     def hidden(self) -> int:
@@ -72,19 +96,12 @@ class IndexedSparseFFN:
         return self.weights.n_records
 
     def workspace(self, stream: torch.cuda.Stream) -> DecodeWorkspace:
-        key = stream.cuda_stream
-        ws = self._workspaces.get(key)
-        if ws is None:
-            with self._lock:
-                ws = self._workspaces.get(key)
-                if ws is None:
-                    ws = DecodeWorkspace(self.weights.device, self.max_batch, self.hidden, self.weights.dtype, stream)
-                    self._workspaces[key] = ws
-        return ws
+        self._streams.add(stream.cuda_stream)
+        return stream_workspace(self.weights.device, stream, self._workspace_bytes)
 
     def check(self) -> None:
-        """Raise if any call since the last check flagged a device-side error."""
-        for ws in list(self._workspaces.values()):
+        """Raise if a call on this engine's streams flagged a device-side error since the last check."""
+        for ws in list(self._streams_ws.values()):
             bits = ws.read_status()
             if bits & _lib.DEV_ID_RANGE:
                 raise ValueError("selected ID out of range")
@@ -104,57 +121,106 @@ class IndexedSparseFFN:
         out_dtype:  x.dtype (default) or torch.float32 (unrounded partial sums).
         activation: optional [B, len(ids)] tensor in x.dtype receiving a_j.
         """
-        w = self.weights
-        squeeze = x.ndim == 1
+        squeeze = x.dim() == 1
         if squeeze:
             x = x.unsqueeze(0)
-        if x.ndim != 2 or x.shape[1] != w.hidden:
-            raise ValueError(f"x must be [batch, {w.hidden}], got {tuple(x.shape)}")
-        if x.dtype != w.dtype:
-            raise TypeError(f"x dtype {x.dtype} must match the weight dtype {w.dtype}")
-        if ids.ndim != 1 or not ids.is_contiguous():
-            raise ValueError("selected IDs must be contiguous one-dimensional int32 or int64")
-        if ids.dtype not in _lib.INDEX_DTYPES:
-            raise ValueError("selected IDs must be contiguous one-dimensional int32 or int64")
-        device = _lib.require_cuda(x, ids, w.packed, token_mask, n_ids_dev, out, activation)
+        plan = self._plan(x, ids, token_mask, n_ids_dev, out, out_dtype, activation)
         if x.stride(1) != 1:
             x = x.contiguous()
         batch = x.shape[0]
-        n_ids = ids.numel()
+        n_ids = ids.shape[0]
+        if out is None:
+            out = torch.empty((batch, self.weights.hidden), dtype=plan.out_dtype, device=x.device)
+        stream = _current_stream(plan.device_index)
+        ws = self._streams_ws.get(stream)
+        if ws is None:
+            ws = self._workspace_for(stream)
+        lib = plan.lib
+        x_ptr, out_ptr = x.data_ptr(), out.data_ptr()
+        x_row, out_row = x.stride(0) * plan.esize_x, out.stride(0) * plan.esize_y
+        mask_ptr = None if token_mask is None else token_mask.data_ptr()
+        count_ptr = None if n_ids_dev is None else n_ids_dev.data_ptr()
+        for start in range(0, batch, self.max_batch):
+            chunk = min(self.max_batch, batch - start)
+            a_ptr = None if activation is None else activation.data_ptr() + start * activation.stride(0) * plan.esize_x
+            if token_mask is not None and start > 0:
+                # Token bits start.. moved down to bit 0.  The temporary comes from
+                # the caching allocator on this stream, so its reuse is ordered
+                # after the kernel that reads it.
+                mask_ptr = torch.bitwise_right_shift(token_mask, start).data_ptr()
+            status = lib.qcc_indexed_ffn_decode(
+                x_ptr + start * x_row, x.stride(0), chunk, plan.hidden, plan.packed_ptr, plan.n_records, plan.code,
+                ids.data_ptr(), plan.ids_code, n_ids, count_ptr, mask_ptr, ws.ptr, ws.nbytes,
+                out_ptr + start * out_row, out.stride(0), plan.y_code, a_ptr, n_ids if a_ptr else 0, stream)
+            if status:
+                _lib.check(status, "qcc_indexed_ffn_decode")
+        if self.check_bounds:
+            self.check()
+        return out.squeeze(0) if squeeze else out
+
+    def _workspace_for(self, stream_handle: int) -> DecodeWorkspace:
+        stream = torch.cuda.ExternalStream(stream_handle, device=self.weights.device)
+        ws = self.workspace(stream)
+        self._streams_ws[stream_handle] = ws
+        return ws
+
+    def _plan(self, x, ids, token_mask, n_ids_dev, out, out_dtype, activation) -> "_Plan":
+        """Checks that depend only on shapes / dtypes / devices, cached per signature."""
+        key = (x.shape, x.dtype, x.device, ids.dim(), ids.dtype, ids.device, ids.is_contiguous(), out_dtype,
+               None if out is None else (out.shape, out.dtype, out.stride(1), out.device),
+               None if token_mask is None else (token_mask.dtype, token_mask.is_contiguous(), token_mask.numel()),
+               None if n_ids_dev is None else (n_ids_dev.dtype, n_ids_dev.numel(), n_ids_dev.device),
+               None if activation is None else (activation.shape, activation.dtype, activation.stride(1)),
+               ids.shape)
+        plan = self._plans.get(key)
+        if plan is not None:
+            return plan
+        w = self.weights
+        if x.dim() != 2 or x.shape[1] != w.hidden:
+            raise ValueError(f"x must be [batch, {w.hidden}], got {tuple(x.shape)}")
+        if x.dtype != w.dtype:
+            raise TypeError(f"x dtype {x.dtype} must match the weight dtype {w.dtype}")
+        if ids.dim() != 1 or not ids.is_contiguous() or ids.dtype not in _lib.INDEX_DTYPES:
+            raise ValueError("selected IDs must be contiguous one-dimensional int32 or int64")
+        device = _lib.require_cuda(x, ids, w.packed, token_mask, n_ids_dev, out, activation)
+        batch, n_ids = x.shape[0], ids.shape[0]
         if token_mask is not None and (token_mask.dtype != torch.uint8 or token_mask.numel() < n_ids
                                        or not token_mask.is_contiguous()):
             raise ValueError("token_mask must be a contiguous uint8 tensor with one byte per id")
         if n_ids_dev is not None and (n_ids_dev.dtype != torch.int32 or n_ids_dev.numel() != 1):
             raise ValueError("n_ids_dev must be a one-element int32 tensor")
-        out_dtype = out_dtype or x.dtype
-        if out is None:
-            out = torch.empty((batch, w.hidden), dtype=out_dtype, device=device)
-        elif out.shape != (batch, w.hidden) or out.stride(1) != 1 or out.dtype != out_dtype:
+        out_dtype = out_dtype or (out.dtype if out is not None else x.dtype)
+        if out is not None and (out.shape != (batch, w.hidden) or out.stride(1) != 1 or out.dtype != out_dtype):
             raise ValueError("out must be a row-contiguous [batch, hidden] tensor of out_dtype")
         if activation is not None and (activation.shape != (batch, n_ids) or activation.dtype != x.dtype
                                        or activation.stride(1) != 1):
             raise ValueError("activation must be a row-contiguous [batch, n_ids] tensor in x dtype")
-        lib = _lib.library()
-        stream = torch.cuda.current_stream(device)
-        ws = self.workspace(stream)
-        y_code = _lib.dtype_code(out_dtype)
-        esize_x, esize_y = x.element_size(), out.element_size()
-        for start in range(0, batch, self.max_batch):
-            chunk = min(self.max_batch, batch - start)
-            a_ptr = None if activation is None else activation.data_ptr() + start * activation.stride(0) * esize_x
-            mask = token_mask
-            if mask is not None and start > 0:
-                # Token bits start.. moved down to bit 0.  The temporary comes from
-                # the caching allocator on this stream, so its reuse is ordered
-                # after the kernel that reads it.
-                mask = torch.bitwise_right_shift(token_mask, start)
-            status = lib.qcc_indexed_ffn_decode(
-                x.data_ptr() + start * x.stride(0) * esize_x, x.stride(0), chunk, w.hidden, w.packed.data_ptr(),
-                w.n_records, self._code, ids.data_ptr(), _lib.INDEX_DTYPES[ids.dtype], n_ids,
-                _lib.ptr(n_ids_dev), _lib.ptr(mask), ws.buffer.data_ptr(), ws.nbytes,
-                out.data_ptr() + start * out.stride(0) * esize_y, out.stride(0), y_code, a_ptr,
-                n_ids if activation is not None else 0, stream.cuda_stream)
-            _lib.check(status, "qcc_indexed_ffn_decode")
-        if self.check_bounds:
-            self.check()
-        return out.squeeze(0) if squeeze else out
+        plan = _Plan(lib=_lib.library(), device_index=device.index, hidden=w.hidden, packed_ptr=w.packed.data_ptr(),
+                     n_records=w.n_records, code=self._code, ids_code=_lib.INDEX_DTYPES[ids.dtype],
+                     out_dtype=out_dtype, y_code=_lib.dtype_code(out_dtype), esize_x=x.element_size(),
+                     esize_y=torch.empty((), dtype=out_dtype).element_size())
+        if len(self._plans) > 64:
+            self._plans.clear()
+        self._plans[key] = plan
+        return plan
+
+
+class _Plan:
+    __slots__ = ("lib", "device_index", "hidden", "packed_ptr", "n_records", "code", "ids_code", "out_dtype",
+                 "y_code", "esize_x", "esize_y")
+
+    def __init__(self, **kw):
+        for k, v in kw.items():
+            setattr(self, k, v)
+
+
+def _current_stream(device_index: int) -> int:
+    """Raw handle of the current CUDA stream of a device."""
+    return _raw_stream(device_index)
+
+
+try:  # the raw-handle query avoids building a torch.cuda.Stream object per call
+    _raw_stream = torch._C._cuda_getCurrentRawStream
+except AttributeError:  # pragma: no cover
+    def _raw_stream(device_index: int) -> int:
+        return torch.cuda.current_stream(device_index).cuda_stream

@@ -43,9 +43,11 @@ def test_pure_host_queries_without_gpu():
     assert lib.qcc_record_bytes(5120, _lib.DTYPE_BF16) == 30720
     assert lib.qcc_record_bytes(5120, _lib.DTYPE_F32) == 61440
     assert lib.qcc_decode_max_batch(5120, _lib.DTYPE_BF16) == 4
-    assert lib.qcc_decode_max_batch(8192, _lib.DTYPE_BF16) == 2
+    assert lib.qcc_decode_max_batch(8192, _lib.DTYPE_BF16) == 1
+    assert lib.qcc_decode_max_batch(2560, _lib.DTYPE_BF16) == 4
     assert lib.qcc_decode_max_batch(20480, _lib.DTYPE_BF16) == 0
-    assert lib.qcc_decode_workspace_bytes(1, 5120, _lib.DTYPE_BF16) == 256 + 5120 * 4
+    # status / counters header + one fp32 partial row per CTA (up to 160 CTAs)
+    assert lib.qcc_decode_workspace_bytes(1, 5120, _lib.DTYPE_BF16) == 256 + 160 * 5120 * 4
     assert lib.qcc_workspace_status_offset() == 0
     assert lib.qcc_status_string(_lib.ERR_SHAPE).decode().startswith("inconsistent")
 
@@ -54,7 +56,8 @@ def test_argument_validation_happens_before_any_cuda_call():
     lib = _lib.library()
     dummy = ctypes.c_void_p(16)
     # batch 0 -> shape error; unknown dtype -> dtype error; tiny workspace -> workspace error.
-    args = [dummy, 8, 0, 8, dummy, 4, _lib.DTYPE_BF16, dummy, _lib.INDEX_I32, 2, None, None, dummy, 4096, dummy, 8,
+    big = 1 << 30
+    args = [dummy, 8, 0, 8, dummy, 4, _lib.DTYPE_BF16, dummy, _lib.INDEX_I32, 2, None, None, dummy, big, dummy, 8,
             _lib.DTYPE_BF16, None, 0, None]
     assert lib.qcc_indexed_ffn_decode(*args) == _lib.ERR_SHAPE
     args[2] = 1
@@ -63,7 +66,7 @@ def test_argument_validation_happens_before_any_cuda_call():
     args[6] = _lib.DTYPE_BF16
     args[13] = 16
     assert lib.qcc_indexed_ffn_decode(*args) == _lib.ERR_WORKSPACE
-    args[13] = 4096
+    args[13] = big
     args[4] = ctypes.c_void_p(18)  # packed not 16-byte aligned
     assert lib.qcc_indexed_ffn_decode(*args) == _lib.ERR_ALIGNMENT
     assert lib.qcc_select_topk(dummy, 4, 1, 4, 5, dummy, 5, None) == _lib.ERR_SHAPE  # k > n
