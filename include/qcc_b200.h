@@ -149,6 +149,36 @@ QCC_API int qcc_indexed_ffn_decode(const void* x, int64_t ldx, int batch, int hi
                            const uint8_t* token_mask, void* workspace, size_t workspace_bytes, void* y_out,
                            int64_t ldy, int y_dtype, void* activation_out, int64_t lda, cudaStream_t stream);
 
+/* Bytes of the scratch built into the library for
+ * qcc_indexed_ffn_decode_static (4 MiB). */
+#define QCC_STATIC_SCRATCH_BYTES (4u << 20)
+
+/*
+ * qcc_indexed_ffn_decode without a workspace argument: for callers that cannot
+ * allocate device memory where they run the layer (inside another
+ * framework's allocator or memory pool, plugin hosts that only hand over the
+ * input and output buffers, loops that must not call cudaMalloc / cudaFree
+ * because those can synchronise the device).  No counterpart in the
+ * reference, whose extension allocates its outputs per call.
+ *
+ * Same arguments and results as qcc_indexed_ffn_decode minus the workspace.
+ * The scratch is a fixed QCC_STATIC_SCRATCH_BYTES array in the library image,
+ * held by every GPU that loads the library until the process exits; requests
+ * needing more (qcc_decode_workspace_bytes(batch, hidden, dtype) larger than
+ * that: one token up to hidden 6552) return QCC_ERR_WORKSPACE.  The call
+ * allocates nothing.  The first call on each device looks the scratch up with
+ * cudaGetSymbolAddress (which may load the module there), so make it before
+ * any stream capture.  All calls on a device share the scratch and each one
+ * clears its header first: calls that can overlap on the GPU race and must be
+ * serialised by the caller.  Device-side status bits (QCC_DEV_*) are not
+ * reported by this variant; out-of-range ids still contribute nothing.
+ */
+QCC_API int qcc_indexed_ffn_decode_static(const void* x, int64_t ldx, int batch, int hidden, const void* packed,
+                                          int64_t n_records, int dtype, const void* ids, int ids_dtype, int n_ids,
+                                          const int32_t* n_ids_dev, const uint8_t* token_mask, void* y_out,
+                                          int64_t ldy, int y_dtype, void* activation_out, int64_t lda,
+                                          cudaStream_t stream);
+
 /* ---------------------------------------------------------------------- */
 /* Selector                                                                */
 /* ---------------------------------------------------------------------- */

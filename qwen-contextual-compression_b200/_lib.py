@@ -43,6 +43,9 @@ SIGNATURES = {
     "qcc_indexed_ffn_decode": (_c_int, [_c_void_p, _c_int64, _c_int, _c_int, _c_void_p, _c_int64, _c_int, _c_void_p,
                                         _c_int, _c_int, _c_void_p, _c_void_p, _c_void_p, _c_size_t, _c_void_p,
                                         _c_int64, _c_int, _c_void_p, _c_int64, _c_void_p]),
+    "qcc_indexed_ffn_decode_static": (_c_int, [_c_void_p, _c_int64, _c_int, _c_int, _c_void_p, _c_int64, _c_int,
+                                               _c_void_p, _c_int, _c_int, _c_void_p, _c_void_p, _c_void_p, _c_int64,
+                                               _c_int, _c_void_p, _c_int64, _c_void_p]),
     "qcc_select_topk": (_c_int, [_c_void_p, _c_int64, _c_int, _c_int, _c_int, _c_void_p, _c_int64, _c_void_p]),
     "qcc_build_union": (_c_int, [_c_void_p, _c_int64, _c_int, _c_int, ctypes.c_int32, ctypes.c_int32, _c_void_p,
                                  _c_void_p, _c_void_p, _c_void_p]),
