@@ -310,24 +310,21 @@ def run_ours(args) -> None:
         for i in range(first, first + count):
             step_call(engines[i % LAYERS], x, ids_all[i], out_buf)
 
-    # Timed: the K steps back to back in one CUDA graph (single GPU), CUDA
-    # events on the launching stream around the replay.
-    graph = None
-    if world == 1:
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph, stream=side):
-            run_steps(args.warmup, args.steps)
-        torch.cuda.synchronize(device)
+    # Timed: the K steps back to back in one CUDA graph, CUDA events on the
+    # launching stream around the replay.  With N > 1 the graph also holds the
+    # NCCL all-reduce of every step (every rank captures the same sequence);
+    # it is released before the process group is destroyed.
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=side):
+        run_steps(args.warmup, args.steps)
+    torch.cuda.synchronize(device)
     barrier()
     start_ev, end_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(device.index) as clocks:
         barrier()
         torch.cuda.synchronize(device)
         start_ev.record(stream)
-        if graph is not None:
-            graph.replay()
-        else:
-            run_steps(args.warmup, args.steps)
+        graph.replay()
         end_ev.record(stream)
         torch.cuda.synchronize(device)
         barrier()

@@ -1,0 +1,82 @@
+"""Intermediate-dimension sharding across real GPUs (NCCL), when at least two are visible.
+
+Each rank packs only its record range, keeps its part of the global ids and
+adds its fp32 partial through an NCCL all-reduce; the result must match the
+single-GPU kernel and the oracle.  Runs as spawned child processes with a
+short process-group timeout; skipped on machines with one GPU.
+"""
+from __future__ import annotations
+
+import os
+import socket
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _rank(rank: int, world: int, port: int, queue) -> None:
+    import datetime
+    import sys
+    from pathlib import Path
+    sys.path.insert(0, str(Path(__file__).resolve().parents[1]))
+    import torch.distributed as dist
+    from oracle import ffn as offn
+    import qcc_b200.workloads as workloads
+    from qcc_b200.runtime.packing import PackedFFNWeights
+    from qcc_b200.runtime.sharded import ShardedIndexedFFN, shard_range
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    device = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=device)
+    try:
+        hidden, n = 2048, 8192
+        begin, end = shard_range(n, world, rank)
+        layer = workloads.decode_layer(hidden=hidden, intermediate=n, device=device, seed=5, record_range=(begin, end))
+        ffn = ShardedIndexedFFN(PackedFFNWeights(layer.packed, hidden, end - begin, begin, n), group=dist.group.WORLD)
+        k = workloads.retention_k(n, 0.25)
+        ids = workloads.decode_ids(n, k, token=4).to(device)
+        x = workloads.decode_x(hidden=hidden).to(device)
+        y = ffn(x, ids)
+        torch.cuda.synchronize(device)
+        # Gather the full layer on rank 0 for the oracle (small layer).
+        parts = [torch.empty_like(layer.packed) if r != rank else layer.packed for r in range(world)]
+        sizes = [shard_range(n, world, r) for r in range(world)]
+        gathered = None
+        if rank == 0:
+            gathered = [torch.empty((e - b, layer.packed.shape[1]), dtype=layer.packed.dtype, device=device)
+                        for b, e in sizes]
+        dist.gather(layer.packed, gathered if rank == 0 else None, dst=0)
+        if rank == 0:
+            full = torch.cat(gathered).cpu()
+            gate, up, down = full[:, :hidden], full[:, hidden:2 * hidden], full[:, 2 * hidden:].t()
+            expected = offn.sparse_ffn_f64(x.cpu(), ids.cpu(), gate, up, down)
+            queue.put(offn.rel_l2(y.double().cpu().numpy(), expected))
+        del parts
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_two_rank_sharded_layer_matches_oracle():
+    ctx = mp.get_context("spawn")
+    queue = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rank, args=(r, 2, port, queue)) for r in range(2)]
+    for p in procs:
+        p.start()
+    err = queue.get(timeout=300)
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    assert err <= 1e-2
