@@ -102,9 +102,8 @@ QCC_API int qcc_pack_records(const void* gate, const void* up, int64_t ld_gu, co
 /* Fused indexed gated FFN (decode / small batch)                          */
 /* ---------------------------------------------------------------------- */
 
-/* Largest batch one qcc_indexed_ffn_decode call accepts (4, or 2 when
- * 1 when hidden > 5120 needs four hidden slots per thread); 0 if hidden is
- * beyond 10240. */
+/* Largest batch one qcc_indexed_ffn_decode call accepts: 4 for hidden <=
+ * 5120, 1 for hidden <= 10240 (four hidden slots per thread), 0 beyond. */
 QCC_API int qcc_decode_max_batch(int hidden, int dtype);
 
 /* Bytes of workspace qcc_indexed_ffn_decode needs for this batch/hidden. */
@@ -137,6 +136,9 @@ QCC_API int qcc_workspace_init(void* workspace, size_t workspace_bytes, cudaStre
  *                Null means every token uses every record (the reference's
  *                one shared 1-D id list, runtime/ffn.py:20-23).
  *   y_out      : [batch, hidden] in y_dtype (dtype or QCC_DTYPE_F32)
+ *   y_in       : optional fp32 [batch, hidden] (row stride ld_in) added to
+ *                the sum before the final rounding: a residual, or the
+ *                partial result of an earlier call over other records
  *   activation_out : optional [batch, n_ids] in `dtype`, the per-record
  *                activation (cuda_indexed_parts' first result,
  *                runtime/cuda_indexed.py:56-59); entries of records a token
@@ -144,10 +146,11 @@ QCC_API int qcc_workspace_init(void* workspace, size_t workspace_bytes, cudaStre
  * batch must be 1..qcc_decode_max_batch(hidden, dtype) per call (a host
  * wrapper chunks larger batches).
  */
-QCC_API int qcc_indexed_ffn_decode(const void* x, int64_t ldx, int batch, int hidden, const void* packed, int64_t n_records,
-                           int dtype, const void* ids, int ids_dtype, int n_ids, const int32_t* n_ids_dev,
-                           const uint8_t* token_mask, void* workspace, size_t workspace_bytes, void* y_out,
-                           int64_t ldy, int y_dtype, void* activation_out, int64_t lda, cudaStream_t stream);
+QCC_API int qcc_indexed_ffn_decode(const void* x, int64_t ldx, int batch, int hidden, const void* packed,
+                                   int64_t n_records, int dtype, const void* ids, int ids_dtype, int n_ids,
+                                   const int32_t* n_ids_dev, const uint8_t* token_mask, void* workspace,
+                                   size_t workspace_bytes, void* y_out, int64_t ldy, int y_dtype, const float* y_in,
+                                   int64_t ld_in, void* activation_out, int64_t lda, cudaStream_t stream);
 
 /* Bytes of the scratch built into the library for
  * qcc_indexed_ffn_decode_static (4 MiB). */
@@ -161,7 +164,8 @@ QCC_API int qcc_indexed_ffn_decode(const void* x, int64_t ldx, int batch, int hi
  * because those can synchronise the device).  No counterpart in the
  * reference, whose extension allocates its outputs per call.
  *
- * Same arguments and results as qcc_indexed_ffn_decode minus the workspace.
+ * Same arguments and results as qcc_indexed_ffn_decode minus the workspace
+ * (and without the y_in input).
  * The scratch is a fixed QCC_STATIC_SCRATCH_BYTES array in the library image,
  * held by every GPU that loads the library until the process exits; requests
  * needing more (qcc_decode_workspace_bytes(batch, hidden, dtype) larger than
@@ -208,6 +212,47 @@ QCC_API int qcc_select_topk(const float* scores, int64_t ld_scores, int batch, i
  */
 QCC_API int qcc_build_union(const int32_t* ids, int64_t ld_ids, int batch, int k, int32_t id_begin, int32_t id_end,
                     int32_t* union_ids, uint8_t* token_mask, int32_t* count_out, cudaStream_t stream);
+
+/* ---------------------------------------------------------------------- */
+/* Host-offload stager                                                     */
+/* ---------------------------------------------------------------------- */
+
+/*
+ * Device-side neuron cache policy for one decode step of one layer whose
+ * records live partly in HBM and partly in a pinned host store.  The HBM
+ * "resident" array holds n_hot always-resident records in slots [0, n_hot)
+ * followed by `capacity` cache slots; slot_of[n] is record n's resident slot
+ * or -1.  For the step's sorted, unique ids (count k, or *k_dev when non-null)
+ * it writes the resident slots of hot records and cache hits
+ * (resident_out), and gives every miss the least recently used cache slot
+ * this step does not use -- empty slots first, ties by the held record's id,
+ * the eviction order of reference runtime/temporal.py:57-75 -- updating
+ * slot_of, cache_owner and cache_last_use in place (miss_slot_out: the slots,
+ * miss_src_out: the records' cold_index entries).  counts_out (device int32
+ * [6]): resident, misses served, cache hits, evicted, hot hits, 1 if misses
+ * exceeded the free slots.  capacity <= 8192, n_records and step < 2^24 - 1.
+ * One CTA; no host round trip.  The reference stages whole layers
+ * synchronously (integration/freetoken_qcc/low_vram/staging.py:43-67) and
+ * keeps its LRU only as a host-side simulation.
+ */
+QCC_API int qcc_cache_resolve(const int32_t* ids, int k, const int32_t* k_dev, int32_t* slot_of, int n_records,
+                              int n_hot, int32_t* cache_owner, int32_t* cache_last_use, int capacity,
+                              const int32_t* cold_index, int step, int32_t* resident_out, int32_t* miss_slot_out,
+                              int32_t* miss_src_out, int32_t* counts_out, cudaStream_t stream);
+
+/*
+ * Copies records src_index[i] of a host store (page-locked host memory, read
+ * through its device mapping; pageable memory returns
+ * QCC_ERR_INVALID_ARGUMENT) into resident slots dst_slot[i] of `packed`,
+ * for i < min(*count_dev, max_count) (max_count when count_dev is null).
+ * Reads the host memory in place over PCIe; runs on `stream`, typically a
+ * side stream overlapping the decode of the resident records.  Replaces the
+ * row gather HostLayer.neuron_tensor
+ * (integration/freetoken_qcc/low_vram/host_store.py:24-26) plus its copy.
+ */
+QCC_API int qcc_gather_records(const void* host_store, int64_t record_bytes, const int32_t* src_index,
+                               const int32_t* dst_slot, const int32_t* count_dev, int max_count, void* packed,
+                               cudaStream_t stream);
 
 /* Elementwise cast of n fp32 values to dtype (used after a cross-rank sum). */
 QCC_API int qcc_cast_f32(const float* src, void* dst, int64_t n, int dtype, cudaStream_t stream);

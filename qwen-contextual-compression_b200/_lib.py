@@ -42,7 +42,7 @@ SIGNATURES = {
     "qcc_workspace_init": (_c_int, [_c_void_p, _c_size_t, _c_void_p]),
     "qcc_indexed_ffn_decode": (_c_int, [_c_void_p, _c_int64, _c_int, _c_int, _c_void_p, _c_int64, _c_int, _c_void_p,
                                         _c_int, _c_int, _c_void_p, _c_void_p, _c_void_p, _c_size_t, _c_void_p,
-                                        _c_int64, _c_int, _c_void_p, _c_int64, _c_void_p]),
+                                        _c_int64, _c_int, _c_void_p, _c_int64, _c_void_p, _c_int64, _c_void_p]),
     "qcc_indexed_ffn_decode_static": (_c_int, [_c_void_p, _c_int64, _c_int, _c_int, _c_void_p, _c_int64, _c_int,
                                                _c_void_p, _c_int, _c_int, _c_void_p, _c_void_p, _c_void_p, _c_int64,
                                                _c_int, _c_void_p, _c_int64, _c_void_p]),
@@ -50,6 +50,11 @@ SIGNATURES = {
     "qcc_build_union": (_c_int, [_c_void_p, _c_int64, _c_int, _c_int, ctypes.c_int32, ctypes.c_int32, _c_void_p,
                                  _c_void_p, _c_void_p, _c_void_p]),
     "qcc_cast_f32": (_c_int, [_c_void_p, _c_void_p, _c_int64, _c_int, _c_void_p]),
+    "qcc_cache_resolve": (_c_int, [_c_void_p, _c_int, _c_void_p, _c_void_p, _c_int, _c_int, _c_void_p, _c_void_p,
+                                   _c_int, _c_void_p, _c_int, _c_void_p, _c_void_p, _c_void_p, _c_void_p,
+                                   _c_void_p]),
+    "qcc_gather_records": (_c_int, [_c_void_p, _c_int64, _c_void_p, _c_void_p, _c_void_p, _c_int, _c_void_p,
+                                    _c_void_p]),
 }
 
 _lock = threading.Lock()

@@ -58,6 +58,8 @@ struct DecodeArgs {
   void* y_out;
   int64_t ldy;
   int y_dtype;
+  const float* y_in;     // optional fp32 [B, ld_in] added to the result
+  int64_t ld_in;
   void* a_out;
   int64_t lda;
   int a_dtype;
@@ -440,7 +442,9 @@ __global__ void __launch_bounds__(kMaxThreads, 1) indexed_ffn_decode_kernel(cons
           const float vals[4] = {acc.x, acc.y, acc.z, acc.w};
 #pragma unroll
           for (int e = 0; e < 4; ++e)
-            if (h0 + e < a.hidden) store_as(a.y_out, b * a.ldy + h0 + e, a.y_dtype, vals[e]);
+            if (h0 + e < a.hidden)
+              store_as(a.y_out, b * a.ldy + h0 + e, a.y_dtype,
+                       vals[e] + (a.y_in != nullptr ? __ldg(a.y_in + b * a.ld_in + h0 + e) : 0.f));
         }
       }
     }
@@ -586,13 +590,15 @@ size_t decode_workspace_bytes(int batch, int hidden, int dtype) {
 int indexed_ffn_decode(const void* x, int64_t ldx, int batch, int hidden, const void* packed, int64_t n_records,
                        int dtype, const void* ids, int ids_dtype, int n_ids, const int32_t* n_ids_dev,
                        const uint8_t* token_mask, void* workspace, size_t workspace_bytes, void* y_out, int64_t ldy,
-                       int y_dtype, void* activation_out, int64_t lda, cudaStream_t stream) {
+                       int y_dtype, const float* y_in, int64_t ld_in, void* activation_out, int64_t lda,
+                       cudaStream_t stream) {
   if (!valid_dtype(dtype) || !valid_dtype(y_dtype)) return QCC_ERR_DTYPE;
   if (y_dtype != dtype && y_dtype != QCC_DTYPE_F32) return QCC_ERR_DTYPE;
   if (ids_dtype != QCC_INDEX_I32 && ids_dtype != QCC_INDEX_I64) return QCC_ERR_DTYPE;
   if (batch < 1 || hidden < 1 || n_records < 0 || n_ids < 0) return QCC_ERR_SHAPE;
   if (batch > decode_max_batch(hidden, dtype)) return QCC_ERR_UNSUPPORTED;
   if (ldx < hidden || ldy < hidden || (activation_out != nullptr && lda < n_ids)) return QCC_ERR_SHAPE;
+  if (y_in != nullptr && ld_in < hidden) return QCC_ERR_SHAPE;
   if (x == nullptr || y_out == nullptr || workspace == nullptr) return QCC_ERR_INVALID_ARGUMENT;
   if (n_ids > 0 && (ids == nullptr || packed == nullptr)) return QCC_ERR_INVALID_ARGUMENT;
   if (workspace_bytes < decode_workspace_bytes(batch, hidden, dtype)) return QCC_ERR_WORKSPACE;
@@ -650,6 +656,8 @@ int indexed_ffn_decode(const void* x, int64_t ldx, int batch, int hidden, const 
   args.y_out = y_out;
   args.ldy = ldy;
   args.y_dtype = y_dtype;
+  args.y_in = y_in;
+  args.ld_in = ld_in;
   args.a_out = activation_out;
   args.lda = lda;
   args.a_dtype = dtype;
@@ -689,8 +697,9 @@ extern "C" int qcc_indexed_ffn_decode(const void* x, int64_t ldx, int batch, int
                                       int64_t n_records, int dtype, const void* ids, int ids_dtype, int n_ids,
                                       const int32_t* n_ids_dev, const uint8_t* token_mask, void* workspace,
                                       size_t workspace_bytes, void* y_out, int64_t ldy, int y_dtype,
-                                      void* activation_out, int64_t lda, cudaStream_t stream) {
+                                      const float* y_in, int64_t ld_in, void* activation_out, int64_t lda,
+                                      cudaStream_t stream) {
   return qcc::indexed_ffn_decode(x, ldx, batch, hidden, packed, n_records, dtype, ids, ids_dtype, n_ids, n_ids_dev,
-                                 token_mask, workspace, workspace_bytes, y_out, ldy, y_dtype, activation_out, lda,
-                                 stream);
+                                 token_mask, workspace, workspace_bytes, y_out, ldy, y_dtype, y_in, ld_in,
+                                 activation_out, lda, stream);
 }

@@ -75,6 +75,6 @@ extern "C" int qcc_indexed_ffn_decode_static(const void* x, int64_t ldx, int bat
   // written before they are read and need no clearing.
   if (!qcc::cuda_ok(cudaMemsetAsync(scratch, 0, qcc::kScratchHeaderBytes, stream))) return QCC_ERR_CUDA;
   return qcc::indexed_ffn_decode(x, ldx, batch, hidden, packed, n_records, dtype, ids, ids_dtype, n_ids, n_ids_dev,
-                                 token_mask, scratch, qcc::kStaticScratchBytes, y_out, ldy, y_dtype, activation_out,
-                                 lda, stream);
+                                 token_mask, scratch, qcc::kStaticScratchBytes, y_out, ldy, y_dtype, nullptr, 0,
+                                 activation_out, lda, stream);
 }

@@ -51,6 +51,7 @@ size_t decode_workspace_bytes(int batch, int hidden, int dtype);
 int indexed_ffn_decode(const void* x, int64_t ldx, int batch, int hidden, const void* packed, int64_t n_records,
                        int dtype, const void* ids, int ids_dtype, int n_ids, const int32_t* n_ids_dev,
                        const uint8_t* token_mask, void* workspace, size_t workspace_bytes, void* y_out, int64_t ldy,
-                       int y_dtype, void* activation_out, int64_t lda, cudaStream_t stream);
+                       int y_dtype, const float* y_in, int64_t ld_in, void* activation_out, int64_t lda,
+                       cudaStream_t stream);
 
 }  // namespace qcc

@@ -113,13 +113,15 @@ class IndexedSparseFFN:
 
     def forward(self, x: torch.Tensor, ids: torch.Tensor, *, token_mask: torch.Tensor | None = None,
                 n_ids_dev: torch.Tensor | None = None, out: torch.Tensor | None = None,
-                out_dtype: torch.dtype | None = None, activation: torch.Tensor | None = None) -> torch.Tensor:
+                out_dtype: torch.dtype | None = None, activation: torch.Tensor | None = None,
+                accumulate: torch.Tensor | None = None) -> torch.Tensor:
         """y [B, H] for x [B, H] (or [H] -> [H]) and the 1-D selected-id list ``ids``.
 
         token_mask: optional uint8 [len(ids)], bit b = token b uses record j.
         n_ids_dev:  optional int32 device scalar; only the first n ids are used.
         out_dtype:  x.dtype (default) or torch.float32 (unrounded partial sums).
         activation: optional [B, len(ids)] tensor in x.dtype receiving a_j.
+        accumulate: optional fp32 [B, H] added before the final rounding.
         """
         squeeze = x.dim() == 1
         if squeeze:
@@ -140,6 +142,13 @@ class IndexedSparseFFN:
         x_row, out_row = x.stride(0) * plan.esize_x, out.stride(0) * plan.esize_y
         mask_ptr = None if token_mask is None else token_mask.data_ptr()
         count_ptr = None if n_ids_dev is None else n_ids_dev.data_ptr()
+        acc_row = acc_ld = 0
+        if accumulate is not None:
+            if (accumulate.dtype != torch.float32 or accumulate.shape != (batch, plan.hidden)
+                    or accumulate.stride(1) != 1 or accumulate.device != x.device):
+                raise ValueError("accumulate must be a row-contiguous fp32 [batch, hidden] tensor on x's device")
+            acc_ld = accumulate.stride(0)
+            acc_row = acc_ld * 4
         for start in range(0, batch, self.max_batch):
             chunk = min(self.max_batch, batch - start)
             a_ptr = None if activation is None else activation.data_ptr() + start * activation.stride(0) * plan.esize_x
@@ -148,10 +157,12 @@ class IndexedSparseFFN:
                 # the caching allocator on this stream, so its reuse is ordered
                 # after the kernel that reads it.
                 mask_ptr = torch.bitwise_right_shift(token_mask, start).data_ptr()
+            acc_ptr = None if accumulate is None else accumulate.data_ptr() + start * acc_row
             status = lib.qcc_indexed_ffn_decode(
                 x_ptr + start * x_row, x.stride(0), chunk, plan.hidden, plan.packed_ptr, plan.n_records, plan.code,
                 ids.data_ptr(), plan.ids_code, n_ids, count_ptr, mask_ptr, ws.ptr, ws.nbytes,
-                out_ptr + start * out_row, out.stride(0), plan.y_code, a_ptr, n_ids if a_ptr else 0, stream)
+                out_ptr + start * out_row, out.stride(0), plan.y_code, acc_ptr, acc_ld, a_ptr, n_ids if a_ptr else 0,
+                stream)
             if status:
                 _lib.check(status, "qcc_indexed_ffn_decode")
         if self.check_bounds:

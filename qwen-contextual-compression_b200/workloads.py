@@ -12,6 +12,12 @@ the same seed gives the same weights on the same GPU/torch build.
 * selector (``selector_scores``): fp32 scores ~ Laplace(0, 1) per token; a
   hot 10% of neurons (seeded permutation) gets boost c*(i+1)^-1.1, c = 8, for
   the i-th hot neuron (Zipf(1.1)-ranked).
+* offload (``offload_hot_set`` / ``offload_token_ids``): 25% of the
+  intermediate neurons (seeded permutation) are "hot" and stay in HBM; per
+  token K = ceil(0.1 N) ids, token 0 drawing 80% of them from the hot set and
+  20% from the cold rest; every later token keeps a seeded 50% of the
+  previous token's ids and draws the rest 80/20 hot/cold, without
+  replacement, from neurons it does not already hold.  Ids sorted.
 * oracle layer (``oracle_layer``): hidden 1024, intermediate 3072, fp32,
   gate/up [N,H] and down [H,N] ~ N(0, 0.02^2) drawn in that order from seed 0,
   64 tokens x ~ N(0,1) RMS-normalised as x / sqrt(mean(x^2) + 1e-6).
@@ -108,3 +114,43 @@ def oracle_layer(hidden: int = 1024, intermediate: int = 3072, tokens: int = 64,
 def decode_bytes(k: int, hidden: int = DECODE_HIDDEN, esize: int = 2, batch: int = 1, index_bytes: int = 4) -> int:
     """Algorithmic HBM bytes of one decode call: K records + x + ids + y."""
     return k * 3 * hidden * esize + batch * hidden * esize + k * index_bytes + batch * hidden * esize
+
+
+def offload_hot_set(intermediate: int = DECODE_INTERMEDIATE, hot_fraction: float = 0.25, seed: int = 11) -> torch.Tensor:
+    """Sorted int64 ids of the always-resident neurons of a layer."""
+    gen = torch.Generator().manual_seed(seed)
+    n_hot = int(round(hot_fraction * intermediate))
+    return torch.randperm(intermediate, generator=gen)[:n_hot].sort().values
+
+
+def offload_token_ids(intermediate: int, k: int, hot: torch.Tensor, tokens: int, hot_pick: float = 0.8,
+                      reuse: float = 0.5, seed: int = 12) -> list[torch.Tensor]:
+    """Per-token sorted int32 id sets with hot-set bias and temporal reuse (CPU)."""
+    gen = torch.Generator().manual_seed(seed)
+    is_hot = torch.zeros(intermediate, dtype=torch.bool)
+    is_hot[hot] = True
+
+    def draw(count: int, exclude: torch.Tensor) -> torch.Tensor:
+        want_hot = int(round(hot_pick * count))
+        hot_pool = torch.nonzero(is_hot & ~exclude).flatten()
+        cold_pool = torch.nonzero(~is_hot & ~exclude).flatten()
+        want_hot = min(want_hot, hot_pool.numel())
+        want_cold = min(count - want_hot, cold_pool.numel())
+        picked = [hot_pool[torch.randperm(hot_pool.numel(), generator=gen)[:want_hot]],
+                  cold_pool[torch.randperm(cold_pool.numel(), generator=gen)[:want_cold]]]
+        return torch.cat(picked)
+
+    out = []
+    prev = None
+    for _ in range(tokens):
+        taken = torch.zeros(intermediate, dtype=torch.bool)
+        if prev is None:
+            ids = draw(k, taken)
+        else:
+            keep = prev[torch.randperm(prev.numel(), generator=gen)[:int(round(reuse * k))]]
+            taken[keep] = True
+            ids = torch.cat([keep, draw(k - keep.numel(), taken)])
+        ids = ids.sort().values
+        out.append(ids.to(torch.int32))
+        prev = ids.long()
+    return out

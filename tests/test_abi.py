@@ -58,7 +58,7 @@ def test_argument_validation_happens_before_any_cuda_call():
     # batch 0 -> shape error; unknown dtype -> dtype error; tiny workspace -> workspace error.
     big = 1 << 30
     args = [dummy, 8, 0, 8, dummy, 4, _lib.DTYPE_BF16, dummy, _lib.INDEX_I32, 2, None, None, dummy, big, dummy, 8,
-            _lib.DTYPE_BF16, None, 0, None]
+            _lib.DTYPE_BF16, None, 0, None, 0, None]
     assert lib.qcc_indexed_ffn_decode(*args) == _lib.ERR_SHAPE
     args[2] = 1
     args[6] = 9

@@ -44,7 +44,7 @@ def _decode_with_workspace(lib, weights, x, ids, stream):
     status = lib.qcc_indexed_ffn_decode(x.data_ptr(), x.stride(0), 1, weights.hidden, weights.packed.data_ptr(),
                                         weights.n_records, code, ids.data_ptr(), _lib.INDEX_I32, ids.numel(), None,
                                         None, ws.data_ptr(), nbytes, y.data_ptr(), y.stride(0), code, None, 0,
-                                        stream)
+                                        None, 0, stream)
     _lib.check(status, "qcc_indexed_ffn_decode")
     return y
 
