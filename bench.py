@@ -65,6 +65,9 @@ def parse_args():
     p.add_argument("--cpu-seconds", type=float, default=15.0, help="bound on the CPU baseline sample")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-sweep", action="store_true")
+    p.add_argument("--no-selector", action="store_true", help="skip the selector + fused FFN measurement")
+    p.add_argument("--no-offload", action="store_true", help="skip the 8-layer host-offload measurement")
+    p.add_argument("--offload-tokens", type=int, default=12)
     return p.parse_args()
 
 
@@ -197,6 +200,123 @@ def host_description() -> str:
     except OSError:
         pass
     return "unknown"
+
+
+def graph_time_us(fn, steps: int, stream: torch.cuda.Stream, side: torch.cuda.Stream) -> float:
+    """Mean device time of fn(i) for i < steps, captured back to back in one CUDA graph."""
+    with torch.cuda.stream(side):
+        for i in range(min(3, steps)):
+            fn(i)
+    torch.cuda.current_stream().wait_stream(side)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=side):
+        for i in range(steps):
+            fn(i)
+    graph.replay()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    graph.replay()
+    end.record(stream)
+    end.synchronize()
+    del graph
+    return 1e3 * start.elapsed_time(end) / steps
+
+
+def measure_selector(engine, x, device, stream, side) -> dict:
+    """Selector workload: top-K (K/N = 0.2) over per-neuron fp32 scores, then the fused FFN.
+
+    Batch 1 uses the selected ids directly; batch 8 merges the per-token id
+    sets (qcc_build_union) and runs the fused kernel with per-record token bits.
+    """
+    from qcc_b200.runtime.selector import build_union, select_topk
+
+    k = workloads.retention_k(INTERMEDIATE, 0.2)
+    out = {"k": k, "scores": "Laplace(0,1) with a Zipf(1.1)-boosted hot 10% (seeded)"}
+    steps = 20
+    scores1 = workloads.selector_scores(steps, seed=21).to(device)
+    ids1 = torch.empty((1, k), dtype=torch.int32, device=device)
+    y1 = torch.empty((1, HIDDEN), dtype=torch.bfloat16, device=device)
+    out["select_us_batch1"] = round(graph_time_us(lambda i: select_topk(scores1[i:i + 1], k, out=ids1), steps,
+                                                  stream, side), 2)
+
+    def step1(i):
+        select_topk(scores1[i:i + 1], k, out=ids1)
+        engine(x, ids1[0], out=y1)
+
+    out["select_ffn_us_batch1"] = round(graph_time_us(step1, steps, stream, side), 2)
+    batch = 8
+    scores8 = [workloads.selector_scores(batch, seed=40 + i).to(device) for i in range(steps)]
+    ids8 = torch.empty((batch, k), dtype=torch.int32, device=device)
+    x8 = workloads.decode_x(batch=batch).to(device)
+    y8 = torch.empty((batch, HIDDEN), dtype=torch.bfloat16, device=device)
+
+    def step8(i):
+        select_topk(scores8[i], k, out=ids8)
+        union, mask, count = build_union(ids8, 0, INTERMEDIATE)
+        engine(x8, union, token_mask=mask, n_ids_dev=count, out=y8)
+
+    out["select_union_ffn_us_batch8"] = round(graph_time_us(step8, steps, stream, side), 2)
+    union, _, count = build_union(select_topk(scores8[0], k), 0, INTERMEDIATE)
+    out["union_records_batch8"] = int(count.item())
+    return out
+
+
+def measure_offload(device, tokens: int) -> dict:
+    """Eight layers with 25 % of their records in HBM and the rest in pinned host RAM.
+
+    Per token every layer selects K = ceil(0.1 N) ids (80 % from the hot set,
+    50 % reused from the previous token); misses stream from the host store
+    into an LRU cache of 2048 slots per layer while the resident records run.
+    """
+    from qcc_b200.runtime.stager import HostOffloadLayer
+
+    n_layers, capacity = 8, 2048
+    k = workloads.retention_k(INTERMEDIATE, 0.1)
+    layers, seqs = [], []
+    for l in range(n_layers):
+        packed = workloads.decode_layer(device=device, seed=100 + l).packed
+        hot = workloads.offload_hot_set(INTERMEDIATE, seed=11 + l)
+        layers.append(HostOffloadLayer(packed, HIDDEN, hot, capacity=capacity, max_k=k, device=device))
+        del packed
+        seqs.append([t.to(device) for t in workloads.offload_token_ids(INTERMEDIATE, k, hot, tokens, seed=12 + l)])
+    torch.cuda.empty_cache()
+    x = workloads.decode_x().to(device)
+    stream = torch.cuda.current_stream(device)
+    per_token_ms, misses = [], []
+    for t in range(tokens):
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        token_misses = 0
+        for l, layer in enumerate(layers):
+            layer(x, seqs[l][t])
+        end.record(stream)
+        end.synchronize()
+        for layer in layers:
+            token_misses += layer.stats()["misses"]
+        per_token_ms.append(start.elapsed_time(end))
+        misses.append(token_misses)
+    record = layers[0].record_bytes
+    steady = list(range(2, tokens))
+    steady_ms = sum(per_token_ms[t] for t in steady)
+    steady_bytes = sum(misses[t] for t in steady) * record
+    # Pinned host -> device copy peak on this box (cudaMemcpyAsync, 256 MiB).
+    host = torch.empty(256 << 20, dtype=torch.uint8).pin_memory()
+    dev = torch.empty_like(host, device=device)
+    best = 0.0
+    for _ in range(3):
+        s0, e0 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s0.record(stream)
+        dev.copy_(host, non_blocking=True)
+        e0.record(stream)
+        e0.synchronize()
+        best = max(best, host.numel() / (s0.elapsed_time(e0) * 1e-3) / 1e9)
+    return {"layers": n_layers, "tokens": tokens, "k": k, "hot_fraction": 0.25, "cache_slots": capacity,
+            "cold_start_us_per_layer": round(1e3 * per_token_ms[0] / n_layers, 1),
+            "steady_us_per_layer": round(1e3 * steady_ms / (len(steady) * n_layers), 1),
+            "steady_miss_records_per_layer": round(sum(misses[t] for t in steady) / (len(steady) * n_layers), 1),
+            "steady_cold_gbs": round(steady_bytes / (steady_ms * 1e-3) / 1e9, 2),
+            "pinned_h2d_peak_gbs": round(best, 2)}
 
 
 # ---------------------------------------------------------------------------
@@ -401,6 +521,13 @@ def run_ours(args) -> None:
             sweep[str(r)] = {"k": kk, "us_per_layer": round(us, 2),
                              "gbs": round(step_bytes(kk) / (us * 1e-6) / 1e9, 1)}
 
+    selector = None
+    if not args.no_selector and world == 1:
+        selector = measure_selector(engines[0], x, device, stream, side)
+    offload = None
+    if not args.no_offload and world == 1:
+        offload = measure_offload(device, args.offload_tokens)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         packed = layer.packed.cpu()
@@ -450,6 +577,10 @@ def run_ours(args) -> None:
     }
     if sweep is not None:
         line["sweep"] = sweep
+    if selector is not None:
+        line["selector_ffn"] = selector
+    if offload is not None:
+        line["offload"] = offload
     if cpu is not None:
         line["cpu_baseline"] = {"value": round(cpu["gbs"], 4), "unit": "GB/s", "cores": cpu["threads"],
                                 "kind": "port", "us_per_layer": round(cpu["seconds_median"] * 1e6, 1),

@@ -195,7 +195,7 @@ QCC_API int qcc_indexed_ffn_decode_static(const void* x, int64_t ldx, int batch,
  * runtime/cuda_selector.py:40 and end_to_end/oracle_sparse_mlp.py:75, whose
  * tie order is unspecified; this is the deterministic order
  * sort(scores, descending, stable)[:k] then ascending.
- * n * 4 bytes must fit in shared memory (n <= 53248).
+ * n * 4 bytes must fit in shared memory (n <= 52224).
  */
 QCC_API int qcc_select_topk(const float* scores, int64_t ld_scores, int batch, int n, int k, int32_t* ids_out, int64_t ld_ids,
                     cudaStream_t stream);

@@ -72,6 +72,9 @@ __global__ void __launch_bounds__(kSelectThreads, 1)
     select_topk_kernel(const float* __restrict__ scores, int64_t ld_scores, int n, int k, int32_t* __restrict__ ids,
                        int64_t ld_ids) {
   extern __shared__ __align__(16) uint32_t keys[];
+  // Per-warp histograms, two 16-bit bin counters per word (a warp sees at most
+  // n / 32 <= 1632 keys per pass, so a counter never overflows).
+  __shared__ uint32_t whist[kSelectThreads / 32][128];
   __shared__ int hist[256];
   __shared__ int suffix[257];
   __shared__ int scan_scratch[64];
@@ -80,6 +83,9 @@ __global__ void __launch_bounds__(kSelectThreads, 1)
 
   const int row = blockIdx.x;
   const int tid = threadIdx.x;
+  const int lane = tid & 31;
+  const int warp = tid >> 5;
+  const int nwarps = blockDim.x >> 5;
   const float* src = scores + row * ld_scores;
   int32_t* out = ids + row * ld_ids;
 
@@ -92,17 +98,29 @@ __global__ void __launch_bounds__(kSelectThreads, 1)
 
   uint32_t mask = 0u;
   for (int shift = 24; shift >= 0; shift -= 8) {
-    for (int i = tid; i < 256; i += blockDim.x) hist[i] = 0;
+    for (int i = tid; i < nwarps * 128; i += blockDim.x) (&whist[0][0])[i] = 0u;
     __syncthreads();
     const uint32_t prefix = s_prefix;
-    for (int i = tid; i < n; i += blockDim.x) {
-      const uint32_t key = keys[i];
-      if ((key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 0xFFu], 1);
+    // Lanes of a warp that fall into the same bin are counted by one atomic
+    // (score distributions crowd the high-order bins).
+    for (int base = 0; base < n; base += blockDim.x) {
+      const int i = base + tid;
+      const uint32_t key = i < n ? keys[i] : 0u;
+      const bool hit = i < n && (key & mask) == prefix;
+      const uint32_t bin = (key >> shift) & 0xFFu;
+      const unsigned peers = __match_any_sync(0xffffffffu, hit ? bin : 0x100u);
+      if (hit && lane == __ffs(peers) - 1)
+        atomicAdd(&whist[warp][bin >> 1], static_cast<uint32_t>(__popc(peers)) << (16 * (bin & 1u)));
+    }
+    __syncthreads();
+    if (tid < 256) {
+      int c = 0;
+      for (int w = 0; w < nwarps; ++w) c += (whist[w][tid >> 1] >> (16 * (tid & 1))) & 0xFFFFu;
+      hist[tid] = c;
     }
     __syncthreads();
     // Inclusive suffix sums over the 256 bins (warps 0..7, one bin per thread).
     if (tid < 256) {
-      const int lane = tid & 31;
       const int w = tid >> 5;
       // Reverse order so that a prefix scan gives suffix sums.
       int x = hist[255 - tid];
@@ -216,7 +234,7 @@ extern "C" int qcc_select_topk(const float* scores, int64_t ld_scores, int batch
   if (!qcc::cuda_ok(cudaGetDevice(&device))) return QCC_ERR_CUDA;
   const qcc::DeviceInfo& info = qcc::device_info(device);
   const size_t smem = static_cast<size_t>(n) * sizeof(uint32_t);
-  const size_t static_smem = 8 * 1024;
+  const size_t static_smem = 20 * 1024;  // per-warp histograms, bins, scan scratch
   if (info.max_smem_optin <= 0 || smem + static_smem > static_cast<size_t>(info.max_smem_optin))
     return QCC_ERR_UNSUPPORTED;
   if (!qcc::ensure_max_dynamic_smem(reinterpret_cast<const void*>(qcc::select_topk_kernel), device))
