@@ -257,6 +257,41 @@ QCC_API int qcc_gather_records(const void* host_store, int64_t record_bytes, con
 /* Elementwise cast of n fp32 values to dtype (used after a cross-rank sum). */
 QCC_API int qcc_cast_f32(const float* src, void* dst, int64_t n, int dtype, cudaStream_t stream);
 
+/* ---------------------------------------------------------------------------
+ * Block-sparse prefill.
+ *
+ * Replaces, for a prefill of n_tokens rows, the per-tile loop of
+ * runtime/ffn.py:20-39 (TorchDynamicSparseFFN on each tile's ids) over ids that
+ * come in whole blocks: block b stands for records [64b, 64b + 64), the
+ * expansion of clustering/block_layout.py:61-64 and the block top-K of
+ * oracle/importance.py:26-35.  Tokens form tiles of 128 rows (the last tile may
+ * be partial); tile t uses the blocks tile_blocks[tile_offsets[t] ..
+ * tile_offsets[t+1]), device arrays, each block at most once per tile, any
+ * order.  For every row r of tile t:
+ *   y[r] = sum over records n of t's blocks of silu(g_n . x_r) (u_n . x_r) d_n,
+ * fp32 accumulation on the tensor cores; the activation is rounded to the
+ * weight type between the two products (as the reference's CUDA path rounds it
+ * to fp16, runtime/cuda_indexed.py:28-30).
+ * ------------------------------------------------------------------------- */
+
+/* Workspace for qcc_indexed_ffn_prefill on the current device (0 on bad
+ * arguments).  Zero it once (qcc_workspace_init); calls leave it reusable. */
+QCC_API size_t qcc_prefill_workspace_bytes(int64_t n_records, int hidden);
+
+/* Byte offset of the int32 status word (QCC_DEV_* bits) in that workspace. */
+QCC_API size_t qcc_prefill_workspace_status_offset(void);
+
+/* x: [n_tokens, hidden] with row stride ldx (elements, ldx * 2 a multiple of
+ * 16), bf16 or fp16 like the records; packed: n_records records as packed by
+ * qcc_pack_records; tile_offsets: ceil(n_tokens / 128) + 1 entries;
+ * y: [n_tokens, hidden], row stride ldy, y_dtype.  fp32 records return
+ * QCC_ERR_UNSUPPORTED.  Block ids out of range are skipped and set
+ * QCC_DEV_ID_RANGE in the workspace status. */
+QCC_API int qcc_indexed_ffn_prefill(const void* x, int64_t ldx, int n_tokens, int hidden, const void* packed,
+                                    int64_t n_records, int dtype, const int32_t* tile_blocks,
+                                    const int32_t* tile_offsets, void* workspace, size_t workspace_bytes, void* y,
+                                    int64_t ldy, int y_dtype, cudaStream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

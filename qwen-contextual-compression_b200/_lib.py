@@ -55,6 +55,11 @@ SIGNATURES = {
                                    _c_void_p]),
     "qcc_gather_records": (_c_int, [_c_void_p, _c_int64, _c_void_p, _c_void_p, _c_void_p, _c_int, _c_void_p,
                                     _c_void_p]),
+    "qcc_prefill_workspace_bytes": (_c_size_t, [_c_int64, _c_int]),
+    "qcc_prefill_workspace_status_offset": (_c_size_t, []),
+    "qcc_indexed_ffn_prefill": (_c_int, [_c_void_p, _c_int64, _c_int, _c_int, _c_void_p, _c_int64, _c_int,
+                                         _c_void_p, _c_void_p, _c_void_p, _c_size_t, _c_void_p, _c_int64, _c_int,
+                                         _c_void_p]),
 }
 
 _lock = threading.Lock()

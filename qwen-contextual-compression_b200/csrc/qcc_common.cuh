@@ -178,6 +178,39 @@ __device__ __forceinline__ void store_as(void* base, int64_t idx, int dtype, flo
     reinterpret_cast<float*>(base)[idx] = v;
 }
 
+// Exclusive block-wide scan of one int per thread (blockDim.x a multiple of
+// 32, at most 1024).  Returns this thread's prefix; *total receives the block
+// sum.  `scratch` holds >= 33 ints.  Contains __syncthreads: call from every
+// thread of the block.
+__device__ __forceinline__ int block_exclusive_scan(int v, int* scratch, int* total) {
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int nwarps = blockDim.x >> 5;
+  int x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) scratch[warp] = x;
+  __syncthreads();
+  if (warp == 0) {
+    int w = lane < nwarps ? scratch[lane] : 0;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, w, o);
+      if (lane >= o) w += y;
+    }
+    if (lane < nwarps) scratch[lane] = w;  // inclusive warp totals
+    if (lane == 31) scratch[32] = w;
+  }
+  __syncthreads();
+  const int before = (warp > 0 ? scratch[warp - 1] : 0) + x - v;
+  *total = scratch[32];
+  __syncthreads();
+  return before;
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);

@@ -2,11 +2,13 @@
 //
 // qcc_select_topk: one CTA per score row.  Scores are mapped to
 // order-preserving 32-bit keys (-0.0 and +0.0 share a key, every NaN maps to
-// the largest key), kept in shared memory, and a 4-pass radix select
-// (8 bits per pass, 256-bin shared histogram) finds the exact key T of the
-// k-th largest score and how many elements equal to T are still needed.  A
-// single block-wide scan then emits, in ascending index order, every index
-// with key > T plus the lowest-index elements with key == T.  The result is
+// the largest key) and kept in shared memory.  A radix select finds the exact
+// key T of the k-th largest score and how many elements equal to T are still
+// needed: a 12-bit top digit, histogrammed while the row is loaded, picks one
+// bin; the keys of that bin are compacted into a small candidate list; two
+// 10-bit digits over the candidates finish T.  An output pass then emits, in
+// ascending index order, every index with key > T plus the lowest-index
+// elements with key == T.  The result is
 // sort(scores, descending, stable)[:k] sorted ascending, which is one of the
 // valid answers of torch.topk(scores, k, sorted=False) as used by
 // runtime/selector.py:24 and end_to_end/oracle_sparse_mlp.py:75, with the
@@ -29,6 +31,10 @@ namespace {
 
 constexpr int kSelectThreads = 1024;
 constexpr int kUnionThreads = 1024;
+constexpr int kDigit1Bins = 1 << 12;                       // key bits 31..20
+constexpr int kDigitBins = 1 << 10;                        // key bits 19..10, then 9..0
+constexpr int kCandidateCap = kDigit1Bins - kDigitBins;   // candidate keys that fit beside a 10-bit histogram
+constexpr int kLoadRound = 8;                              // loads in flight per thread
 
 __device__ __forceinline__ uint32_t score_key(float f) {
   uint32_t u = __float_as_uint(f);
@@ -37,149 +43,200 @@ __device__ __forceinline__ uint32_t score_key(float f) {
   return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
 
-// Exclusive block scan of one int per thread; returns the prefix, *total
-// receives the block sum.  `scratch` holds >= 33 ints.
-__device__ __forceinline__ int block_exclusive_scan(int v, int* scratch, int* total) {
-  const int lane = threadIdx.x & 31;
-  const int warp = threadIdx.x >> 5;
-  const int nwarps = blockDim.x >> 5;
-  int x = v;
+// Finds the bin holding the rem-th largest element of a histogram whose bins
+// are visited from the highest down.  Thread t holds PER consecutive bins, its
+// highest one first, so an exclusive scan in thread order counts the elements
+// in all higher bins.  Writes the bin and rem minus the elements above it.
+// Requires 1 <= rem <= total count and nbins == PER * blockDim.x.
+template <int PER>
+__device__ __forceinline__ void find_bin(const int* hist, int rem, int* scratch, int* out_bin, int* out_rem) {
+  const int top = PER * static_cast<int>(blockDim.x) - 1 - PER * static_cast<int>(threadIdx.x);
+  int c[PER];
+  int s = 0;
 #pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const int y = __shfl_up_sync(0xffffffffu, x, o);
-    if (lane >= o) x += y;
+  for (int j = 0; j < PER; ++j) {
+    c[j] = hist[top - j];
+    s += c[j];
   }
-  if (lane == 31) scratch[warp] = x;
-  __syncthreads();
-  if (warp == 0) {
-    int w = lane < nwarps ? scratch[lane] : 0;
+  int total;
+  int above = block_exclusive_scan(s, scratch, &total);
 #pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const int y = __shfl_up_sync(0xffffffffu, w, o);
-      if (lane >= o) w += y;
+  for (int j = 0; j < PER; ++j) {
+    if (above < rem && above + c[j] >= rem) {
+      *out_bin = top - j;
+      *out_rem = rem - above;
     }
-    if (lane < nwarps) scratch[lane] = w;  // inclusive warp totals
-    if (lane == 31) scratch[32] = w;
+    above += c[j];
   }
-  __syncthreads();
-  const int before = (warp > 0 ? scratch[warp - 1] : 0) + x - v;
-  *total = scratch[32];
-  __syncthreads();
-  return before;
 }
 
 __global__ void __launch_bounds__(kSelectThreads, 1)
     select_topk_kernel(const float* __restrict__ scores, int64_t ld_scores, int n, int k, int32_t* __restrict__ ids,
                        int64_t ld_ids) {
   extern __shared__ __align__(16) uint32_t keys[];
-  // Per-warp histograms, two 16-bit bin counters per word (a warp sees at most
-  // n / 32 <= 1632 keys per pass, so a counter never overflows).
-  __shared__ uint32_t whist[kSelectThreads / 32][128];
-  __shared__ int hist[256];
-  __shared__ int suffix[257];
+  // Top-digit histogram; after that digit is chosen the same space holds the
+  // candidate keys ([0, kCandidateCap)) and the 10-bit histograms after them.
+  __shared__ __align__(16) int hist[kDigit1Bins];
   __shared__ int scan_scratch[64];
-  __shared__ uint32_t s_prefix;
-  __shared__ int s_remaining;
+  __shared__ int warp_gt[32], warp_eq[32];
+  __shared__ int s_bin, s_rem, s_count;
 
-  const int row = blockIdx.x;
   const int tid = threadIdx.x;
   const int lane = tid & 31;
   const int warp = tid >> 5;
-  const int nwarps = blockDim.x >> 5;
-  const float* src = scores + row * ld_scores;
-  int32_t* out = ids + row * ld_ids;
+  const float* src = scores + blockIdx.x * ld_scores;
+  int32_t* out = ids + blockIdx.x * ld_ids;
 
-  for (int i = tid; i < n; i += blockDim.x) keys[i] = score_key(__ldg(src + i));
-  if (tid == 0) {
-    s_prefix = 0u;
-    s_remaining = k;
+  for (int i = tid; i < kDigit1Bins; i += kSelectThreads) hist[i] = 0;
+  if (tid == 0) s_count = 0;
+  __syncthreads();
+
+  // 1. Keys into shared memory, fused with the histogram of the top 12 bits.
+  //    All loads of a round are issued before any is used (one memory latency
+  //    per round); 16-byte loads when the row is 16-byte aligned.
+  const bool vec = (reinterpret_cast<uintptr_t>(src) & 15u) == 0;
+  const int n_vec = vec ? n / 4 : 0;
+  for (int base = 0; base < n_vec; base += kLoadRound * kSelectThreads) {
+    float4 v[kLoadRound];
+#pragma unroll
+    for (int u = 0; u < kLoadRound; ++u) {
+      const int i = base + u * kSelectThreads + tid;
+      v[u] = i < n_vec ? __ldg(reinterpret_cast<const float4*>(src) + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+#pragma unroll
+    for (int u = 0; u < kLoadRound; ++u) {
+      const int i = base + u * kSelectThreads + tid;
+      if (i < n_vec) {
+        const uint4 q = make_uint4(score_key(v[u].x), score_key(v[u].y), score_key(v[u].z), score_key(v[u].w));
+        reinterpret_cast<uint4*>(keys)[i] = q;
+        atomicAdd(&hist[q.x >> 20], 1);
+        atomicAdd(&hist[q.y >> 20], 1);
+        atomicAdd(&hist[q.z >> 20], 1);
+        atomicAdd(&hist[q.w >> 20], 1);
+      }
+    }
+  }
+  for (int base = 4 * n_vec; base < n; base += kLoadRound * kSelectThreads) {
+    float v[kLoadRound];
+#pragma unroll
+    for (int u = 0; u < kLoadRound; ++u) {
+      const int i = base + u * kSelectThreads + tid;
+      v[u] = i < n ? __ldg(src + i) : 0.f;
+    }
+#pragma unroll
+    for (int u = 0; u < kLoadRound; ++u) {
+      const int i = base + u * kSelectThreads + tid;
+      if (i < n) {
+        const uint32_t key = score_key(v[u]);
+        keys[i] = key;
+        atomicAdd(&hist[key >> 20], 1);
+      }
+    }
   }
   __syncthreads();
 
-  uint32_t mask = 0u;
-  for (int shift = 24; shift >= 0; shift -= 8) {
-    for (int i = tid; i < nwarps * 128; i += blockDim.x) (&whist[0][0])[i] = 0u;
-    __syncthreads();
-    const uint32_t prefix = s_prefix;
-    // Lanes of a warp that fall into the same bin are counted by one atomic
-    // (score distributions crowd the high-order bins).
-    for (int base = 0; base < n; base += blockDim.x) {
-      const int i = base + tid;
-      const uint32_t key = i < n ? keys[i] : 0u;
-      const bool hit = i < n && (key & mask) == prefix;
-      const uint32_t bin = (key >> shift) & 0xFFu;
-      const unsigned peers = __match_any_sync(0xffffffffu, hit ? bin : 0x100u);
-      if (hit && lane == __ffs(peers) - 1)
-        atomicAdd(&whist[warp][bin >> 1], static_cast<uint32_t>(__popc(peers)) << (16 * (bin & 1u)));
-    }
-    __syncthreads();
-    if (tid < 256) {
-      int c = 0;
-      for (int w = 0; w < nwarps; ++w) c += (whist[w][tid >> 1] >> (16 * (tid & 1))) & 0xFFFFu;
-      hist[tid] = c;
-    }
-    __syncthreads();
-    // Inclusive suffix sums over the 256 bins (warps 0..7, one bin per thread).
-    if (tid < 256) {
-      const int w = tid >> 5;
-      // Reverse order so that a prefix scan gives suffix sums.
-      int x = hist[255 - tid];
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const int y = __shfl_up_sync(0xffffffffu, x, o);
-        if (lane >= o) x += y;
-      }
-      if (lane == 31) scan_scratch[w] = x;
-      suffix[255 - tid] = x;  // partial: within-warp
-    }
-    __syncthreads();
-    if (tid < 256) {
-      const int w = tid >> 5;
-      int add = 0;
-      for (int q = 0; q < w; ++q) add += scan_scratch[q];
-      suffix[255 - tid] += add;  // suffix[b] = sum of hist[b..255]
-    }
-    if (tid == 0) suffix[256] = 0;
-    __syncthreads();
-    const int remaining = s_remaining;
-    if (tid < 256) {
-      const int above = suffix[tid + 1];
-      if (suffix[tid] >= remaining && above < remaining) {
-        s_prefix = prefix | (static_cast<uint32_t>(tid) << shift);
-        s_remaining = remaining - above;
-      }
-    }
-    mask |= 0xFFu << shift;
-    __syncthreads();
-  }
-  const uint32_t thr = s_prefix;
-  const int need = s_remaining;  // elements equal to thr to take, lowest index first
+  // 2. Top digit of the k-th largest key.
+  find_bin<kDigit1Bins / kSelectThreads>(hist, k, scan_scratch, &s_bin, &s_rem);
+  __syncthreads();
+  uint32_t prefix = static_cast<uint32_t>(s_bin) << 20;
+  uint32_t mask = 0xFFF00000u;
+  int rem = s_rem;
+  const int in_bin = hist[s_bin];
+  __syncthreads();  // the histogram space is reused below
 
-  // Contiguous chunk per thread, one scan for (> thr) and one for (== thr).
-  const int chunk = (n + blockDim.x - 1) / blockDim.x;
-  const int lo = min(n, tid * chunk);
-  const int hi = min(n, lo + chunk);
-  int gt = 0, eq = 0;
-  for (int i = lo; i < hi; ++i) {
-    const uint32_t key = keys[i];
-    gt += key > thr;
-    eq += key == thr;
-  }
-  int total;
-  int gt_before = block_exclusive_scan(gt, scan_scratch, &total);
-  int eq_before = block_exclusive_scan(eq, scan_scratch, &total);
-  for (int i = lo; i < hi; ++i) {
-    const uint32_t key = keys[i];
-    if (key > thr) {
-      out[gt_before + min(eq_before, need)] = i;
-      ++gt_before;
-    } else if (key == thr) {
-      if (eq_before < need) out[gt_before + eq_before] = i;
-      ++eq_before;
+  // 3. The keys of that bin become the candidates (warp-aggregated append; the
+  //    order does not matter for counting).  A bin larger than the candidate
+  //    space (heavily tied inputs) is instead filtered from all keys below.
+  uint32_t* cand = reinterpret_cast<uint32_t*>(hist);
+  int* hist2 = hist + kCandidateCap;
+  const bool compact = in_bin <= kCandidateCap;
+  if (compact) {
+    const uint32_t bin1 = prefix >> 20;
+    for (int base = 0; base < n; base += kSelectThreads) {
+      const int i = base + tid;
+      const bool take = i < n && (keys[i] >> 20) == bin1;
+      const unsigned ballot = __ballot_sync(0xffffffffu, take);
+      if (ballot != 0u) {
+        const int leader = __ffs(ballot) - 1;
+        int pos = 0;
+        if (lane == leader) pos = atomicAdd(&s_count, __popc(ballot));
+        pos = __shfl_sync(0xffffffffu, pos, leader);
+        if (take) cand[pos + __popc(ballot & ((1u << lane) - 1u))] = keys[i];
+      }
     }
+    __syncthreads();
+  }
+  const int n_src = compact ? in_bin : n;
+  const uint32_t* src_keys = compact ? cand : keys;
+
+  // 4. Two 10-bit digits over the candidates.
+  for (int shift = 10; shift >= 0; shift -= 10) {
+    for (int i = tid; i < kDigitBins; i += kSelectThreads) hist2[i] = 0;
+    __syncthreads();
+    for (int i = tid; i < n_src; i += kSelectThreads) {
+      const uint32_t key = src_keys[i];
+      if ((key & mask) == prefix) atomicAdd(&hist2[(key >> shift) & (kDigitBins - 1)], 1);
+    }
+    __syncthreads();
+    find_bin<kDigitBins / kSelectThreads>(hist2, rem, scan_scratch, &s_bin, &s_rem);
+    __syncthreads();
+    prefix |= static_cast<uint32_t>(s_bin) << shift;
+    mask |= static_cast<uint32_t>(kDigitBins - 1) << shift;
+    rem = s_rem;
+    __syncthreads();
+  }
+  const uint32_t thr = prefix;  // key of the k-th largest score
+  const int need = rem;         // elements equal to thr to take, lowest index first
+
+  // 5. Output in ascending index order.  Warp w owns a contiguous segment;
+  //    lanes read consecutive keys and ballots give each element its rank.
+  const int seg = ((n + 31) / 32 + 31) / 32 * 32;
+  const int seg_lo = min(n, warp * seg);
+  const int seg_hi = min(n, seg_lo + seg);
+  int gt = 0, eq = 0;
+  for (int base = seg_lo; base < seg_hi; base += 32) {
+    const int i = base + lane;
+    const uint32_t key = i < seg_hi ? keys[i] : 0u;
+    gt += __popc(__ballot_sync(0xffffffffu, i < seg_hi && key > thr));
+    eq += __popc(__ballot_sync(0xffffffffu, i < seg_hi && key == thr));
+  }
+  if (lane == 0) {
+    warp_gt[warp] = gt;
+    warp_eq[warp] = eq;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    int g = warp_gt[lane], e = warp_eq[lane];
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int yg = __shfl_up_sync(0xffffffffu, g, o);
+      const int ye = __shfl_up_sync(0xffffffffu, e, o);
+      if (lane >= o) {
+        g += yg;
+        e += ye;
+      }
+    }
+    warp_gt[lane] = g - warp_gt[lane];  // exclusive
+    warp_eq[lane] = e - warp_eq[lane];
+  }
+  __syncthreads();
+  int run_gt = warp_gt[warp], run_eq = warp_eq[warp];
+  const unsigned lt = (1u << lane) - 1u;
+  for (int base = seg_lo; base < seg_hi; base += 32) {
+    const int i = base + lane;
+    const uint32_t key = i < seg_hi ? keys[i] : 0u;
+    const bool is_gt = i < seg_hi && key > thr;
+    const bool is_eq = i < seg_hi && key == thr;
+    const unsigned b_gt = __ballot_sync(0xffffffffu, is_gt);
+    const unsigned b_eq = __ballot_sync(0xffffffffu, is_eq);
+    const int gt_before = run_gt + __popc(b_gt & lt);
+    const int eq_before = run_eq + __popc(b_eq & lt);
+    if (is_gt) out[gt_before + min(eq_before, need)] = i;
+    else if (is_eq && eq_before < need) out[gt_before + eq_before] = i;
+    run_gt += __popc(b_gt);
+    run_eq += __popc(b_eq);
   }
 }
-
 __global__ void __launch_bounds__(kUnionThreads, 1)
     build_union_kernel(const int32_t* __restrict__ ids, int64_t ld_ids, int batch, int k, int32_t id_begin,
                        int32_t id_end, int32_t* __restrict__ union_ids, uint8_t* __restrict__ token_mask,

@@ -34,35 +34,6 @@ constexpr int kResolveThreads = 1024;
 constexpr int kMaxCapacity = 8192;
 constexpr unsigned long long kActiveKey = ~0ull;
 
-__device__ __forceinline__ int block_scan_exclusive(int v, int* scratch, int* total) {
-  const int lane = threadIdx.x & 31;
-  const int warp = threadIdx.x >> 5;
-  const int nwarps = blockDim.x >> 5;
-  int x = v;
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const int y = __shfl_up_sync(0xffffffffu, x, o);
-    if (lane >= o) x += y;
-  }
-  if (lane == 31) scratch[warp] = x;
-  __syncthreads();
-  if (warp == 0) {
-    int w = lane < nwarps ? scratch[lane] : 0;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const int y = __shfl_up_sync(0xffffffffu, w, o);
-      if (lane >= o) w += y;
-    }
-    if (lane < nwarps) scratch[lane] = w;
-    if (lane == 31) scratch[32] = w;
-  }
-  __syncthreads();
-  const int before = (warp > 0 ? scratch[warp - 1] : 0) + x - v;
-  *total = scratch[32];
-  __syncthreads();
-  return before;
-}
-
 // counts_out: [0] resident, [1] misses served, [2] cache hits, [3] evicted,
 //             [4] hot hits, [5] 1 if misses exceeded the free slots
 __global__ void __launch_bounds__(kResolveThreads, 1)
@@ -110,8 +81,8 @@ __global__ void __launch_bounds__(kResolveThreads, 1)
   if (hits) atomicAdd(&s_cnt[0], hits);
   if (hot) atomicAdd(&s_cnt[1], hot);
   int total_res, total_miss;
-  int res_pos = block_scan_exclusive(n_res, scratch, &total_res);
-  int miss_pos = block_scan_exclusive(n_miss, scratch, &total_miss);
+  int res_pos = block_exclusive_scan(n_res, scratch, &total_res);
+  int miss_pos = block_exclusive_scan(n_miss, scratch, &total_miss);
   for (int i = lo; i < hi; ++i) {
     const int32_t id = ids[i];
     const int32_t s = (id >= 0 && id < n_records) ? slot_of[id] : -2;

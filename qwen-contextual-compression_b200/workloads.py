@@ -154,3 +154,58 @@ def offload_token_ids(intermediate: int, k: int, hot: torch.Tensor, tokens: int,
         out.append(ids.to(torch.int32))
         prev = ids.long()
     return out
+
+
+PREFILL_TOKENS = 512
+PREFILL_TILE = 128
+PREFILL_BLOCK = 64
+
+
+def prefill_tile_blocks(intermediate: int = DECODE_INTERMEDIATE, tokens: int = PREFILL_TOKENS, density: float = 0.3,
+                        hot_fraction: float = 0.2, seed: int = 21) -> tuple[torch.Tensor, list[torch.Tensor]]:
+    """Block selections of a block-sparse prefill: (hot block ids, per-tile sorted block ids).
+
+    Records form blocks of 64.  A seeded ``hot_fraction`` of the blocks is on
+    for every 128-token tile; every other block is on per tile with
+    probability p chosen so that the expected fraction of blocks per tile is
+    ``density`` (p = (density * blocks - hot) / (blocks - hot)).
+    """
+    n_blocks = (intermediate + PREFILL_BLOCK - 1) // PREFILL_BLOCK
+    n_tiles = (tokens + PREFILL_TILE - 1) // PREFILL_TILE
+    gen = torch.Generator().manual_seed(seed)
+    n_hot = int(round(hot_fraction * n_blocks))
+    order = torch.randperm(n_blocks, generator=gen)
+    hot = order[:n_hot].sort().values
+    cold = order[n_hot:]
+    p = max(0.0, (density * n_blocks - n_hot) / max(1, n_blocks - n_hot))
+    tiles = []
+    for _ in range(n_tiles):
+        on = torch.rand(cold.numel(), generator=gen) < p
+        tiles.append(torch.cat([hot, cold[on]]).sort().values.to(torch.int32))
+    return hot, tiles
+
+
+def prefill_x(tokens: int = PREFILL_TOKENS, hidden: int = DECODE_HIDDEN, dtype: torch.dtype = torch.bfloat16,
+              seed: int = 22, device: str | torch.device = "cpu") -> torch.Tensor:
+    """x ~ N(0, 1) of a prefill, [tokens, hidden]."""
+    gen = torch.Generator().manual_seed(seed)
+    return torch.randn(tokens, hidden, generator=gen).to(dtype).to(device)
+
+
+def prefill_flops(tile_blocks: list[torch.Tensor], hidden: int = DECODE_HIDDEN, intermediate: int | None = None,
+                  tile: int = PREFILL_TILE) -> int:
+    """Algorithmic FLOPs: per tile 2 * 128 * 3 * hidden * (records of its blocks)."""
+    total = 0
+    for blocks in tile_blocks:
+        records = blocks.numel() * PREFILL_BLOCK
+        if intermediate is not None and blocks.numel() and int(blocks.max()) == (intermediate - 1) // PREFILL_BLOCK:
+            records -= (int(blocks.max()) + 1) * PREFILL_BLOCK - intermediate
+        total += 2 * tile * 3 * hidden * records
+    return total
+
+
+def prefill_unique_bytes(tile_blocks: list[torch.Tensor], hidden: int = DECODE_HIDDEN, tokens: int = PREFILL_TOKENS,
+                         esize: int = 2) -> int:
+    """Bytes a block-major prefill must move: each used block once, plus x and y."""
+    used = torch.unique(torch.cat([b.to(torch.int64) for b in tile_blocks])).numel()
+    return used * PREFILL_BLOCK * 3 * hidden * esize + 2 * tokens * hidden * esize
