@@ -52,6 +52,7 @@ import qcc_b200.workloads as workloads  # noqa: E402
 METRIC = "indexed sparse-FFN µs/layer & achieved HBM GB/s (bs=1, K/N=0.25, bf16) at 1–8 GPUs"
 HIDDEN, INTERMEDIATE, RETENTION = workloads.DECODE_HIDDEN, workloads.DECODE_INTERMEDIATE, 0.25
 FALLBACK_HBM_GBS = 6650.0
+FALLBACK_BF16_TFLOPS = 1590.0
 LAYERS = 4  # independently drawn layers the steps cycle through
 
 
@@ -68,6 +69,7 @@ def parse_args():
     p.add_argument("--no-selector", action="store_true", help="skip the selector + fused FFN measurement")
     p.add_argument("--no-offload", action="store_true", help="skip the 8-layer host-offload measurement")
     p.add_argument("--offload-tokens", type=int, default=12)
+    p.add_argument("--no-prefill", action="store_true", help="skip the block-sparse prefill measurement")
     return p.parse_args()
 
 
@@ -260,6 +262,75 @@ def measure_selector(engine, x, device, stream, side) -> dict:
     union, _, count = build_union(select_topk(scores8[0], k), 0, INTERMEDIATE)
     out["union_records_batch8"] = int(count.item())
     return out
+
+
+def measure_prefill(device, stream, side, cpu_seconds: float) -> dict:
+    """Block-sparse prefill: 512 tokens in four 128-token tiles, hidden 5120, N 17408, bf16.
+
+    Records form 272 blocks of 64; a seeded 20 % of the blocks is on for every
+    tile, every other block per tile with the probability that makes 30 % of
+    the blocks on per tile.  Steps alternate between two independently drawn
+    layers (1.07 GB of records) in one CUDA graph.  Roofline: tensor-core
+    FLOPs (2 * 128 * 3 * H per selected record per tile) against the measured
+    bf16 GEMM peak; the unique record bytes are reported beside it.
+    """
+    from qcc_b200.runtime.packing import PackedFFNWeights
+    from qcc_b200.runtime.prefill import BlockSparsePrefill, tile_block_lists
+
+    layers = [workloads.decode_layer(device=device, seed=300 + s) for s in range(2)]
+    engines = [BlockSparsePrefill(PackedFFNWeights(l.packed, HIDDEN, INTERMEDIATE)) for l in layers]
+    x = workloads.prefill_x(device=device)
+    _, tiles = workloads.prefill_tile_blocks()
+    flat, offsets = tile_block_lists(tiles, device)
+    y = torch.empty_like(x)
+    steps = 20
+    us = graph_time_us(lambda i: engines[i % 2](x, (flat, offsets), out=y), steps, stream, side)
+    flops = workloads.prefill_flops(tiles)
+    unique = workloads.prefill_unique_bytes(tiles)
+    peaks = measured_peaks()
+    peak = peaks.get("bf16_tflops")
+    peak_src = "measured" if peak else "fallback"
+    peak = float(peak or FALLBACK_BF16_TFLOPS)
+    achieved = flops / (us * 1e-6) / 1e12
+    out = {"tokens": workloads.PREFILL_TOKENS, "tiles": len(tiles), "blocks_per_tile": [t.numel() for t in tiles],
+           "block_records": workloads.PREFILL_BLOCK, "us": round(us, 2), "tflops": round(achieved, 1),
+           "tokens_per_s": round(workloads.PREFILL_TOKENS / (us * 1e-6), 1),
+           "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
+                        "frac": round(achieved / peak, 4), "peak_source": peak_src, "flops": flops,
+                        "unique_record_bytes": unique,
+                        "hbm_gbs_of_unique_bytes": round(unique / (us * 1e-6) / 1e9, 1)},
+           "gpu_launches_per_step": 4}
+    del engines, layers
+    torch.cuda.empty_cache()
+    if cpu_seconds > 0:
+        out["cpu_baseline"] = prefill_cpu_sample(tiles, cpu_seconds)
+    return out
+
+
+def prefill_cpu_sample(tiles, seconds: float) -> dict:
+    """The reference's per-tile path on the host: TorchDynamicSparseFFN on the expanded ids of a tile."""
+    from oracle import ffn as offn  # CPU baseline leg only
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    layer = workloads.decode_layer(device="cpu", seed=300)
+    gate, up = layer.gate().contiguous(), layer.up().contiguous()
+    down = layer.down().contiguous()
+    x = workloads.prefill_x()
+    times = []
+    start = time.perf_counter()
+    with torch.inference_mode():
+        for t, blocks in enumerate(tiles):
+            ids = (blocks.long()[:, None] * workloads.PREFILL_BLOCK + torch.arange(workloads.PREFILL_BLOCK)).flatten()
+            t0 = time.perf_counter()
+            offn.dynamic_sparse_ffn(x[t * 128:(t + 1) * 128], ids, gate, up, down)
+            times.append(time.perf_counter() - t0)
+            if time.perf_counter() - start > seconds:
+                break
+    per_tile = statistics.median(times)
+    return {"value": round(per_tile * len(tiles) * 1e6, 1), "unit": "us per 512-token prefill", "cores": threads,
+            "kind": "port", "sample": f"{len(times)} of {len(tiles)} tiles (128 tokens each), median tile time x "
+                                      f"{len(tiles)}, {threads} threads"}
 
 
 def measure_offload(device, tokens: int) -> dict:
@@ -527,6 +598,9 @@ def run_ours(args) -> None:
     offload = None
     if not args.no_offload and world == 1:
         offload = measure_offload(device, args.offload_tokens)
+    prefill = None
+    if not args.no_prefill and world == 1:
+        prefill = measure_prefill(device, stream, side, 0.0 if args.no_cpu_baseline else 10.0)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -581,6 +655,8 @@ def run_ours(args) -> None:
         line["selector_ffn"] = selector
     if offload is not None:
         line["offload"] = offload
+    if prefill is not None:
+        line["prefill"] = prefill
     if cpu is not None:
         line["cpu_baseline"] = {"value": round(cpu["gbs"], 4), "unit": "GB/s", "cores": cpu["threads"],
                                 "kind": "port", "us_per_layer": round(cpu["seconds_median"] * 1e6, 1),

@@ -7,26 +7,30 @@
 // The reference computes each tile with runtime/ffn.py:20-39 on the expanded
 // ids (three gathers and three GEMMs per tile).
 //
-// A call runs groups of up to four tiles (512 tokens); each group is four
-// launches:
-//  plan      one CTA: per-block tile masks from the per-tile block lists, the
-//            gate/up work units (a block with one or two of its tiles) and the
-//            union of blocks with their masks.
-//  gate/up   persistent; per unit A[tok, 64b .. 64b+63] = silu(X G_b^T) * (X U_b^T)
-//            for the unit's tiles: M = 128 tokens, N = 128 (64 gate + 64 up
-//            records), K = hidden in 64-wide chunks.  A block used by three or
-//            four tiles is two units that run side by side, so the second
-//            read of its gate/up rows usually hits L2.
-//  down      y^T[h, tok] = sum over blocks of D_b[h, n] A[tok, n]: M = 128 hidden
-//            rows of one chunk, N = 128 tokens of a tile, K = 64 records of a
-//            block.  The accumulators of all four tiles live in TMEM (512
-//            columns).  The union is split S ways per hidden chunk so that the
-//            grid fills the GPU; each CTA writes an fp32 partial.
-//  reduce    sums the S partials in a fixed order and writes y (only when S > 1).
+// A call runs groups of up to four tiles (512 tokens); a group is two launches:
+//  plan     one CTA: per-block tile masks from the per-tile block lists; the
+//           gate/up work units (a block with one or two of its tiles) with the
+//           prefix of their costs; each tile's ascending block list.
+//  prefill  one persistent CTA per SM (cooperative launch), two phases split by
+//           a grid barrier:
+//   1. gate/up: per unit, A[tok, 64b .. 64b+63] = silu(X G_b^T) * (X U_b^T) for
+//      the unit's tiles: M = 128 tokens, N = 128 (64 gate + 64 up records),
+//      K = hidden in chunks of 64.
+//   2. down: per unit (tile t, 256 hidden outputs), y = A[tile, blocks] D[blocks, h]:
+//      M = 128 tokens, N = 256, K = 64 records per block of the tile.
+//  Both phases are balanced stream-K style: the cost-weighted sequence of
+//  (unit, K step) iterations is cut into one contiguous range per CTA, so a
+//  unit may be split between consecutive CTAs.  The CTA that runs a unit's
+//  first K step finishes it: a CTA whose range starts inside a unit writes its
+//  fp32 accumulators to its slot and raises a flag; the finishing CTA, which
+//  reaches the unit at the end of its own range, adds them before the
+//  activation (phase 1) or the output (phase 2).
 //
 // Operands move by tiled TMA (128-byte swizzle, no multicast) through a 4-stage
-// shared-memory ring; one thread issues the loads, one thread issues the
-// MMAs, four warps read TMEM.  Every wait is bounded (2 s) and reports
+// shared-memory ring; one thread loads the weight boxes and one the
+// activation boxes (both arrive on the stage's barrier), one thread issues the
+// MMAs, four warps read TMEM (two 256-column accumulator buffers, so the
+// epilogue of one unit overlaps the MMAs of the next).  Every wait is bounded (2 s) and reports
 // QCC_DEV_TIMEOUT through the workspace status word.
 
 #include <cuda.h>
@@ -34,6 +38,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cstddef>
 #include <mutex>
 
 #include "qcc_common.cuh"
@@ -44,38 +49,92 @@ namespace qcc {
 
 namespace {
 
-constexpr int kTile = 128;                // tokens per tile
+constexpr int kTile = 128;                // tokens per tile (MMA M)
 constexpr int kBlock = 64;                // records per block
-constexpr int kChunk = 64;                // hidden elements per K chunk (one 128-byte swizzled row)
-constexpr int kMaxTiles = 4;              // tiles per group: 4 x 128 TMEM columns
+constexpr int kChunk = 64;                // hidden elements per gate/up K step (one 128-byte swizzled row)
+constexpr int kHRange = 256;              // hidden outputs per down unit (MMA N)
+constexpr int kMaxTiles = 4;
 constexpr int kGroupTokens = kTile * kMaxTiles;
-constexpr int kHChunk = 128;              // hidden rows per down-projection CTA
-constexpr int kMaxSplits = 4;
 constexpr int kStages = 4;
-constexpr int kThreads = 192;             // warp 0: TMA, warp 1: MMA, warps 2-5: TMEM readers
+constexpr int kThreads = 224;             // warp 0: weight TMA, warp 1: MMA, warps 2-5: TMEM readers, warp 6: activation TMA
+constexpr int kActWarp = 6;               // issues the x / activation boxes (one thread issues ~5 M TMA copies/s)
+constexpr int kFirstReader = 2, kReaders = 4;  // warps 2-5 read TMEM (warp w: lanes 32*(w%4) .. +31)
 constexpr int kPlanThreads = 1024;
-constexpr uint32_t kHalfBox = 64 * 128;   // [64 rows x 64 elements] of 16-bit: 8 KB
-constexpr uint32_t kTileBox = 128 * 128;  // [128 rows x 64 elements]: 16 KB
-constexpr uint32_t kStageBytes = 2 * kHalfBox + 2 * kTileBox;  // 48 KB
-constexpr uint32_t kSmemBytes = kStages * kStageBytes + 256 + 1024;  // + barriers + alignment slack
+constexpr uint32_t kBox64 = 64 * 128;     // [64 rows x 64 elements] of 16-bit: 8 KB
+constexpr uint32_t kBox128 = 128 * 128;   // [128 rows x 64 elements]: 16 KB
+constexpr uint32_t kStageBytes = 48 * 1024;
+constexpr int kSmemList = 2048;           // down steps staged in shared memory
+constexpr int kPlanUnits = 4096;          // gate/up units the plan kernel keeps in shared memory
+constexpr uint32_t kControlBytes = 12 * 1024;
+constexpr uint32_t kSmemBytes = kStages * kStageBytes + kControlBytes + 1024;  // + alignment slack
 constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kAccCols = 256;        // one accumulator buffer
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
-constexpr int kMaxBlocks = 1 << 16;       // byte map of the plan kernel in shared memory
+constexpr int kMaxBlocks = 1 << 16;
+constexpr int kMaxDownUnits = 512;        // tiles x 256-wide hidden ranges (hidden <= 32768)
+constexpr size_t kSlotFloats = 128 * 256; // one CTA's partial accumulators
+constexpr int kMaxContrib = 16;           // CTAs that may hand partial sums to one unit's finishing CTA
+constexpr int kSplitTarget = 8;           // ranges are at least 1/8 of the largest unit's cost
 
 // Workspace header (int32 words).
 constexpr int kHdrStatus = 0;
 constexpr int kHdrUnits = 1;
-constexpr int kHdrUnion = 2;
+constexpr int kHdrCost = 2;               // total gate/up cost
+constexpr int kHdrEpoch = 3;              // incremented by every plan launch
+constexpr int kHdrArrive = 4;             // grid-barrier counter, reset by every plan launch
+constexpr int kHdrTileCount = 8;          // [kMaxTiles] blocks per tile
 constexpr size_t kHeaderBytes = 256;
 
-struct Barriers {
+// Stream-K ranges of one CTA for both phases (index 0: gate/up, 1: down),
+// [(lo_u, lo_k), (hi_u, hi_k)), and the CTAs that hand partial sums to the
+// unit this CTA finishes last.  Written by the plan kernel.
+struct alignas(16) Ranges {
+  int lo_u[2], lo_k[2], hi_u[2], hi_k[2];
+  int n_contrib[2];
+  int contrib[2][kMaxContrib];
+  int pad[2];
+};
+static_assert(sizeof(Ranges) % 16 == 0, "ranges record");
+
+struct Control {
   uint64_t full[kStages];
   uint64_t empty[kStages];
   uint64_t acc_full[2];
   uint64_t acc_empty[2];
   uint64_t drain;
+  uint64_t steps_ready;    // the down-step list below is filled
   uint32_t tmem_base;
   int abort;
+  int epoch;
+  Ranges r;
+  int steps[kSmemList];    // (down unit << 16) | block of each of this CTA's down steps, in order
+  int n_steps;             // down steps of this CTA (entries of `steps` valid: min(n_steps, kSmemList))
+};
+static_assert(sizeof(Control) <= kControlBytes, "control block");
+static_assert(offsetof(Control, r) % 16 == 0, "the ranges record is copied with 16-byte accesses");
+static_assert(kActWarp >= kFirstReader + kReaders && kActWarp * 32 < kThreads, "warp roles");
+
+struct PrefillArgs {
+  int32_t* header;
+  const int32_t* units;
+  const int32_t* unit_prefix;  // [n_units + 1] exclusive cost prefix
+  const int32_t* tile_list;    // [kMaxTiles][n_blocks]
+  const Ranges* ranges;        // [gridDim.x]
+  int n_blocks;
+  int n_chunks;                // gate/up K steps
+  int n_hranges;               // down units per tile
+  int hidden;
+  int n_tokens;                // rows of this group
+  int n_tiles;
+  uint16_t* abuf;
+  int64_t ld_abuf;
+  float* partials;             // [gridDim.x][kSlotFloats]
+  int32_t* flags1;             // [gridDim.x]
+  int32_t* flags2;             // [gridDim.x]
+  void* y;
+  int64_t ldy;
+  int y_dtype;
+  int y_vec;                   // 16-byte stores allowed
 };
 
 __device__ __forceinline__ uint8_t* align_1024(uint8_t* p) {
@@ -99,7 +158,6 @@ __device__ __forceinline__ bool wait_phase(uint64_t* bar, uint32_t parity, volat
   }
 }
 
-// The same wait for a whole warp: lane 0 polls, every lane gets the result.
 __device__ __forceinline__ bool warp_wait_phase(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
                                                 int* status) {
   int ok = 0;
@@ -107,12 +165,46 @@ __device__ __forceinline__ bool warp_wait_phase(uint64_t* bar, uint32_t parity, 
   return __shfl_sync(0xffffffffu, ok, 0) != 0;
 }
 
-// Waits, without regard to an abort, for the loads of the last issued stages
-// so that no copy is still writing shared memory when the CTA exits.
-__device__ __forceinline__ void drain_loads(Barriers* bars, uint32_t issued) {
-  const uint32_t first = issued > static_cast<uint32_t>(kStages) ? issued - kStages : 0u;
-  for (uint32_t i = first; i < issued; ++i) mbar_wait_bounded(&bars->full[i % kStages], (i / kStages) & 1u, kWaitLimitNs);
+__device__ __forceinline__ int ld_acquire(const int32_t* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
 }
+
+// Lane 0 of the warp waits (bounded) until flags[list[i]] == epoch for every
+// i < n; all lanes get the result.
+__device__ __forceinline__ bool warp_wait_flags(const int32_t* flags, const int* list, int n, int epoch,
+                                                volatile int* abort_flag, int* status) {
+  int ok = 1;
+  if ((threadIdx.x & 31) == 0) {
+    const uint64_t start = global_timer_ns();
+    for (int i = 0; i < n && ok; ++i) {
+      while (ld_acquire(flags + list[i]) != epoch) {
+        if (*abort_flag || global_timer_ns() - start > kWaitLimitNs) {
+          if (!*abort_flag) atomicOr(status, QCC_DEV_TIMEOUT);
+          *abort_flag = 1;
+          ok = 0;
+          break;
+        }
+      }
+    }
+  }
+  ok = __shfl_sync(0xffffffffu, ok, 0);
+  __syncwarp();
+  return ok != 0;
+}
+
+__device__ __forceinline__ void drain_loads(Control* ctl, uint32_t issued) {
+  const uint32_t first = issued > static_cast<uint32_t>(kStages) ? issued - kStages : 0u;
+  for (uint32_t i = first; i < issued; ++i) mbar_wait_bounded(&ctl->full[i % kStages], (i / kStages) & 1u, kWaitLimitNs);
+}
+
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
+// Named barrier of the four TMEM-reading warps.
+__device__ __forceinline__ void epilogue_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 
 __device__ __forceinline__ float silu(float g) { return __fdividef(g, 1.f + __expf(-g)); }
 
@@ -127,17 +219,115 @@ __device__ __forceinline__ uint32_t pack2(float a, float b) {
   }
 }
 
-// Unit word: block << 8 | first tile << 4 | second tile (0xF: none).
-// Union word: block << 8 | tile mask.
+__device__ __forceinline__ int unit_tiles(int unit) { return (unit & 0xF) == 0xF ? 1 : 2; }
+
+// ---------------------------------------------------------------------------
+// Stream-K ranges.
+// ---------------------------------------------------------------------------
+
+// Phase 1: (unit, chunk) at cost position p.  A chunk of a unit costs its
+// tiles + 1 (one 16 KB box of x per tile plus 16 KB of gate/up rows).
+__device__ void locate_gate_up(const int* units, const int* prefix, int n_units, int total, int64_t p, int* u,
+                               int* k) {
+  if (p >= total || n_units == 0) {
+    *u = n_units;
+    *k = 0;
+    return;
+  }
+  int lo = 0, hi = n_units - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) / 2;
+    if (prefix[mid] <= p)
+      lo = mid;
+    else
+      hi = mid - 1;
+  }
+  *u = lo;
+  *k = static_cast<int>((p - prefix[lo]) / (unit_tiles(units[lo]) + 1));
+}
+
+// Phase 2: (unit, step) at position p; units without steps share their
+// prefix with the next unit, and the search lands on the one with steps.
+__device__ void locate_down(const int* prefix, int n_units, int64_t p, int* u, int* k) {
+  const int total = prefix[n_units];
+  if (p >= total || n_units == 0) {
+    *u = n_units;
+    *k = 0;
+    return;
+  }
+  int lo = 0, hi = n_units - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) / 2;
+    if (prefix[mid] <= p)
+      lo = mid;
+    else
+      hi = mid - 1;
+  }
+  *u = lo;
+  *k = static_cast<int>(p - prefix[lo]);
+}
+
+// Number of ranges actually used: at most the grid, and few enough that a
+// range covers at least 1/kSplitTarget of the costliest unit (so no unit is
+// shared by more than about kSplitTarget + 1 CTAs).
+__device__ __forceinline__ int effective_ranges(int64_t total, int64_t unit_max, int grid) {
+  if (total <= 0 || unit_max <= 0) return 1;
+  int64_t cap = total * kSplitTarget / unit_max;
+  if (cap > grid) cap = grid;
+  return cap < 1 ? 1 : static_cast<int>(cap);
+}
+
+// Range of CTA i out of g and the CTAs with non-empty ranges that hand partial
+// sums to its last unit.  Returns false if that needs more than kMaxContrib.
+template <typename Bound>
+__device__ bool range_of(int i, int g, Bound bound, Ranges* r, int ph) {
+  r->n_contrib[ph] = 0;
+  if (i >= g) {
+    bound(g, &r->lo_u[ph], &r->lo_k[ph]);
+    r->hi_u[ph] = r->lo_u[ph];
+    r->hi_k[ph] = r->lo_k[ph];
+    return true;
+  }
+  bound(i, &r->lo_u[ph], &r->lo_k[ph]);
+  bound(i + 1, &r->hi_u[ph], &r->hi_k[ph]);
+  const int hi_u = r->hi_u[ph], hi_k = r->hi_k[ph];
+  if (hi_k == 0 || (hi_u == r->lo_u[ph] && r->lo_k[ph] > 0)) return true;  // last segment complete or not a head
+  int u1 = hi_u, k1 = hi_k;  // start of range j
+  for (int j = i + 1; j < g; ++j) {
+    const int u = u1, k = k1;
+    if (u != hi_u || k == 0) break;
+    bound(j + 1, &u1, &k1);
+    if (u1 == u && k1 == k) continue;  // empty range
+    if (r->n_contrib[ph] == kMaxContrib) return false;
+    r->contrib[ph][r->n_contrib[ph]++] = j;
+  }
+  return true;
+}
+
+// ---------------------------------------------------------------------------
+// Plan.  Unit word: block << 8 | first tile << 4 | second tile (0xF: none).
+// One CTA: per-block tile masks, the gate/up units and their cost prefix,
+// each tile's ascending block list, then the stream-K ranges of every CTA
+// of the prefill grid (one thread per CTA).
+// ---------------------------------------------------------------------------
+
 __global__ void __launch_bounds__(kPlanThreads)
     prefill_plan_kernel(const int32_t* __restrict__ tile_blocks, const int32_t* __restrict__ tile_offsets,
-                        int n_tiles, int n_blocks, int32_t* __restrict__ header, int32_t* __restrict__ units,
-                        int32_t* __restrict__ unions) {
-  extern __shared__ __align__(16) uint32_t words[];  // one mask byte per block
+                        int n_tiles, int n_blocks, int n_chunks, int n_hranges, int grid, int32_t* __restrict__ header,
+                        int32_t* __restrict__ units, int32_t* __restrict__ unit_prefix,
+                        int32_t* __restrict__ tile_list, Ranges* __restrict__ ranges) {
+  extern __shared__ __align__(16) uint32_t words[];  // one mask byte per block, then the staged units / prefix
   __shared__ int scratch[64];
+  __shared__ int s_down[kMaxDownUnits + 1];
+  __shared__ int s_tile_count[kMaxTiles];
+  __shared__ int s_fail;
   const int tid = threadIdx.x;
   const int n_words = (n_blocks + 3) / 4;
+  const int cap = min(2 * n_blocks, kPlanUnits);
+  int* s_units = reinterpret_cast<int*>(words + n_words);
+  int* s_prefix = s_units + cap;
   for (int i = tid; i < n_words; i += blockDim.x) words[i] = 0u;
+  if (tid == 0) s_fail = 0;
   __syncthreads();
   bool bad = false;
   for (int t = 0; t < n_tiles; ++t) {
@@ -161,332 +351,543 @@ __global__ void __launch_bounds__(kPlanThreads)
   const int chunk = (n_blocks + blockDim.x - 1) / blockDim.x;
   const int lo = min(n_blocks, tid * chunk);
   const int hi = min(n_blocks, lo + chunk);
-  int n_union = 0, n_units = 0;
+  int n_units = 0, cost = 0;
   for (int i = lo; i < hi; ++i) {
-    const int m = mask[i];
-    if (m != 0) {
-      ++n_union;
-      n_units += (__popc(m) + 1) / 2;
-    }
+    const int c = __popc(mask[i]);
+    n_units += (c + 1) / 2;
+    cost += c + (c + 1) / 2;  // per unit: tiles + 1
   }
-  int total_union, total_units;
-  int pos_union = block_exclusive_scan(n_union, scratch, &total_union);
-  int pos_units = block_exclusive_scan(n_units, scratch, &total_units);
+  int total_units, total_cost;
+  int pos = block_exclusive_scan(n_units, scratch, &total_units);
+  int run = block_exclusive_scan(cost, scratch, &total_cost) * n_chunks;
   for (int i = lo; i < hi; ++i) {
     const int m = mask[i];
-    if (m == 0) continue;
-    unions[pos_union++] = (i << 8) | m;
     int tl[kMaxTiles];
     int c = 0;
 #pragma unroll
     for (int t = 0; t < kMaxTiles; ++t)
       if ((m >> t) & 1) tl[c++] = t;
-    for (int p = 0; p < c; p += 2) units[pos_units++] = (i << 8) | (tl[p] << 4) | (p + 1 < c ? tl[p + 1] : 0xF);
+    for (int p = 0; p < c; p += 2) {
+      const bool two = p + 1 < c;
+      const int word = (i << 8) | (tl[p] << 4) | (two ? tl[p + 1] : 0xF);
+      units[pos] = word;
+      unit_prefix[pos] = run;
+      if (pos < cap) {
+        s_units[pos] = word;
+        s_prefix[pos] = run;
+      }
+      run += (two ? 3 : 2) * n_chunks;
+      ++pos;
+    }
   }
+  // Each tile's blocks in ascending order.
+  for (int t = 0; t < n_tiles; ++t) {
+    int cnt = 0;
+    for (int i = lo; i < hi; ++i) cnt += (mask[i] >> t) & 1;
+    int total;
+    int p = block_exclusive_scan(cnt, scratch, &total);
+    for (int i = lo; i < hi; ++i)
+      if ((mask[i] >> t) & 1) tile_list[t * n_blocks + p++] = i;
+    if (tid == 0) s_tile_count[t] = total;
+  }
+  const int total1 = total_cost * n_chunks;
   if (tid == 0) {
+    for (int t = 0; t < kMaxTiles; ++t) header[kHdrTileCount + t] = t < n_tiles ? s_tile_count[t] : 0;
     header[kHdrUnits] = total_units;
-    header[kHdrUnion] = total_union;
+    header[kHdrCost] = total1;
+    unit_prefix[total_units] = total1;
+    if (total_units < cap) s_prefix[total_units] = total1;
+    header[kHdrEpoch] = header[kHdrEpoch] + 1;
+    header[kHdrArrive] = 0;
+    // Down units: v = range * n_tiles + tile, steps = blocks of the tile.
+    int r = 0;
+    for (int v = 0; v < n_hranges * n_tiles; ++v) {
+      s_down[v] = r;
+      r += s_tile_count[v % n_tiles];
+    }
+    s_down[n_hranges * n_tiles] = r;
   }
+  __syncthreads();
+  // Ranges of every CTA of the prefill grid.
+  const bool staged = total_units < cap;
+  const int* u_arr = staged ? s_units : units;
+  const int* p_arr = staged ? s_prefix : unit_prefix;
+  const int g1 = effective_ranges(total1, 3ll * n_chunks, grid);
+  const int n_down = n_hranges * n_tiles;
+  const int total2 = s_down[n_down];
+  int max_steps = 0;
+  for (int t = 0; t < n_tiles; ++t) max_steps = max(max_steps, s_tile_count[t]);
+  const int g2 = effective_ranges(total2, max_steps, grid);
+  for (int i = tid; i < grid; i += blockDim.x) {
+    Ranges r;
+    auto bound1 = [&](int j, int* u, int* k) {
+      locate_gate_up(u_arr, p_arr, total_units, total1, static_cast<int64_t>(j) * total1 / g1, u, k);
+    };
+    auto bound2 = [&](int j, int* u, int* k) {
+      locate_down(s_down, n_down, static_cast<int64_t>(j) * total2 / g2, u, k);
+    };
+    const bool ok = range_of(i, g1, bound1, &r, 0) & range_of(i, g2, bound2, &r, 1);
+    if (!ok) s_fail = 1;
+    r.pad[0] = r.pad[1] = 0;
+    ranges[i] = r;
+  }
+  __syncthreads();
+  if (tid == 0 && s_fail) atomicOr(header + kHdrStatus, QCC_DEV_TIMEOUT);
 }
 
-// Common prologue of the tensor-core kernels: barriers, TMEM allocation.
-__device__ __forceinline__ Barriers* setup(uint8_t* smem) {
-  Barriers* bars = reinterpret_cast<Barriers*>(smem + kStages * kStageBytes);
+// idx-th unit of a CTA's range in processing order, or -1 past the end: a
+// first segment that continues another CTA's unit goes first (it hands over
+// partial sums), then an unfinished last segment (this CTA completes that
+// unit once the partial sums of the CTAs running its later steps are in),
+// then the units in between.
+__device__ __forceinline__ int seg_unit(const Ranges& r, int ph, int idx, int n_units) {
+  const int lo_u = r.lo_u[ph], lo_k = r.lo_k[ph], hi_u = r.hi_u[ph], hi_k = r.hi_k[ph];
+  const bool c = lo_k > 0 && lo_u < n_units;
+  const bool h = hi_k > 0 && !(hi_u == lo_u && lo_k > 0) && hi_u < n_units;
+  if (c) {
+    if (idx == 0) return lo_u;
+    --idx;
+  }
+  if (h) {
+    if (idx == 0) return hi_u;
+    --idx;
+  }
+  const int mid_lo = c ? lo_u + 1 : lo_u;
+  const int mid_hi = min(h ? hi_u : hi_u + 1, n_units);
+  const int u = mid_lo + idx;
+  return u < mid_hi ? u : -1;
+}
+
+// Segment [ks, ke) of unit u inside [lo, hi); returns false if empty.
+__device__ __forceinline__ bool segment(int u, int lo_u, int lo_k, int hi_u, int hi_k, int steps, int* ks, int* ke) {
+  *ks = u == lo_u ? lo_k : 0;
+  *ke = u == hi_u ? hi_k : steps;
+  return *ks < *ke;
+}
+
+// ---------------------------------------------------------------------------
+// The prefill kernel.
+// ---------------------------------------------------------------------------
+
+template <bool kBf16>
+__global__ void __launch_bounds__(kThreads, 1)
+    prefill_kernel(const __grid_constant__ CUtensorMap tm_records, const __grid_constant__ CUtensorMap tm_x,
+                   const __grid_constant__ CUtensorMap tm_abuf, const PrefillArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align_1024(smem_raw);
+  Control* ctl = reinterpret_cast<Control*>(smem + kStages * kStageBytes);
+  volatile int* abort_flag = &ctl->abort;
+  int* status = a.header + kHdrStatus;
   const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
-      mbar_init(&bars->full[s], 1);
-      mbar_init(&bars->empty[s], 1);
+      mbar_init(&ctl->full[s], 2);  // the two loading threads each arrive with their bytes
+      mbar_init(&ctl->empty[s], 1);
     }
     for (int j = 0; j < 2; ++j) {
-      mbar_init(&bars->acc_full[j], 1);
-      mbar_init(&bars->acc_empty[j], 4);  // one arrival per TMEM-reading warp
+      mbar_init(&ctl->acc_full[j], 1);
+      mbar_init(&ctl->acc_empty[j], 4);  // one arrival per TMEM-reading warp
     }
-    mbar_init(&bars->drain, 1);
-    bars->abort = 0;
+    mbar_init(&ctl->drain, 1);
+    mbar_init(&ctl->steps_ready, 1);
+    ctl->abort = 0;
+    ctl->epoch = a.header[kHdrEpoch];
     fence_barrier_init();
   }
+  {
+    // This CTA's ranges, computed by the plan kernel.
+    const int4* src = reinterpret_cast<const int4*>(a.ranges + blockIdx.x);
+    int4* dst = reinterpret_cast<int4*>(&ctl->r);
+    for (int i = threadIdx.x; i < static_cast<int>(sizeof(Ranges) / 16); i += blockDim.x) dst[i] = src[i];
+  }
   if (warp == 1) {
-    tmem_alloc(&bars->tmem_base, kTmemCols);
+    tmem_alloc(&ctl->tmem_base, kTmemCols);
     tmem_relinquish();
   }
   tc_fence_before_sync();
   __syncthreads();
   tc_fence_after_sync();
-  return bars;
-}
-
-// Common end: every MMA has completed before TMEM is released.
-__device__ __forceinline__ void teardown(Barriers* bars, bool mma_thread) {
-  if (mma_thread) {
-    tc_commit(&bars->drain);
-    mbar_wait_bounded(&bars->drain, 0, kWaitLimitNs);
+  const uint32_t tmem = ctl->tmem_base;
+  const int epoch = ctl->epoch;
+  const int n_units = a.header[kHdrUnits];
+  const int n_down = a.n_hranges * a.n_tiles;
+  if (warp == kFirstReader) {
+    // This CTA's down steps in order, staged for the TMA thread.
+    int n = 0;
+    for (int si = 0, v; (v = seg_unit(ctl->r, 1, si, n_down)) >= 0; ++si) {
+      const int t = v % a.n_tiles;
+      int ks, ke;
+      if (!segment(v, ctl->r.lo_u[1], ctl->r.lo_k[1], ctl->r.hi_u[1], ctl->r.hi_k[1], a.header[kHdrTileCount + t], &ks, &ke))
+        continue;
+      for (int j = ks + lane; j < ke; j += 32)
+        if (n + (j - ks) < kSmemList) ctl->steps[n + (j - ks)] = (v << 16) | a.tile_list[t * a.n_blocks + j];
+      n += ke - ks;
+    }
+    __syncwarp();
+    if (lane == 0) {
+      ctl->n_steps = n;
+      mbar_arrive(&ctl->steps_ready);
+    }
   }
-  tc_fence_before_sync();
-  __syncthreads();
-  if ((threadIdx.x >> 5) == 1) {
-    tc_fence_after_sync();
-    tmem_dealloc(bars->tmem_base, kTmemCols);
-  }
-}
 
-template <bool kBf16>
-__global__ void __launch_bounds__(kThreads, 1)
-    prefill_gate_up_kernel(const __grid_constant__ CUtensorMap tm_records, const __grid_constant__ CUtensorMap tm_x,
-                           int n_chunks, int32_t* __restrict__ header, const int32_t* __restrict__ units,
-                           uint16_t* __restrict__ abuf, int64_t ld_abuf) {
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = align_1024(smem_raw);
-  Barriers* bars = setup(smem);
-  volatile int* abort_flag = &bars->abort;
-  int* status = header + kHdrStatus;
-  const int warp = threadIdx.x >> 5;
-  const int lane = threadIdx.x & 31;
-  const int n_units = header[kHdrUnits];
-  const uint32_t tmem = bars->tmem_base;
+  // Per-role pipeline state, carried from phase 1 into phase 2.
+  uint32_t it = 0;  // producer / MMA: ring iterations
+  uint32_t ut = 0;  // MMA / TMEM readers: accumulator buffers used
 
+  // ------------------------------ phase 1 ------------------------------
   if (warp == 0) {
-    if (lane == 0) {
-      tma_prefetch_map(&tm_records);
-      tma_prefetch_map(&tm_x);
-      uint32_t it = 0;
-      for (int u = blockIdx.x; u < n_units; u += gridDim.x) {
-        const int unit = units[u];
-        const int b = unit >> 8;
-        const int ta = (unit >> 4) & 0xF;
-        const int tb = unit & 0xF;
-        const int nt = tb == 0xF ? 1 : 2;
-        const uint32_t bytes = 2 * kHalfBox + nt * kTileBox;
-        bool ok = true;
-        for (int kc = 0; kc < n_chunks; ++kc, ++it) {
+    // Weight loader: lane 0 issues the gate/up boxes.  (Prefetching later
+    // weight boxes into L2, by TMA or by the other lanes, measured slower: the
+    // loads are not waiting on DRAM.)
+    if (lane == 0) tma_prefetch_map(&tm_records);
+    bool stop = false;
+    for (int si = 0, u; !stop && (u = seg_unit(ctl->r, 0, si, n_units)) >= 0; ++si) {
+      int ks, ke;
+      if (!segment(u, ctl->r.lo_u[0], ctl->r.lo_k[0], ctl->r.hi_u[0], ctl->r.hi_k[0], a.n_chunks, &ks, &ke)) continue;
+      const int b = a.units[u] >> 8;
+      for (int kc = ks; kc < ke; ++kc, ++it) {
+        int ok = 1;
+        if (lane == 0) {
           const int s = it % kStages;
-          if (!wait_phase(&bars->empty[s], ((it / kStages) & 1u) ^ 1u, abort_flag, status)) {
-            ok = false;
-            break;
+          ok = wait_phase(&ctl->empty[s], ((it / kStages) & 1u) ^ 1u, abort_flag, status) ? 1 : 0;
+          if (ok) {
+            uint8_t* st = smem + s * kStageBytes;
+            mbar_arrive_expect_tx(&ctl->full[s], kBox128);
+            tma_load_3d(st, &tm_records, kc * kChunk, 0, b * kBlock, &ctl->full[s]);
+            tma_load_3d(st + kBox64, &tm_records, kc * kChunk, 1, b * kBlock, &ctl->full[s]);
           }
-          uint8_t* st = smem + s * kStageBytes;
-          mbar_arrive_expect_tx(&bars->full[s], bytes);
-          tma_load_3d(st, &tm_records, kc * kChunk, 0, b * kBlock, &bars->full[s]);
-          tma_load_3d(st + kHalfBox, &tm_records, kc * kChunk, 1, b * kBlock, &bars->full[s]);
-          tma_load_2d(st + 2 * kHalfBox, &tm_x, kc * kChunk, ta * kTile, &bars->full[s]);
-          if (nt == 2) tma_load_2d(st + 2 * kHalfBox + kTileBox, &tm_x, kc * kChunk, tb * kTile, &bars->full[s]);
         }
-        if (!ok) break;
-      }
-      drain_loads(bars, it);
-    }
-  } else if (warp == 1) {
-    if (lane == 0) {
-      constexpr uint32_t idesc = idesc_f16_f32(128, 128, kBf16, false, false);
-      uint32_t it = 0, ut = 0;
-      for (int u = blockIdx.x; u < n_units; u += gridDim.x, ++ut) {
-        const int unit = units[u];
-        const int nt = (unit & 0xF) == 0xF ? 1 : 2;
-        const uint32_t j = ut & 1u;
-        if (!wait_phase(&bars->acc_empty[j], ((ut >> 1) & 1u) ^ 1u, abort_flag, status)) break;
-        tc_fence_after_sync();
-        const uint32_t d0 = tmem + j * 256u;
-        bool ok = true;
-        for (int kc = 0; kc < n_chunks; ++kc, ++it) {
-          const int s = it % kStages;
-          if (!wait_phase(&bars->full[s], (it / kStages) & 1u, abort_flag, status)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after_sync();
-          const uint32_t st = smem_addr(smem + s * kStageBytes);
-          const uint64_t b_desc = smem_desc_sw128(st, 16, 1024);
-          for (int i = 0; i < nt; ++i) {
-            const uint64_t a_desc = smem_desc_sw128(st + 2 * kHalfBox + i * kTileBox, 16, 1024);
-#pragma unroll
-            for (int kk = 0; kk < kChunk / 16; ++kk)
-              tc_mma_f16(d0 + i * 128u, a_desc + 2u * kk, b_desc + 2u * kk, idesc, (kc | kk) != 0 ? 1u : 0u);
-          }
-          tc_commit(&bars->empty[s]);
+        if (!__shfl_sync(0xffffffffu, ok, 0)) {
+          stop = true;
+          break;
         }
-        if (!ok) break;
-        tc_commit(&bars->acc_full[j]);
       }
     }
-  } else {
-    // TMEM readers: warp w may read lanes 32*(w%4) .. +31 = token rows of the tile.
-    const int q = warp & 3;
-    const int row = q * 32 + lane;
-    uint32_t ut = 0;
-    for (int u = blockIdx.x; u < n_units; u += gridDim.x, ++ut) {
-      const int unit = units[u];
-      const int b = unit >> 8;
+  } else if (warp == kActWarp && lane == 0) {
+    // Activation loader: the x boxes of the unit's tiles.
+    tma_prefetch_map(&tm_x);
+    tma_prefetch_map(&tm_abuf);
+    for (int si = 0, u; (u = seg_unit(ctl->r, 0, si, n_units)) >= 0 && !*abort_flag; ++si) {
+      int ks, ke;
+      if (!segment(u, ctl->r.lo_u[0], ctl->r.lo_k[0], ctl->r.hi_u[0], ctl->r.hi_k[0], a.n_chunks, &ks, &ke)) continue;
+      const int unit = a.units[u];
       const int ta = (unit >> 4) & 0xF;
       const int tb = unit & 0xF;
-      const int nt = tb == 0xF ? 1 : 2;
+      const int nt = unit_tiles(unit);
+      for (int kc = ks; kc < ke; ++kc, ++it) {
+        const int s = it % kStages;
+        if (!wait_phase(&ctl->empty[s], ((it / kStages) & 1u) ^ 1u, abort_flag, status)) break;
+        uint8_t* st = smem + s * kStageBytes;
+        mbar_arrive_expect_tx(&ctl->full[s], nt * kBox128);
+        tma_load_2d(st + kBox128, &tm_x, kc * kChunk, ta * kTile, &ctl->full[s]);
+        if (nt == 2) tma_load_2d(st + 2 * kBox128, &tm_x, kc * kChunk, tb * kTile, &ctl->full[s]);
+      }
+    }
+  } else if (warp == 1 && lane == 0) {
+    constexpr uint32_t idesc = idesc_f16_f32(128, 128, kBf16, false, false);
+    for (int si = 0, u; (u = seg_unit(ctl->r, 0, si, n_units)) >= 0 && !*abort_flag; ++si) {
+      int ks, ke;
+      if (!segment(u, ctl->r.lo_u[0], ctl->r.lo_k[0], ctl->r.hi_u[0], ctl->r.hi_k[0], a.n_chunks, &ks, &ke)) continue;
+      const int nt = unit_tiles(a.units[u]);
       const uint32_t j = ut & 1u;
-      if (!warp_wait_phase(&bars->acc_full[j], (ut >> 1) & 1u, abort_flag, status)) break;
+      if (!wait_phase(&ctl->acc_empty[j], ((ut >> 1) & 1u) ^ 1u, abort_flag, status)) break;
       tc_fence_after_sync();
-      for (int i = 0; i < nt; ++i) {
-        const int t = i == 0 ? ta : tb;
-        const uint32_t col0 = tmem + (static_cast<uint32_t>(q * 32) << 16) + j * 256u + i * 128u;
-        uint16_t* dst = abuf + static_cast<int64_t>(t * kTile + row) * ld_abuf + static_cast<int64_t>(b) * kBlock;
+      const uint32_t d0 = tmem + j * kAccCols;
+      bool ok = true;
+      for (int kc = ks; kc < ke; ++kc, ++it) {
+        const int s = it % kStages;
+        if (!wait_phase(&ctl->full[s], (it / kStages) & 1u, abort_flag, status)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after_sync();
+        const uint32_t st = smem_addr(smem + s * kStageBytes);
+        const uint64_t b_desc = smem_desc_sw128(st, 16, 1024);
+        for (int i = 0; i < nt; ++i) {
+          const uint64_t a_desc = smem_desc_sw128(st + kBox128 + i * kBox128, 16, 1024);
 #pragma unroll
-        for (int c = 0; c < 2; ++c) {
-          float g[32], v[32];
-          tmem_load32(col0 + c * 32, g);
-          tmem_load32(col0 + 64 + c * 32, v);
-          uint32_t w[16];
+          for (int kk = 0; kk < kChunk / 16; ++kk)
+            tc_mma_f16(d0 + i * 128u, a_desc + 2u * kk, b_desc + 2u * kk, idesc, (kc > ks || kk > 0) ? 1u : 0u);
+        }
+        tc_commit(&ctl->empty[s]);
+      }
+      if (!ok) break;
+      tc_commit(&ctl->acc_full[j]);
+      ++ut;
+    }
+  } else if (warp >= kFirstReader && warp < kFirstReader + kReaders) {
+    const int q = warp & 3;  // TMEM lanes 32q .. 32q+31 = token rows of the tile
+    const int row = q * 32 + lane;
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>(q * 32) << 16);
+    for (int si = 0, u; (u = seg_unit(ctl->r, 0, si, n_units)) >= 0; ++si) {
+      int ks, ke;
+      if (!segment(u, ctl->r.lo_u[0], ctl->r.lo_k[0], ctl->r.hi_u[0], ctl->r.hi_k[0], a.n_chunks, &ks, &ke)) continue;
+      const int unit = a.units[u];
+      const int b = unit >> 8;
+      const int nt = unit_tiles(unit);
+      const uint32_t j = ut & 1u;
+      if (!warp_wait_phase(&ctl->acc_full[j], (ut >> 1) & 1u, abort_flag, status)) break;
+      tc_fence_after_sync();
+      const uint32_t col0 = lane_base + j * kAccCols;
+      if (ks > 0) {
+        // Not this unit's first K steps: hand the accumulators to the CTA that finishes it.
+        float* slot = a.partials + static_cast<size_t>(blockIdx.x) * kSlotFloats;
+        for (int i = 0; i < nt; ++i) {
+          float4* dst = reinterpret_cast<float4*>(slot + (static_cast<size_t>(i) * 128 + row) * 128);
+#pragma unroll 1
+          for (int c = 0; c < 4; ++c) {
+            float v[32];
+            tmem_load32(col0 + i * 128u + c * 32u, v);
 #pragma unroll
-          for (int e = 0; e < 16; ++e)
-            w[e] = pack2<kBf16>(silu(g[2 * e]) * v[2 * e], silu(g[2 * e + 1]) * v[2 * e + 1]);
-          uint4* d4 = reinterpret_cast<uint4*>(dst + c * 32);
+            for (int e = 0; e < 8; ++e) dst[c * 8 + e] = make_float4(v[4 * e], v[4 * e + 1], v[4 * e + 2], v[4 * e + 3]);
+          }
+        }
+        __threadfence();
+        epilogue_sync();
+        if (threadIdx.x == 64) atomicExch(a.flags1 + blockIdx.x, epoch);
+      } else {
+        const bool wait_others = ke < a.n_chunks;
+        if (wait_others)
+          warp_wait_flags(a.flags1, ctl->r.contrib[0], ctl->r.n_contrib[0], epoch, abort_flag, status);
+        for (int i = 0; i < nt; ++i) {
+          const int t = i == 0 ? (unit >> 4) & 0xF : unit & 0xF;
+          uint16_t* dst = a.abuf + static_cast<int64_t>(t * kTile + row) * a.ld_abuf + static_cast<int64_t>(b) * kBlock;
+#pragma unroll 1
+          for (int c = 0; c < 2; ++c) {
+            float g[32], v[32];
+            tmem_load32(col0 + i * 128u + c * 32u, g);
+            tmem_load32(col0 + i * 128u + 64u + c * 32u, v);
+            if (wait_others) {
+              for (int ci = 0; ci < ctl->r.n_contrib[0]; ++ci) {
+                const float4* p = reinterpret_cast<const float4*>(
+                    a.partials + static_cast<size_t>(ctl->r.contrib[0][ci]) * kSlotFloats + (static_cast<size_t>(i) * 128 + row) * 128);
 #pragma unroll
-          for (int e = 0; e < 4; ++e) d4[e] = make_uint4(w[4 * e], w[4 * e + 1], w[4 * e + 2], w[4 * e + 3]);
+                for (int e = 0; e < 8; ++e) {
+                  const float4 pg = __ldcg(p + c * 8 + e);
+                  const float4 pu = __ldcg(p + 16 + c * 8 + e);
+                  g[4 * e] += pg.x, g[4 * e + 1] += pg.y, g[4 * e + 2] += pg.z, g[4 * e + 3] += pg.w;
+                  v[4 * e] += pu.x, v[4 * e + 1] += pu.y, v[4 * e + 2] += pu.z, v[4 * e + 3] += pu.w;
+                }
+              }
+            }
+            uint32_t w[16];
+#pragma unroll
+            for (int e = 0; e < 16; ++e)
+              w[e] = pack2<kBf16>(silu(g[2 * e]) * v[2 * e], silu(g[2 * e + 1]) * v[2 * e + 1]);
+            uint4* d4 = reinterpret_cast<uint4*>(dst + c * 32);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) d4[e] = make_uint4(w[4 * e], w[4 * e + 1], w[4 * e + 2], w[4 * e + 3]);
+          }
         }
       }
       tc_fence_before_sync();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&bars->acc_empty[j]);
+      if (lane == 0) mbar_arrive(&ctl->acc_empty[j]);
+      ++ut;
     }
+    // Activations written with generic stores are read by TMA in phase 2.
+    fence_proxy_async_global();
   }
-  teardown(bars, warp == 1 && lane == 0);
-}
 
-template <bool kBf16>
-__global__ void __launch_bounds__(kThreads, 1)
-    prefill_down_kernel(const __grid_constant__ CUtensorMap tm_records, const __grid_constant__ CUtensorMap tm_abuf,
-                        int32_t* __restrict__ header, const int32_t* __restrict__ unions, int n_hchunks, int splits,
-                        int hidden, int n_tokens, float* __restrict__ partials, int64_t ld_part, void* __restrict__ y,
-                        int64_t ldy, int y_dtype) {
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = align_1024(smem_raw);
-  Barriers* bars = setup(smem);
-  volatile int* abort_flag = &bars->abort;
-  int* status = header + kHdrStatus;
-  const int warp = threadIdx.x >> 5;
-  const int lane = threadIdx.x & 31;
-  const int hc = blockIdx.x % n_hchunks;
-  const int split = blockIdx.x / n_hchunks;
-  const int n_union = header[kHdrUnion];
-  const int e_begin = static_cast<int>(static_cast<int64_t>(split) * n_union / splits);
-  const int e_end = static_cast<int>(static_cast<int64_t>(split + 1) * n_union / splits);
-  const uint32_t tmem = bars->tmem_base;
+  // --------------------------- grid barrier ----------------------------
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    atomicAdd(a.header + kHdrArrive, 1);
+    const uint64_t start = global_timer_ns();
+    while (ld_acquire(a.header + kHdrArrive) < static_cast<int>(gridDim.x)) {
+      if (global_timer_ns() - start > kWaitLimitNs) {
+        ctl->abort = 1;
+        atomicOr(status, QCC_DEV_TIMEOUT);
+        break;
+      }
+    }
+    fence_proxy_async_global();
+  }
+  __syncthreads();
 
+  // ------------------------------ phase 2 ------------------------------
+  const int staged = min(ctl->n_steps, kSmemList);
   if (warp == 0) {
-    if (lane == 0) {
-      tma_prefetch_map(&tm_records);
-      tma_prefetch_map(&tm_abuf);
-      uint32_t it = 0;
-      bool ok = true;
-      for (int e = e_begin; e < e_end && ok; ++e) {
-        const int word = unions[e];
-        const int b = word >> 8;
-        int m = word & 0xF;
-        while (m != 0 && ok) {
-          const int t0 = __ffs(m) - 1;
-          m &= m - 1;
-          const int t1 = m != 0 ? __ffs(m) - 1 : -1;
-          if (t1 >= 0) m &= m - 1;
+    bool stop = false;
+    int si = 0;  // position in this CTA's step sequence
+    for (int sv = 0, v; !stop && (v = seg_unit(ctl->r, 1, sv, n_down)) >= 0; ++sv) {
+      const int t = v % a.n_tiles, r = v / a.n_tiles;
+      int ks, ke;
+      if (!segment(v, ctl->r.lo_u[1], ctl->r.lo_k[1], ctl->r.hi_u[1], ctl->r.hi_k[1], a.header[kHdrTileCount + t], &ks,
+                   &ke))
+        continue;
+      for (int step = ks; step < ke; ++step, ++it, ++si) {
+        int ok = 1;
+        if (lane == 0) {
+          const int b = si < staged ? (ctl->steps[si] & 0xFFFF) : a.tile_list[t * a.n_blocks + step];
           const int s = it % kStages;
-          if (!wait_phase(&bars->empty[s], ((it / kStages) & 1u) ^ 1u, abort_flag, status)) {
-            ok = false;
-            break;
+          ok = wait_phase(&ctl->empty[s], ((it / kStages) & 1u) ^ 1u, abort_flag, status) ? 1 : 0;
+          if (ok) {
+            uint8_t* st = smem + s * kStageBytes;
+            mbar_arrive_expect_tx(&ctl->full[s], 4 * kBox64);
+            for (int qq = 0; qq < 4; ++qq)
+              tma_load_3d(st + kBox128 + qq * kBox64, &tm_records, r * kHRange + qq * 64, 2, b * kBlock,
+                          &ctl->full[s]);
           }
-          uint8_t* st = smem + s * kStageBytes;
-          mbar_arrive_expect_tx(&bars->full[s], 2 * kHalfBox + (t1 >= 0 ? 2 : 1) * kTileBox);
-          tma_load_3d(st, &tm_records, hc * kHChunk, 2, b * kBlock, &bars->full[s]);
-          tma_load_3d(st + kHalfBox, &tm_records, hc * kHChunk + 64, 2, b * kBlock, &bars->full[s]);
-          tma_load_2d(st + 2 * kHalfBox, &tm_abuf, b * kBlock, t0 * kTile, &bars->full[s]);
-          if (t1 >= 0) tma_load_2d(st + 2 * kHalfBox + kTileBox, &tm_abuf, b * kBlock, t1 * kTile, &bars->full[s]);
-          ++it;
+        }
+        if (!__shfl_sync(0xffffffffu, ok, 0)) {
+          stop = true;
+          break;
         }
       }
-      drain_loads(bars, it);
     }
-  } else if (warp == 1) {
-    if (lane == 0) {
-      constexpr uint32_t idesc = idesc_f16_f32(128, 128, kBf16, true, false);
-      uint32_t it = 0, started = 0;
+    if (lane == 0) drain_loads(ctl, it);
+  } else if (warp == kActWarp && lane == 0) {
+    int si = 0;
+    for (int sv = 0, v; (v = seg_unit(ctl->r, 1, sv, n_down)) >= 0 && !*abort_flag; ++sv) {
+      const int t = v % a.n_tiles;
+      int ks, ke;
+      if (!segment(v, ctl->r.lo_u[1], ctl->r.lo_k[1], ctl->r.hi_u[1], ctl->r.hi_k[1], a.header[kHdrTileCount + t], &ks,
+                   &ke))
+        continue;
+      for (int step = ks; step < ke; ++step, ++it, ++si) {
+        const int b = si < staged ? (ctl->steps[si] & 0xFFFF) : a.tile_list[t * a.n_blocks + step];
+        const int s = it % kStages;
+        if (!wait_phase(&ctl->empty[s], ((it / kStages) & 1u) ^ 1u, abort_flag, status)) break;
+        uint8_t* st = smem + s * kStageBytes;
+        mbar_arrive_expect_tx(&ctl->full[s], kBox128);
+        tma_load_2d(st, &tm_abuf, b * kBlock, t * kTile, &ctl->full[s]);
+      }
+    }
+  } else if (warp == 1 && lane == 0) {
+    constexpr uint32_t idesc = idesc_f16_f32(128, 256, kBf16, false, true);
+    for (int sv = 0, v; (v = seg_unit(ctl->r, 1, sv, n_down)) >= 0 && !*abort_flag; ++sv) {
+      const int t = v % a.n_tiles;
+      int ks, ke;
+      if (!segment(v, ctl->r.lo_u[1], ctl->r.lo_k[1], ctl->r.hi_u[1], ctl->r.hi_k[1], a.header[kHdrTileCount + t], &ks, &ke))
+        continue;
+      const uint32_t j = ut & 1u;
+      if (!wait_phase(&ctl->acc_empty[j], ((ut >> 1) & 1u) ^ 1u, abort_flag, status)) break;
+      tc_fence_after_sync();
+      const uint32_t d0 = tmem + j * kAccCols;
       bool ok = true;
-      for (int e = e_begin; e < e_end && ok; ++e) {
-        int m = unions[e] & 0xF;
-        while (m != 0) {
-          const int t0 = __ffs(m) - 1;
-          m &= m - 1;
-          const int t1 = m != 0 ? __ffs(m) - 1 : -1;
-          if (t1 >= 0) m &= m - 1;
-          const int s = it % kStages;
-          if (!wait_phase(&bars->full[s], (it / kStages) & 1u, abort_flag, status)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after_sync();
-          const uint32_t st = smem_addr(smem + s * kStageBytes);
-          // D slice: MN-major, 64 hidden rows per 128-byte line, second 64 rows kHalfBox further.
-          const uint64_t a_desc = smem_desc_sw128(st, kHalfBox, 1024);
-          for (int i = 0; i < (t1 >= 0 ? 2 : 1); ++i) {
-            const int t = i == 0 ? t0 : t1;
-            const uint64_t b_desc = smem_desc_sw128(st + 2 * kHalfBox + i * kTileBox, 16, 1024);
-            const uint32_t acc = (started >> t) & 1u;
+      for (int step = ks; step < ke; ++step, ++it) {
+        const int s = it % kStages;
+        if (!wait_phase(&ctl->full[s], (it / kStages) & 1u, abort_flag, status)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after_sync();
+        const uint32_t st = smem_addr(smem + s * kStageBytes);
+        const uint64_t a_desc = smem_desc_sw128(st, 16, 1024);          // activations, K-major
+        const uint64_t b_desc = smem_desc_sw128(st + kBox128, kBox64, 1024);  // down rows, hidden-major
 #pragma unroll
-            for (int kk = 0; kk < kBlock / 16; ++kk)
-              tc_mma_f16(tmem + t * 128u, a_desc + 128u * kk, b_desc + 2u * kk, idesc, (acc | kk) != 0 ? 1u : 0u);
-            started |= 1u << t;
-          }
-          tc_commit(&bars->empty[s]);
-          ++it;
-        }
+        for (int kk = 0; kk < kBlock / 16; ++kk)
+          tc_mma_f16(d0, a_desc + 2u * kk, b_desc + 128u * kk, idesc, (step > ks || kk > 0) ? 1u : 0u);
+        tc_commit(&ctl->empty[s]);
       }
-      tc_commit(&bars->acc_full[0]);
+      if (!ok) break;
+      tc_commit(&ctl->acc_full[j]);
+      ++ut;
     }
-  } else {
+  } else if (warp >= kFirstReader && warp < kFirstReader + kReaders) {
     const int q = warp & 3;
-    const int hl = q * 32 + lane;  // TMEM lane = hidden row of the chunk
-    const int h = hc * kHChunk + hl;
-    uint32_t started = 0;
-    for (int e = e_begin; e < e_end; ++e) started |= unions[e] & 0xF;
-    const bool ready = warp_wait_phase(&bars->acc_full[0], 0, abort_flag, status);
-    tc_fence_after_sync();
-    const int n_tiles = (n_tokens + kTile - 1) / kTile;
-    float* part = partials + static_cast<int64_t>(split) * kGroupTokens * ld_part;
-    for (int t = 0; t < n_tiles && ready; ++t) {
-      const bool have = (started >> t) & 1u;
-      for (int c = 0; c < kTile / 32; ++c) {
-        float v[32];
-        if (have) {
-          tmem_load32(tmem + (static_cast<uint32_t>(q * 32) << 16) + t * 128u + c * 32u, v);
-        } else {
+    const int row = q * 32 + lane;
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>(q * 32) << 16);
+    const size_t y_es = a.y_dtype == QCC_DTYPE_F32 ? 4 : 2;
+    for (int sv = 0, v; (v = seg_unit(ctl->r, 1, sv, n_down)) >= 0; ++sv) {
+      const int t = v % a.n_tiles, r = v / a.n_tiles;
+      int ks, ke;
+      const int steps = a.header[kHdrTileCount + t];
+      if (!segment(v, ctl->r.lo_u[1], ctl->r.lo_k[1], ctl->r.hi_u[1], ctl->r.hi_k[1], steps, &ks, &ke)) continue;
+      const uint32_t j = ut & 1u;
+      if (!warp_wait_phase(&ctl->acc_full[j], (ut >> 1) & 1u, abort_flag, status)) break;
+      tc_fence_after_sync();
+      const uint32_t col0 = lane_base + j * kAccCols;
+      if (ks > 0) {
+        float4* dst = reinterpret_cast<float4*>(a.partials + static_cast<size_t>(blockIdx.x) * kSlotFloats +
+                                                static_cast<size_t>(row) * 256);
+#pragma unroll 1
+        for (int c = 0; c < 8; ++c) {
+          float vv[32];
+          tmem_load32(col0 + c * 32u, vv);
 #pragma unroll
-          for (int k = 0; k < 32; ++k) v[k] = 0.f;
+          for (int e = 0; e < 8; ++e)
+            dst[c * 8 + e] = make_float4(vv[4 * e], vv[4 * e + 1], vv[4 * e + 2], vv[4 * e + 3]);
         }
-        if (h < hidden) {
+        __threadfence();
+        epilogue_sync();
+        if (threadIdx.x == 64) atomicExch(a.flags2 + blockIdx.x, epoch);
+      } else {
+        const bool wait_others = ke < steps;
+        if (wait_others)
+          warp_wait_flags(a.flags2, ctl->r.contrib[1], ctl->r.n_contrib[1], epoch, abort_flag, status);
+        const int tok = t * kTile + row;
+        const bool row_ok = tok < a.n_tokens;
+        uint8_t* yrow = static_cast<uint8_t*>(a.y) + static_cast<size_t>(tok) * a.ldy * y_es;
+#pragma unroll 1
+        for (int c = 0; c < 8; ++c) {
+          float vv[32];
+          tmem_load32(col0 + c * 32u, vv);
+          if (wait_others) {
+            for (int ci = 0; ci < ctl->r.n_contrib[1]; ++ci) {
+              const float4* p = reinterpret_cast<const float4*>(
+                  a.partials + static_cast<size_t>(ctl->r.contrib[1][ci]) * kSlotFloats + static_cast<size_t>(row) * 256);
 #pragma unroll
-          for (int k = 0; k < 32; ++k) {
-            const int tok = t * kTile + c * 32 + k;
-            if (tok < n_tokens) {
-              if (splits == 1)
-                store_as(y, static_cast<int64_t>(tok) * ldy + h, y_dtype, v[k]);
-              else
-                part[static_cast<int64_t>(tok) * ld_part + h] = v[k];
+              for (int e = 0; e < 8; ++e) {
+                const float4 pv = __ldcg(p + c * 8 + e);
+                vv[4 * e] += pv.x, vv[4 * e + 1] += pv.y, vv[4 * e + 2] += pv.z, vv[4 * e + 3] += pv.w;
+              }
             }
           }
+          const int h0 = r * kHRange + c * 32;
+          if (!row_ok || h0 >= a.hidden) continue;
+          if (a.y_vec && h0 + 32 <= a.hidden) {
+            if (a.y_dtype == QCC_DTYPE_F32) {
+              float4* d4 = reinterpret_cast<float4*>(yrow + static_cast<size_t>(h0) * 4);
+#pragma unroll
+              for (int e = 0; e < 8; ++e) d4[e] = make_float4(vv[4 * e], vv[4 * e + 1], vv[4 * e + 2], vv[4 * e + 3]);
+            } else {
+              uint32_t w[16];
+#pragma unroll
+              for (int e = 0; e < 16; ++e)
+                w[e] = a.y_dtype == QCC_DTYPE_BF16 ? pack2<true>(vv[2 * e], vv[2 * e + 1])
+                                                   : pack2<false>(vv[2 * e], vv[2 * e + 1]);
+              uint4* d4 = reinterpret_cast<uint4*>(yrow + static_cast<size_t>(h0) * 2);
+#pragma unroll
+              for (int e = 0; e < 4; ++e) d4[e] = make_uint4(w[4 * e], w[4 * e + 1], w[4 * e + 2], w[4 * e + 3]);
+            }
+          } else {
+#pragma unroll
+            for (int e = 0; e < 32; ++e)
+              if (h0 + e < a.hidden) store_as(a.y, static_cast<int64_t>(tok) * a.ldy + h0 + e, a.y_dtype, vv[e]);
+          }
         }
       }
+      tc_fence_before_sync();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&ctl->acc_empty[j]);
+      ++ut;
+    }
+    // Tiles without blocks: their rows are zero.  Spread over the grid by (tile, range).
+    for (int v = blockIdx.x; v < n_down; v += gridDim.x) {
+      const int t = v % a.n_tiles, r = v / a.n_tiles;
+      if (a.header[kHdrTileCount + t] != 0) continue;
+      const int tok = t * kTile + row;
+      if (tok >= a.n_tokens) continue;
+      for (int h = r * kHRange; h < min(a.hidden, (r + 1) * kHRange); ++h)
+        store_as(a.y, static_cast<int64_t>(tok) * a.ldy + h, a.y_dtype, 0.f);
     }
   }
-  teardown(bars, warp == 1 && lane == 0);
-}
 
-// y = sum of the S partials (fixed order), converted to the output type.
-__global__ void __launch_bounds__(256)
-    prefill_reduce_kernel(const float* __restrict__ partials, int64_t ld_part, int splits, int n_tokens, int hidden,
-                          void* __restrict__ y, int64_t ldy, int y_dtype) {
-  const int64_t total = static_cast<int64_t>(n_tokens) * hidden;
-  const int64_t plane = static_cast<int64_t>(kGroupTokens) * ld_part;
-  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
-       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int64_t tok = i / hidden;
-    const int64_t h = i - tok * hidden;
-    const int64_t off = tok * ld_part + h;
-    float acc = __ldcg(partials + off);
-    for (int s = 1; s < splits; ++s) acc += __ldcg(partials + s * plane + off);
-    store_as(y, tok * ldy + h, y_dtype, acc);
+  // ------------------------------ teardown -----------------------------
+  if (warp == 1 && lane == 0) {
+    tc_commit(&ctl->drain);
+    mbar_wait_bounded(&ctl->drain, 0, kWaitLimitNs);
+  }
+  tc_fence_before_sync();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after_sync();
+    tmem_dealloc(tmem, kTmemCols);
   }
 }
 
@@ -523,29 +924,35 @@ bool make_map(CUtensorMap* map, int dtype, int rank, const void* base, const uin
 }
 
 struct PrefillLayout {
-  int n_blocks = 0, n_hchunks = 0, splits = 1;
-  int64_t npad = 0, ld_part = 0;
-  size_t units = 0, unions = 0, abuf = 0, partials = 0, total = 0;
+  int n_blocks = 0, grid = 0;
+  int64_t npad = 0;
+  size_t units = 0, prefix = 0, tile_list = 0, ranges = 0, flags1 = 0, flags2 = 0, abuf = 0, partials = 0, total = 0;
 };
 
 size_t round_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
-PrefillLayout prefill_layout(int64_t n_records, int hidden, int num_sms) {
+PrefillLayout prefill_layout(int64_t n_records, int num_sms) {
   PrefillLayout l;
   l.n_blocks = static_cast<int>((n_records + kBlock - 1) / kBlock);
-  l.n_hchunks = (hidden + kHChunk - 1) / kHChunk;
-  l.splits = std::max(1, std::min(kMaxSplits, num_sms / std::max(1, l.n_hchunks)));
+  l.grid = num_sms;
   l.npad = static_cast<int64_t>(l.n_blocks) * kBlock;
-  l.ld_part = round_up(static_cast<size_t>(hidden), 4);
   size_t off = kHeaderBytes;
   l.units = off;
   off = round_up(off + 2 * static_cast<size_t>(l.n_blocks) * 4, 256);
-  l.unions = off;
-  off = round_up(off + static_cast<size_t>(l.n_blocks) * 4, 1024);
+  l.prefix = off;
+  off = round_up(off + (2 * static_cast<size_t>(l.n_blocks) + 1) * 4, 256);
+  l.tile_list = off;
+  off = round_up(off + static_cast<size_t>(kMaxTiles) * l.n_blocks * 4, 256);
+  l.ranges = off;
+  off = round_up(off + static_cast<size_t>(l.grid) * sizeof(Ranges), 256);
+  l.flags1 = off;
+  off = round_up(off + static_cast<size_t>(l.grid) * 4, 256);
+  l.flags2 = off;
+  off = round_up(off + static_cast<size_t>(l.grid) * 4, 1024);
   l.abuf = off;
   off = round_up(off + static_cast<size_t>(kGroupTokens) * l.npad * 2, 1024);
   l.partials = off;
-  if (l.splits > 1) off += static_cast<size_t>(l.splits) * kGroupTokens * l.ld_part * 4;
+  off += static_cast<size_t>(l.grid) * kSlotFloats * 4;
   l.total = round_up(off, 256);
   return l;
 }
@@ -559,7 +966,7 @@ extern "C" size_t qcc_prefill_workspace_bytes(int64_t n_records, int hidden) {
   int device = 0;
   if (!qcc::cuda_ok(cudaGetDevice(&device))) return 0;
   const qcc::DeviceInfo& info = qcc::device_info(device);
-  return qcc::prefill_layout(n_records, hidden, info.num_sms).total;
+  return qcc::prefill_layout(n_records, info.num_sms).total;
 }
 
 extern "C" size_t qcc_prefill_workspace_status_offset(void) { return 0; }
@@ -573,6 +980,7 @@ extern "C" int qcc_indexed_ffn_prefill(const void* x, int64_t ldx, int n_tokens,
   if (!valid_dtype(y_dtype)) return QCC_ERR_DTYPE;
   if (n_tokens < 0 || hidden <= 0 || n_records <= 0 || ldx < hidden || ldy < hidden) return QCC_ERR_SHAPE;
   if (n_records > static_cast<int64_t>(kMaxBlocks) * kBlock) return QCC_ERR_UNSUPPORTED;
+  if ((hidden + kHRange - 1) / kHRange * kMaxTiles > kMaxDownUnits) return QCC_ERR_UNSUPPORTED;
   if (n_tokens == 0) return QCC_OK;
   if (x == nullptr || packed == nullptr || tile_blocks == nullptr || tile_offsets == nullptr || workspace == nullptr ||
       y == nullptr)
@@ -582,15 +990,31 @@ extern "C" int qcc_indexed_ffn_prefill(const void* x, int64_t ldx, int n_tokens,
   int device = 0;
   if (!cuda_ok(cudaGetDevice(&device))) return QCC_ERR_CUDA;
   const DeviceInfo& info = device_info(device);
-  const PrefillLayout l = prefill_layout(n_records, hidden, info.num_sms);
+  const PrefillLayout l = prefill_layout(n_records, info.num_sms);
   if (workspace_bytes < l.total) return QCC_ERR_WORKSPACE;
+  if (info.max_smem_optin < static_cast<int>(kSmemBytes)) return QCC_ERR_UNSUPPORTED;
   const int hp = hidden_pad(hidden, dtype);
   uint8_t* ws = static_cast<uint8_t*>(workspace);
-  int32_t* header = reinterpret_cast<int32_t*>(ws);
-  int32_t* units = reinterpret_cast<int32_t*>(ws + l.units);
-  int32_t* unions = reinterpret_cast<int32_t*>(ws + l.unions);
-  uint16_t* abuf = reinterpret_cast<uint16_t*>(ws + l.abuf);
-  float* partials = reinterpret_cast<float*>(ws + l.partials);
+
+  PrefillArgs args{};
+  args.header = reinterpret_cast<int32_t*>(ws);
+  args.units = reinterpret_cast<int32_t*>(ws + l.units);
+  args.unit_prefix = reinterpret_cast<int32_t*>(ws + l.prefix);
+  args.tile_list = reinterpret_cast<int32_t*>(ws + l.tile_list);
+  args.ranges = reinterpret_cast<const Ranges*>(ws + l.ranges);
+  args.n_blocks = l.n_blocks;
+  args.n_chunks = (hidden + kChunk - 1) / kChunk;
+  args.n_hranges = (hidden + kHRange - 1) / kHRange;
+  args.hidden = hidden;
+  args.abuf = reinterpret_cast<uint16_t*>(ws + l.abuf);
+  args.ld_abuf = l.npad;
+  args.partials = reinterpret_cast<float*>(ws + l.partials);
+  args.flags1 = reinterpret_cast<int32_t*>(ws + l.flags1);
+  args.flags2 = reinterpret_cast<int32_t*>(ws + l.flags2);
+  args.ldy = ldy;
+  args.y_dtype = y_dtype;
+  const size_t y_es = static_cast<size_t>(dtype_bytes(y_dtype));
+  args.y_vec = aligned16(y) && (static_cast<size_t>(ldy) * y_es) % 16 == 0;
 
   // Records as a 3-D tensor {hidden_pad, segment (gate, up, down), record}.
   CUtensorMap tm_records, tm_abuf;
@@ -604,29 +1028,24 @@ extern "C" int qcc_indexed_ffn_prefill(const void* x, int64_t ldx, int n_tokens,
     const uint64_t dims[2] = {static_cast<uint64_t>(l.npad), static_cast<uint64_t>(kGroupTokens)};
     const uint64_t strides[1] = {static_cast<uint64_t>(l.npad) * 2};
     const uint32_t box[2] = {64, 128};
-    if (!make_map(&tm_abuf, dtype, 2, abuf, dims, strides, box)) return QCC_ERR_UNSUPPORTED;
+    if (!make_map(&tm_abuf, dtype, 2, args.abuf, dims, strides, box)) return QCC_ERR_UNSUPPORTED;
   }
-  const void* fns[4] = {reinterpret_cast<const void*>(prefill_plan_kernel),
-                        dtype == QCC_DTYPE_BF16 ? reinterpret_cast<const void*>(prefill_gate_up_kernel<true>)
-                                                : reinterpret_cast<const void*>(prefill_gate_up_kernel<false>),
-                        dtype == QCC_DTYPE_BF16 ? reinterpret_cast<const void*>(prefill_down_kernel<true>)
-                                                : reinterpret_cast<const void*>(prefill_down_kernel<false>),
-                        reinterpret_cast<const void*>(prefill_reduce_kernel)};
-  for (const void* fn : fns)
-    if (!ensure_max_dynamic_smem(fn, device)) return QCC_ERR_CUDA;
-  if (info.max_smem_optin < static_cast<int>(kSmemBytes)) return QCC_ERR_UNSUPPORTED;
-  const size_t plan_smem = round_up(static_cast<size_t>(l.n_blocks), 4);
-  const int n_chunks = (hidden + kChunk - 1) / kChunk;
-  const int units_grid = std::max(1, std::min(info.num_sms, 2 * l.n_blocks));
-  const int down_grid = l.n_hchunks * l.splits;
+  const void* kernel = dtype == QCC_DTYPE_BF16 ? reinterpret_cast<const void*>(prefill_kernel<true>)
+                                               : reinterpret_cast<const void*>(prefill_kernel<false>);
+  if (!ensure_max_dynamic_smem(reinterpret_cast<const void*>(prefill_plan_kernel), device) ||
+      !ensure_max_dynamic_smem(kernel, device))
+    return QCC_ERR_CUDA;
+  const size_t plan_smem =
+      round_up(static_cast<size_t>(l.n_blocks), 4) + (2 * static_cast<size_t>(std::min(2 * l.n_blocks, kPlanUnits)) + 1) * 4;
   const uint8_t* xb = static_cast<const uint8_t*>(x);
   uint8_t* yb = static_cast<uint8_t*>(y);
-  const size_t y_esize = static_cast<size_t>(dtype_bytes(y_dtype));
 
   clear_stale_error();
   for (int g0 = 0; g0 < n_tokens; g0 += kGroupTokens) {
     const int rows = std::min(kGroupTokens, n_tokens - g0);
-    const int n_tiles = (rows + kTile - 1) / kTile;
+    args.n_tokens = rows;
+    args.n_tiles = (rows + kTile - 1) / kTile;
+    args.y = yb + static_cast<size_t>(g0) * ldy * y_es;
     CUtensorMap tm_x;
     {
       const uint64_t dims[2] = {static_cast<uint64_t>(hidden), static_cast<uint64_t>(rows)};
@@ -635,32 +1054,24 @@ extern "C" int qcc_indexed_ffn_prefill(const void* x, int64_t ldx, int n_tokens,
       if (!make_map(&tm_x, dtype, 2, xb + static_cast<size_t>(g0) * ldx * 2, dims, strides, box))
         return QCC_ERR_UNSUPPORTED;
     }
-    void* yg = yb + static_cast<size_t>(g0) * ldy * y_esize;
-    prefill_plan_kernel<<<1, kPlanThreads, plan_smem, stream>>>(tile_blocks, tile_offsets + g0 / kTile, n_tiles,
-                                                                l.n_blocks, header, units, unions);
+    prefill_plan_kernel<<<1, kPlanThreads, plan_smem, stream>>>(
+        tile_blocks, tile_offsets + g0 / kTile, args.n_tiles, l.n_blocks, args.n_chunks, args.n_hranges, l.grid,
+        args.header, const_cast<int32_t*>(args.units), const_cast<int32_t*>(args.unit_prefix),
+        const_cast<int32_t*>(args.tile_list), const_cast<Ranges*>(args.ranges));
     if (!launch_ok()) return QCC_ERR_CUDA;
-    if (dtype == QCC_DTYPE_BF16)
-      prefill_gate_up_kernel<true><<<units_grid, kThreads, kSmemBytes, stream>>>(tm_records, tm_x, n_chunks, header,
-                                                                                 units, abuf, l.npad);
-    else
-      prefill_gate_up_kernel<false><<<units_grid, kThreads, kSmemBytes, stream>>>(tm_records, tm_x, n_chunks, header,
-                                                                                  units, abuf, l.npad);
-    if (!launch_ok()) return QCC_ERR_CUDA;
-    if (dtype == QCC_DTYPE_BF16)
-      prefill_down_kernel<true><<<down_grid, kThreads, kSmemBytes, stream>>>(
-          tm_records, tm_abuf, header, unions, l.n_hchunks, l.splits, hidden, rows, partials, l.ld_part, yg, ldy,
-          y_dtype);
-    else
-      prefill_down_kernel<false><<<down_grid, kThreads, kSmemBytes, stream>>>(
-          tm_records, tm_abuf, header, unions, l.n_hchunks, l.splits, hidden, rows, partials, l.ld_part, yg, ldy,
-          y_dtype);
-    if (!launch_ok()) return QCC_ERR_CUDA;
-    if (l.splits > 1) {
-      const int64_t total = static_cast<int64_t>(rows) * hidden;
-      const int grid = static_cast<int>(std::min<int64_t>(4 * info.num_sms, (total + 255) / 256));
-      prefill_reduce_kernel<<<grid, 256, 0, stream>>>(partials, l.ld_part, l.splits, rows, hidden, yg, ldy, y_dtype);
-      if (!launch_ok()) return QCC_ERR_CUDA;
-    }
+    // Every CTA must be resident at once (grid barrier, cross-CTA flags).
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(l.grid));
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = kSmemBytes;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    void* kargs[] = {&tm_records, &tm_x, &tm_abuf, &args};
+    if (!cuda_ok(cudaLaunchKernelExC(&cfg, kernel, kargs))) return QCC_ERR_CUDA;
   }
   return QCC_OK;
 }
