@@ -227,18 +227,21 @@ QCC_API int qcc_build_union(const int32_t* ids, int64_t ld_ids, int batch, int k
  * (resident_out), and gives every miss the least recently used cache slot
  * this step does not use -- empty slots first, ties by the held record's id,
  * the eviction order of reference runtime/temporal.py:57-75 -- updating
- * slot_of, cache_owner and cache_last_use in place (miss_slot_out: the slots,
- * miss_src_out: the records' cold_index entries).  counts_out (device int32
- * [6]): resident, misses served, cache hits, evicted, hot hits, 1 if misses
- * exceeded the free slots.  capacity <= 8192, n_records and step < 2^24 - 1.
+ * slot_of, cache_owner, cache_last_use and lru_order in place (miss_slot_out:
+ * the slots, miss_src_out: the records' cold_index entries).  lru_order
+ * [capacity] lists the cache slots from least to most recently used;
+ * initialise it to 0 .. capacity - 1 (with cache_owner = -1).  counts_out
+ * (device int32 [6]): resident, misses served, cache hits, evicted, hot hits,
+ * 1 if misses exceeded the free slots.  k <= 16384, capacity <= 8192,
+ * n_records and step < 2^24 - 1.
  * One CTA; no host round trip.  The reference stages whole layers
  * synchronously (integration/freetoken_qcc/low_vram/staging.py:43-67) and
  * keeps its LRU only as a host-side simulation.
  */
 QCC_API int qcc_cache_resolve(const int32_t* ids, int k, const int32_t* k_dev, int32_t* slot_of, int n_records,
-                              int n_hot, int32_t* cache_owner, int32_t* cache_last_use, int capacity,
-                              const int32_t* cold_index, int step, int32_t* resident_out, int32_t* miss_slot_out,
-                              int32_t* miss_src_out, int32_t* counts_out, cudaStream_t stream);
+                              int n_hot, int32_t* cache_owner, int32_t* cache_last_use, int32_t* lru_order,
+                              int capacity, const int32_t* cold_index, int step, int32_t* resident_out,
+                              int32_t* miss_slot_out, int32_t* miss_src_out, int32_t* counts_out, cudaStream_t stream);
 
 /*
  * Copies records src_index[i] of a host store (page-locked host memory, read

@@ -51,7 +51,7 @@ SIGNATURES = {
                                  _c_void_p, _c_void_p, _c_void_p]),
     "qcc_cast_f32": (_c_int, [_c_void_p, _c_void_p, _c_int64, _c_int, _c_void_p]),
     "qcc_cache_resolve": (_c_int, [_c_void_p, _c_int, _c_void_p, _c_void_p, _c_int, _c_int, _c_void_p, _c_void_p,
-                                   _c_int, _c_void_p, _c_int, _c_void_p, _c_void_p, _c_void_p, _c_void_p,
+                                   _c_void_p, _c_int, _c_void_p, _c_int, _c_void_p, _c_void_p, _c_void_p, _c_void_p,
                                    _c_void_p]),
     "qcc_gather_records": (_c_int, [_c_void_p, _c_int64, _c_void_p, _c_void_p, _c_void_p, _c_int, _c_void_p,
                                     _c_void_p]),

@@ -8,9 +8,10 @@
 //   qcc_cache_resolve (one CTA) splits the step's sorted ids into resident
 //   ones (hot records and cache hits: their resident-array slots) and misses;
 //   each miss takes the least recently used cache slot that the step does not
-//   use (empty slots first; among equal last use the record with the lower id
-//   goes first -- the eviction order of the reference's OrderedDict LRU,
-//   runtime/temporal.py:57-75), and the slot table is updated in place.
+//   use (empty slots first; among slots last used by the same step the record
+//   with the lower id goes first -- the eviction order of the reference's
+//   OrderedDict LRU, runtime/temporal.py:57-75), keeping the slots in an LRU
+//   list on the device, and the slot table is updated in place.
 //
 //   qcc_gather_records copies the missed records from the pinned host store
 //   (read in place over PCIe through the unified address space) into their
@@ -32,33 +33,49 @@ namespace {
 
 constexpr int kResolveThreads = 1024;
 constexpr int kMaxCapacity = 8192;
-constexpr unsigned long long kActiveKey = ~0ull;
+constexpr int kMaxIds = 16384;
 
 // counts_out: [0] resident, [1] misses served, [2] cache hits, [3] evicted,
 //             [4] hot hits, [5] 1 if misses exceeded the free slots
+//
+// The cache slots are kept in an LRU list, lru[0] least recently used.  One
+// step: classify the ids (hot / hit / miss) in id order; stable-partition the
+// list into the slots this step does not use and the ones it hits; the
+// misses take the first unused slots (evicting their records); the new list
+// is the remaining unused slots followed by every slot the step used, in id
+// order.  This is the order the reference's OrderedDict reaches by moving
+// hits and appending misses id by id (runtime/temporal.py:63-73): empty
+// slots never used stay at the front in slot order.
 __global__ void __launch_bounds__(kResolveThreads, 1)
     cache_resolve_kernel(const int32_t* __restrict__ ids, int k, const int32_t* __restrict__ k_dev,
                          int32_t* __restrict__ slot_of, int n_records, int n_hot, int32_t* __restrict__ owner,
-                         int32_t* __restrict__ last_use, int capacity, int sort_n, const int32_t* __restrict__ cold_index,
-                         int step, int32_t* __restrict__ resident_out, int32_t* __restrict__ miss_slot_out,
-                         int32_t* __restrict__ miss_src_out, int32_t* __restrict__ counts_out) {
+                         int32_t* __restrict__ last_use, int32_t* __restrict__ lru, int capacity,
+                         const int32_t* __restrict__ cold_index, int step, int32_t* __restrict__ resident_out,
+                         int32_t* __restrict__ miss_slot_out, int32_t* __restrict__ miss_src_out,
+                         int32_t* __restrict__ counts_out) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  unsigned long long* keys = reinterpret_cast<unsigned long long*>(smem_raw);    // [sort_n]
-  int32_t* miss_ids = reinterpret_cast<int32_t*>(keys + sort_n);                 // [capacity]
-  uint8_t* active = reinterpret_cast<uint8_t*>(miss_ids + capacity);            // [capacity]
+  int32_t* ring = reinterpret_cast<int32_t*>(smem_raw);   // [capacity] LRU order at the start of the step
+  int32_t* unused = ring + capacity;                       // [capacity] slots the step does not use, in order
+  int32_t* miss_ids = unused + capacity;                   // [capacity] missed ids, in id order
+  int32_t* cls = miss_ids + capacity;                      // [kMaxIds] per id: slot >= 0, -1 miss, -2 invalid
+  uint8_t* active = reinterpret_cast<uint8_t*>(cls + kMaxIds);  // [capacity]
   __shared__ int scratch[64];
-  __shared__ int s_cnt[4];  // cache hits, hot hits, evicted
+  __shared__ int s_cnt[3];  // cache hits, hot hits, evicted
 
   const int tid = threadIdx.x;
   const int nthreads = blockDim.x;
   int n = k;
   if (k_dev != nullptr) n = min(n, max(0, __ldg(k_dev)));
+  n = min(n, kMaxIds);
 
-  for (int c = tid; c < capacity; c += nthreads) active[c] = 0;
-  if (tid < 4) s_cnt[tid] = 0;
+  for (int c = tid; c < capacity; c += nthreads) {
+    active[c] = 0;
+    ring[c] = lru[c];
+  }
+  if (tid < 3) s_cnt[tid] = 0;
   __syncthreads();
 
-  // 1. Classify in id order: resident (hot or cache hit) or miss.
+  // 1. Classify in id order.  Contiguous chunk of ids per thread.
   const int chunk = (n + nthreads - 1) / nthreads;
   const int lo = min(n, tid * chunk);
   const int hi = min(n, lo + chunk);
@@ -66,6 +83,7 @@ __global__ void __launch_bounds__(kResolveThreads, 1)
   for (int i = lo; i < hi; ++i) {
     const int32_t id = ids[i];
     const int32_t s = (id >= 0 && id < n_records) ? slot_of[id] : -2;
+    cls[i] = s;
     if (s >= 0) {
       ++n_res;
       if (s < n_hot) {
@@ -82,53 +100,39 @@ __global__ void __launch_bounds__(kResolveThreads, 1)
   if (hot) atomicAdd(&s_cnt[1], hot);
   int total_res, total_miss;
   int res_pos = block_exclusive_scan(n_res, scratch, &total_res);
-  int miss_pos = block_exclusive_scan(n_miss, scratch, &total_miss);
+  const int miss_base = block_exclusive_scan(n_miss, scratch, &total_miss);
+  int miss_pos = miss_base;
   for (int i = lo; i < hi; ++i) {
-    const int32_t id = ids[i];
-    const int32_t s = (id >= 0 && id < n_records) ? slot_of[id] : -2;
+    const int32_t s = cls[i];
     if (s >= 0) {
       resident_out[res_pos++] = s;
       if (s >= n_hot) last_use[s - n_hot] = step;
     } else if (s == -1) {
-      if (miss_pos < capacity) miss_ids[miss_pos] = id;
+      if (miss_pos < capacity) miss_ids[miss_pos] = ids[i];
       ++miss_pos;
     }
   }
-  __syncthreads();
+  __syncthreads();  // active[] complete
 
-  // 2. Eviction order of the slots this step does not use: empty slots first,
-  //    then by last use, then by the held record's id.
-  for (int c = tid; c < sort_n; c += nthreads) {
-    unsigned long long key = kActiveKey;
-    if (c < capacity && !active[c])
-      key = (static_cast<unsigned long long>(last_use[c] + 1) << 40) |
-            (static_cast<unsigned long long>(owner[c] + 1) << 16) | static_cast<unsigned long long>(c);
-    keys[c] = key;
+  // 2. Slots the step does not use, in LRU order.
+  const int cchunk = (capacity + nthreads - 1) / nthreads;
+  const int clo = min(capacity, tid * cchunk);
+  const int chi = min(capacity, clo + cchunk);
+  int n_unused = 0;
+  for (int p = clo; p < chi; ++p) n_unused += !active[ring[p]];
+  int total_unused;
+  int up = block_exclusive_scan(n_unused, scratch, &total_unused);
+  for (int p = clo; p < chi; ++p) {
+    const int c = ring[p];
+    if (!active[c]) unused[up++] = c;
   }
   __syncthreads();
-  for (int size = 2; size <= sort_n; size <<= 1) {  // bitonic sort, ascending
-    for (int stride = size >> 1; stride > 0; stride >>= 1) {
-      for (int i = tid; i < sort_n / 2; i += nthreads) {
-        const int a = 2 * stride * (i / stride) + (i % stride);
-        const int b = a + stride;
-        const bool up = ((a & size) == 0);
-        const unsigned long long ka = keys[a], kb = keys[b];
-        if ((ka > kb) == up) {
-          keys[a] = kb;
-          keys[b] = ka;
-        }
-      }
-      __syncthreads();
-    }
-  }
 
-  // 3. Miss i takes the i-th slot of that order.
-  const int served = min(total_miss, capacity);
+  // 3. Miss i takes the i-th unused slot.
+  const int served = min(total_miss, total_unused);
   int evicted = 0;
   for (int i = tid; i < served; i += nthreads) {
-    const unsigned long long key = keys[i];
-    if (key == kActiveKey) continue;  // more misses than free slots: left unserved
-    const int c = static_cast<int>(key & 0xFFFFull);
+    const int c = unused[i];
     const int32_t old = owner[c];
     if (old >= 0) {
       slot_of[old] = -1;
@@ -142,16 +146,41 @@ __global__ void __launch_bounds__(kResolveThreads, 1)
     miss_src_out[i] = cold_index[id];
   }
   if (evicted) atomicAdd(&s_cnt[2], evicted);
+
+  // 4. New order: the unused slots not taken, then the slots this step used in id order.
+  const int keep = total_unused - served;
+  for (int i = served + tid; i < total_unused; i += nthreads) lru[i - served] = unused[i];
+  int n_used = 0;
+  int mp = miss_base;
+  for (int i = lo; i < hi; ++i) {
+    const int32_t s = cls[i];
+    if (s >= n_hot) {
+      ++n_used;
+    } else if (s == -1) {
+      n_used += mp < served;
+      ++mp;
+    }
+  }
+  int total_used;
+  int pos = block_exclusive_scan(n_used, scratch, &total_used);
+  mp = miss_base;
+  for (int i = lo; i < hi; ++i) {
+    const int32_t s = cls[i];
+    if (s >= n_hot) {
+      lru[keep + pos++] = s - n_hot;
+    } else if (s == -1) {
+      if (mp < served) lru[keep + pos++] = unused[mp];
+      ++mp;
+    }
+  }
   __syncthreads();
   if (tid == 0) {
-    int ok_misses = served;
-    while (ok_misses > 0 && keys[ok_misses - 1] == kActiveKey) --ok_misses;
     counts_out[0] = total_res;
-    counts_out[1] = ok_misses;
+    counts_out[1] = served;
     counts_out[2] = s_cnt[0];
     counts_out[3] = s_cnt[2];
     counts_out[4] = s_cnt[1];
-    counts_out[5] = ok_misses < total_miss ? 1 : 0;
+    counts_out[5] = served < total_miss ? 1 : 0;
   }
 }
 
@@ -189,34 +218,29 @@ __global__ void __launch_bounds__(512)
   }
 }
 
-int pow2_at_least(int v) {
-  int p = 1;
-  while (p < v) p <<= 1;
-  return p;
-}
-
 }  // namespace
 }  // namespace qcc
 
 extern "C" int qcc_cache_resolve(const int32_t* ids, int k, const int32_t* k_dev, int32_t* slot_of, int n_records,
-                                 int n_hot, int32_t* cache_owner, int32_t* cache_last_use, int capacity,
-                                 const int32_t* cold_index, int step, int32_t* resident_out, int32_t* miss_slot_out,
-                                 int32_t* miss_src_out, int32_t* counts_out, cudaStream_t stream) {
-  if (k < 0 || n_records < 0 || n_hot < 0 || capacity < 1 || capacity > qcc::kMaxCapacity) return QCC_ERR_SHAPE;
+                                 int n_hot, int32_t* cache_owner, int32_t* cache_last_use, int32_t* lru_order,
+                                 int capacity, const int32_t* cold_index, int step, int32_t* resident_out,
+                                 int32_t* miss_slot_out, int32_t* miss_src_out, int32_t* counts_out,
+                                 cudaStream_t stream) {
+  if (k < 0 || k > qcc::kMaxIds || n_records < 0 || n_hot < 0 || capacity < 1 || capacity > qcc::kMaxCapacity)
+    return QCC_ERR_SHAPE;
   if (n_records >= (1 << 24) - 1 || step < 0 || step >= (1 << 24) - 1) return QCC_ERR_UNSUPPORTED;
-  if (slot_of == nullptr || cache_owner == nullptr || cache_last_use == nullptr || cold_index == nullptr ||
-      counts_out == nullptr ||
+  if (slot_of == nullptr || cache_owner == nullptr || cache_last_use == nullptr || lru_order == nullptr ||
+      cold_index == nullptr || counts_out == nullptr ||
       (k > 0 && (ids == nullptr || resident_out == nullptr || miss_slot_out == nullptr || miss_src_out == nullptr)))
     return QCC_ERR_INVALID_ARGUMENT;
   int device = 0;
   if (!qcc::cuda_ok(cudaGetDevice(&device))) return QCC_ERR_CUDA;
-  const int sort_n = qcc::pow2_at_least(capacity);
-  const size_t smem = static_cast<size_t>(sort_n) * 8 + static_cast<size_t>(capacity) * 5 + 16;
+  const size_t smem = static_cast<size_t>(capacity) * 13 + static_cast<size_t>(qcc::kMaxIds) * 4 + 16;
   if (!qcc::ensure_max_dynamic_smem(reinterpret_cast<const void*>(qcc::cache_resolve_kernel), device))
     return QCC_ERR_CUDA;
   qcc::clear_stale_error();
   qcc::cache_resolve_kernel<<<1, qcc::kResolveThreads, smem, stream>>>(
-      ids, k, k_dev, slot_of, n_records, n_hot, cache_owner, cache_last_use, capacity, sort_n, cold_index, step,
+      ids, k, k_dev, slot_of, n_records, n_hot, cache_owner, cache_last_use, lru_order, capacity, cold_index, step,
       resident_out, miss_slot_out, miss_src_out, counts_out);
   if (!qcc::launch_ok()) return QCC_ERR_CUDA;
   return QCC_OK;

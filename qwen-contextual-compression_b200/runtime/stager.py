@@ -9,7 +9,7 @@ keeps:
 * an HBM resident array: the always-resident ("hot") records in slots
   [0, n_hot) and ``capacity`` cache slots after them;
 * the remaining ("cold") records in a pinned host store;
-* a device slot table and LRU state updated by ``qcc_cache_resolve``.
+* a device slot table and LRU list updated by ``qcc_cache_resolve``.
 
 Per decode step (all device-side, no host round trip): resolve the step's
 sorted ids into resident slots and misses; on a side stream copy the missed
@@ -61,6 +61,7 @@ class HostOffloadLayer:
         self.cold_index = cold_index.to(device)
         self.owner = torch.full((capacity,), -1, dtype=torch.int32, device=device)
         self.last_use = torch.full((capacity,), -1, dtype=torch.int32, device=device)
+        self.lru_order = torch.arange(capacity, dtype=torch.int32, device=device)  # least recently used first
         self.resident_ids = torch.empty(max(1, max_k), dtype=torch.int32, device=device)
         self.miss_slot = torch.empty(max(1, max_k), dtype=torch.int32, device=device)
         self.miss_src = torch.empty(max(1, max_k), dtype=torch.int32, device=device)
@@ -92,7 +93,8 @@ class HostOffloadLayer:
         stream = torch.cuda.current_stream(self.device)
         k = ids.numel()
         _lib.check(lib.qcc_cache_resolve(ids.data_ptr(), k, None, self.slot_of.data_ptr(), self.n_records,
-                                         self.n_hot, self.owner.data_ptr(), self.last_use.data_ptr(), self.capacity,
+                                         self.n_hot, self.owner.data_ptr(), self.last_use.data_ptr(),
+                                         self.lru_order.data_ptr(), self.capacity,
                                          self.cold_index.data_ptr(), self.step, self.resident_ids.data_ptr(),
                                          self.miss_slot.data_ptr(), self.miss_src.data_ptr(),
                                          self.counts.data_ptr(), stream.cuda_stream), "qcc_cache_resolve")
