@@ -8,14 +8,15 @@
 // ids (three gathers and three GEMMs per tile).
 //
 // A call runs groups of up to four tiles (512 tokens); a group is two launches:
-//  plan     one CTA: per-block tile masks from the per-tile block lists; the
-//           gate/up work units (a block with one or two of its tiles) with the
-//           prefix of their costs; each tile's ascending block list.
+//  plan     one CTA: per-block tile masks from the per-tile block lists; each
+//           tile's ascending block list; the gate/up work units (a tile with
+//           a pair of its blocks) with the prefix of their costs; every CTA's
+//           stream-K ranges.
 //  prefill  one persistent CTA per SM (cooperative launch), two phases split by
 //           a grid barrier:
-//   1. gate/up: per unit, A[tok, 64b .. 64b+63] = silu(X G_b^T) * (X U_b^T) for
-//      the unit's tiles: M = 128 tokens, N = 128 (64 gate + 64 up records),
-//      K = hidden in chunks of 64.
+//   1. gate/up: per unit (a tile and one or two of its blocks),
+//      A[tok, 64b .. 64b+63] = silu(X G_b^T) * (X U_b^T): M = 128 tokens,
+//      N = 128 per block (64 gate + 64 up records), K = hidden in chunks of 64.
 //   2. down: per unit (tile t, 256 hidden outputs), y = A[tile, blocks] D[blocks, h]:
 //      M = 128 tokens, N = 256, K = 64 records per block of the tile.
 //  Both phases are balanced stream-K style: the cost-weighted sequence of
@@ -70,7 +71,7 @@ constexpr uint32_t kSmemBytes = kStages * kStageBytes + kControlBytes + 1024;  /
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kAccCols = 256;        // one accumulator buffer
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
-constexpr int kMaxBlocks = 1 << 16;
+constexpr int kMaxBlocks = 1 << 15;        // block ids fit the 15-bit fields of a unit word
 constexpr int kMaxDownUnits = 512;        // tiles x 256-wide hidden ranges (hidden <= 32768)
 constexpr size_t kSlotFloats = 128 * 256; // one CTA's partial accumulators
 constexpr int kMaxContrib = 16;           // CTAs that may hand partial sums to one unit's finishing CTA
@@ -219,14 +220,20 @@ __device__ __forceinline__ uint32_t pack2(float a, float b) {
   }
 }
 
-__device__ __forceinline__ int unit_tiles(int unit) { return (unit & 0xF) == 0xF ? 1 : 2; }
+// Gate/up unit word: tile << 30 | second block << 15 | first block (second
+// block 0x7FFF: none).  A unit is one 128-token tile against the gate and up
+// rows of one or two of its blocks (MMA N = 128 per block).
+constexpr int kNoBlock = 0x7FFF;
+__device__ __forceinline__ int unit_tile(int unit) { return static_cast<int>(static_cast<uint32_t>(unit) >> 30); }
+__device__ __forceinline__ int unit_block(int unit, int j) { return j == 0 ? unit & 0x7FFF : (unit >> 15) & 0x7FFF; }
+__device__ __forceinline__ int unit_blocks(int unit) { return ((unit >> 15) & 0x7FFF) == kNoBlock ? 1 : 2; }
 
 // ---------------------------------------------------------------------------
 // Stream-K ranges.
 // ---------------------------------------------------------------------------
 
 // Phase 1: (unit, chunk) at cost position p.  A chunk of a unit costs its
-// tiles + 1 (one 16 KB box of x per tile plus 16 KB of gate/up rows).
+// blocks + 1 (16 KB of gate/up rows per block plus one 16 KB box of x).
 __device__ void locate_gate_up(const int* units, const int* prefix, int n_units, int total, int64_t p, int* u,
                                int* k) {
   if (p >= total || n_units == 0) {
@@ -243,7 +250,7 @@ __device__ void locate_gate_up(const int* units, const int* prefix, int n_units,
       hi = mid - 1;
   }
   *u = lo;
-  *k = static_cast<int>((p - prefix[lo]) / (unit_tiles(units[lo]) + 1));
+  *k = static_cast<int>((p - prefix[lo]) / (unit_blocks(units[lo]) + 1));
 }
 
 // Phase 2: (unit, step) at position p; units without steps share their
@@ -323,7 +330,7 @@ __global__ void __launch_bounds__(kPlanThreads)
   __shared__ int s_fail;
   const int tid = threadIdx.x;
   const int n_words = (n_blocks + 3) / 4;
-  const int cap = min(2 * n_blocks, kPlanUnits);
+  const int cap = min(2 * n_blocks + 8, kPlanUnits);
   int* s_units = reinterpret_cast<int*>(words + n_words);
   int* s_prefix = s_units + cap;
   for (int i = tid; i < n_words; i += blockDim.x) words[i] = 0u;
@@ -351,35 +358,6 @@ __global__ void __launch_bounds__(kPlanThreads)
   const int chunk = (n_blocks + blockDim.x - 1) / blockDim.x;
   const int lo = min(n_blocks, tid * chunk);
   const int hi = min(n_blocks, lo + chunk);
-  int n_units = 0, cost = 0;
-  for (int i = lo; i < hi; ++i) {
-    const int c = __popc(mask[i]);
-    n_units += (c + 1) / 2;
-    cost += c + (c + 1) / 2;  // per unit: tiles + 1
-  }
-  int total_units, total_cost;
-  int pos = block_exclusive_scan(n_units, scratch, &total_units);
-  int run = block_exclusive_scan(cost, scratch, &total_cost) * n_chunks;
-  for (int i = lo; i < hi; ++i) {
-    const int m = mask[i];
-    int tl[kMaxTiles];
-    int c = 0;
-#pragma unroll
-    for (int t = 0; t < kMaxTiles; ++t)
-      if ((m >> t) & 1) tl[c++] = t;
-    for (int p = 0; p < c; p += 2) {
-      const bool two = p + 1 < c;
-      const int word = (i << 8) | (tl[p] << 4) | (two ? tl[p + 1] : 0xF);
-      units[pos] = word;
-      unit_prefix[pos] = run;
-      if (pos < cap) {
-        s_units[pos] = word;
-        s_prefix[pos] = run;
-      }
-      run += (two ? 3 : 2) * n_chunks;
-      ++pos;
-    }
-  }
   // Each tile's blocks in ascending order.
   for (int t = 0; t < n_tiles; ++t) {
     int cnt = 0;
@@ -390,6 +368,46 @@ __global__ void __launch_bounds__(kPlanThreads)
       if ((mask[i] >> t) & 1) tile_list[t * n_blocks + p++] = i;
     if (tid == 0) s_tile_count[t] = total;
   }
+  __syncthreads();  // tile lists (global) and counts visible to the block
+  // Gate/up units: each tile's blocks in pairs.  Order: pair i of every tile,
+  // then pair i + 1, so units sharing hot blocks run side by side; the cost
+  // prefix follows in closed form (a pair costs 3 per chunk, a single 2).
+  int n_pairs[kMaxTiles], odd[kMaxTiles];
+  int total_units = 0;
+#pragma unroll
+  for (int t = 0; t < kMaxTiles; ++t) {
+    const int c = t < n_tiles ? s_tile_count[t] : 0;
+    n_pairs[t] = (c + 1) / 2;
+    odd[t] = c & 1;
+    total_units += n_pairs[t];
+  }
+  for (int t = 0; t < n_tiles; ++t) {
+    for (int i = tid; i < n_pairs[t]; i += blockDim.x) {
+      int pos = 0, singles = 0;
+#pragma unroll
+      for (int t2 = 0; t2 < kMaxTiles; ++t2) {
+        pos += min(n_pairs[t2], i) + ((t2 < t && n_pairs[t2] > i) ? 1 : 0);
+        const int last = n_pairs[t2] - 1;  // index of t2's single, if it has one
+        singles += (odd[t2] && (last < i || (last == i && t2 < t))) ? 1 : 0;
+      }
+      const int b1 = tile_list[t * n_blocks + 2 * i];
+      const bool two = 2 * i + 1 < s_tile_count[t];
+      const int b2 = two ? tile_list[t * n_blocks + 2 * i + 1] : kNoBlock;
+      const int word = static_cast<int>((static_cast<uint32_t>(t) << 30) | (static_cast<uint32_t>(b2) << 15) |
+                                        static_cast<uint32_t>(b1));
+      const int run = (3 * pos - singles) * n_chunks;
+      units[pos] = word;
+      unit_prefix[pos] = run;
+      if (pos < cap) {
+        s_units[pos] = word;
+        s_prefix[pos] = run;
+      }
+    }
+  }
+  int total_singles = 0;
+#pragma unroll
+  for (int t = 0; t < kMaxTiles; ++t) total_singles += odd[t];
+  const int total_cost = 3 * total_units - total_singles;
   const int total1 = total_cost * n_chunks;
   if (tid == 0) {
     for (int t = 0; t < kMaxTiles; ++t) header[kHdrTileCount + t] = t < n_tiles ? s_tile_count[t] : 0;
@@ -546,17 +564,22 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int si = 0, u; !stop && (u = seg_unit(ctl->r, 0, si, n_units)) >= 0; ++si) {
       int ks, ke;
       if (!segment(u, ctl->r.lo_u[0], ctl->r.lo_k[0], ctl->r.hi_u[0], ctl->r.hi_k[0], a.n_chunks, &ks, &ke)) continue;
-      const int b = a.units[u] >> 8;
+      const int unit = a.units[u];
+      const int nb = unit_blocks(unit);
       for (int kc = ks; kc < ke; ++kc, ++it) {
         int ok = 1;
         if (lane == 0) {
           const int s = it % kStages;
           ok = wait_phase(&ctl->empty[s], ((it / kStages) & 1u) ^ 1u, abort_flag, status) ? 1 : 0;
           if (ok) {
-            uint8_t* st = smem + s * kStageBytes;
-            mbar_arrive_expect_tx(&ctl->full[s], kBox128);
-            tma_load_3d(st, &tm_records, kc * kChunk, 0, b * kBlock, &ctl->full[s]);
-            tma_load_3d(st + kBox64, &tm_records, kc * kChunk, 1, b * kBlock, &ctl->full[s]);
+            // B operand: gate and up rows of the unit's blocks, 128 rows per block.
+            uint8_t* st = smem + s * kStageBytes + kBox128;
+            mbar_arrive_expect_tx(&ctl->full[s], nb * kBox128);
+            for (int jb = 0; jb < nb; ++jb) {
+              const int b = unit_block(unit, jb);
+              tma_load_3d(st + jb * kBox128, &tm_records, kc * kChunk, 0, b * kBlock, &ctl->full[s]);
+              tma_load_3d(st + jb * kBox128 + kBox64, &tm_records, kc * kChunk, 1, b * kBlock, &ctl->full[s]);
+            }
           }
         }
         if (!__shfl_sync(0xffffffffu, ok, 0)) {
@@ -566,31 +589,30 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else if (warp == kActWarp && lane == 0) {
-    // Activation loader: the x boxes of the unit's tiles.
+    // Activation loader: the x box of the unit's tile (A operand).
     tma_prefetch_map(&tm_x);
     tma_prefetch_map(&tm_abuf);
     for (int si = 0, u; (u = seg_unit(ctl->r, 0, si, n_units)) >= 0 && !*abort_flag; ++si) {
       int ks, ke;
       if (!segment(u, ctl->r.lo_u[0], ctl->r.lo_k[0], ctl->r.hi_u[0], ctl->r.hi_k[0], a.n_chunks, &ks, &ke)) continue;
-      const int unit = a.units[u];
-      const int ta = (unit >> 4) & 0xF;
-      const int tb = unit & 0xF;
-      const int nt = unit_tiles(unit);
+      const int t = unit_tile(a.units[u]);
       for (int kc = ks; kc < ke; ++kc, ++it) {
         const int s = it % kStages;
         if (!wait_phase(&ctl->empty[s], ((it / kStages) & 1u) ^ 1u, abort_flag, status)) break;
         uint8_t* st = smem + s * kStageBytes;
-        mbar_arrive_expect_tx(&ctl->full[s], nt * kBox128);
-        tma_load_2d(st + kBox128, &tm_x, kc * kChunk, ta * kTile, &ctl->full[s]);
-        if (nt == 2) tma_load_2d(st + 2 * kBox128, &tm_x, kc * kChunk, tb * kTile, &ctl->full[s]);
+        mbar_arrive_expect_tx(&ctl->full[s], kBox128);
+        tma_load_2d(st, &tm_x, kc * kChunk, t * kTile, &ctl->full[s]);
       }
     }
   } else if (warp == 1 && lane == 0) {
-    constexpr uint32_t idesc = idesc_f16_f32(128, 128, kBf16, false, false);
+    // One MMA per 16-wide K step: M = 128 tokens, N = 128 per block (256 for a
+    // block pair -- the instruction rate, not the width, bounds tcgen05 here).
+    constexpr uint32_t idesc1 = idesc_f16_f32(128, 128, kBf16, false, false);
+    constexpr uint32_t idesc2 = idesc_f16_f32(128, 256, kBf16, false, false);
     for (int si = 0, u; (u = seg_unit(ctl->r, 0, si, n_units)) >= 0 && !*abort_flag; ++si) {
       int ks, ke;
       if (!segment(u, ctl->r.lo_u[0], ctl->r.lo_k[0], ctl->r.hi_u[0], ctl->r.hi_k[0], a.n_chunks, &ks, &ke)) continue;
-      const int nt = unit_tiles(a.units[u]);
+      const uint32_t idesc = unit_blocks(a.units[u]) == 2 ? idesc2 : idesc1;
       const uint32_t j = ut & 1u;
       if (!wait_phase(&ctl->acc_empty[j], ((ut >> 1) & 1u) ^ 1u, abort_flag, status)) break;
       tc_fence_after_sync();
@@ -604,13 +626,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tc_fence_after_sync();
         const uint32_t st = smem_addr(smem + s * kStageBytes);
-        const uint64_t b_desc = smem_desc_sw128(st, 16, 1024);
-        for (int i = 0; i < nt; ++i) {
-          const uint64_t a_desc = smem_desc_sw128(st + kBox128 + i * kBox128, 16, 1024);
+        const uint64_t a_desc = smem_desc_sw128(st, 16, 1024);            // x tile, K-major
+        const uint64_t b_desc = smem_desc_sw128(st + kBox128, 16, 1024);  // gate/up rows, K-major
 #pragma unroll
-          for (int kk = 0; kk < kChunk / 16; ++kk)
-            tc_mma_f16(d0 + i * 128u, a_desc + 2u * kk, b_desc + 2u * kk, idesc, (kc > ks || kk > 0) ? 1u : 0u);
-        }
+        for (int kk = 0; kk < kChunk / 16; ++kk)
+          tc_mma_f16(d0, a_desc + 2u * kk, b_desc + 2u * kk, idesc, (kc > ks || kk > 0) ? 1u : 0u);
         tc_commit(&ctl->empty[s]);
       }
       if (!ok) break;
@@ -625,8 +645,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       int ks, ke;
       if (!segment(u, ctl->r.lo_u[0], ctl->r.lo_k[0], ctl->r.hi_u[0], ctl->r.hi_k[0], a.n_chunks, &ks, &ke)) continue;
       const int unit = a.units[u];
-      const int b = unit >> 8;
-      const int nt = unit_tiles(unit);
+      const int t = unit_tile(unit);
+      const int nt = unit_blocks(unit);  // accumulator column groups of 128: one per block
       const uint32_t j = ut & 1u;
       if (!warp_wait_phase(&ctl->acc_full[j], (ut >> 1) & 1u, abort_flag, status)) break;
       tc_fence_after_sync();
@@ -652,7 +672,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (wait_others)
           warp_wait_flags(a.flags1, ctl->r.contrib[0], ctl->r.n_contrib[0], epoch, abort_flag, status);
         for (int i = 0; i < nt; ++i) {
-          const int t = i == 0 ? (unit >> 4) & 0xF : unit & 0xF;
+          const int b = unit_block(unit, i);
           uint16_t* dst = a.abuf + static_cast<int64_t>(t * kTile + row) * a.ld_abuf + static_cast<int64_t>(b) * kBlock;
 #pragma unroll 1
           for (int c = 0; c < 2; ++c) {
@@ -937,10 +957,10 @@ PrefillLayout prefill_layout(int64_t n_records, int num_sms) {
   l.grid = num_sms;
   l.npad = static_cast<int64_t>(l.n_blocks) * kBlock;
   size_t off = kHeaderBytes;
-  l.units = off;
-  off = round_up(off + 2 * static_cast<size_t>(l.n_blocks) * 4, 256);
+  l.units = off;  // at most one unit per two blocks of each tile, rounded up: 2 * n_blocks + 4
+  off = round_up(off + (2 * static_cast<size_t>(l.n_blocks) + 8) * 4, 256);
   l.prefix = off;
-  off = round_up(off + (2 * static_cast<size_t>(l.n_blocks) + 1) * 4, 256);
+  off = round_up(off + (2 * static_cast<size_t>(l.n_blocks) + 9) * 4, 256);
   l.tile_list = off;
   off = round_up(off + static_cast<size_t>(kMaxTiles) * l.n_blocks * 4, 256);
   l.ranges = off;
@@ -1036,7 +1056,8 @@ extern "C" int qcc_indexed_ffn_prefill(const void* x, int64_t ldx, int n_tokens,
       !ensure_max_dynamic_smem(kernel, device))
     return QCC_ERR_CUDA;
   const size_t plan_smem =
-      round_up(static_cast<size_t>(l.n_blocks), 4) + (2 * static_cast<size_t>(std::min(2 * l.n_blocks, kPlanUnits)) + 1) * 4;
+      round_up(static_cast<size_t>(l.n_blocks), 4) +
+      (2 * static_cast<size_t>(std::min(2 * l.n_blocks + 8, kPlanUnits)) + 1) * 4;
   const uint8_t* xb = static_cast<const uint8_t*>(x);
   uint8_t* yb = static_cast<uint8_t*>(y);
 
