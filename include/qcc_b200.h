@@ -257,6 +257,51 @@ QCC_API int qcc_gather_records(const void* host_store, int64_t record_bytes, con
                                const int32_t* dst_slot, const int32_t* count_dev, int max_count, void* packed,
                                cudaStream_t stream);
 
+/* ---------------------------------------------------------------------- */
+/* Cross-rank sum fused into the decode (intermediate-dimension shards)    */
+/* ---------------------------------------------------------------------- */
+
+#define QCC_IPC_HANDLE_BYTES 64
+
+/* Bytes of one rank's exchange buffer (a 256-byte header holding the
+ * buffer's launch counter, then three rotating slots of column sums for every
+ * rank) for world ranks, batch tokens and this hidden size. */
+QCC_API size_t qcc_exchange_bytes(int world, int batch, int hidden, int dtype);
+
+/* Setup-time helpers (these allocate / map, unlike every compute entry):
+ * an exchange buffer initialised for use (counter zero, every column-sum word
+ * the empty mark, the bits of -0.0f; synchronises the device), its CUDA IPC handle
+ * (QCC_IPC_HANDLE_BYTES bytes), and the mapping of another process's buffer
+ * from its handle. */
+QCC_API int qcc_exchange_alloc(size_t bytes, void** ptr);
+QCC_API int qcc_exchange_free(void* ptr);
+QCC_API int qcc_ipc_handle(void* ptr, void* handle);
+QCC_API int qcc_ipc_open(const void* handle, void** ptr);
+QCC_API int qcc_ipc_close(void* ptr);
+
+/*
+ * qcc_indexed_ffn_decode on this rank's record shard with the sum over the
+ * world ranks fused into its epilogue: y_out (on every rank) =
+ *   sum over ranks q in rank order of rank q's partial, + y_in.
+ * exchange: host array of the world ranks' exchange buffers (exchange[rank]
+ * is this rank's own; the others are peer mappings from qcc_ipc_open),
+ * each exchange_bytes large and initialised by qcc_exchange_alloc.  Every
+ * rank makes the same sequence of calls on its buffer (the buffer counts its
+ * launches; call e uses slot e % 3).  Each CTA stores its column sums into
+ * every rank's buffer with relaxed system-scope 16-byte stores over NVLink; the words themselves signal arrival (a reader waits, bounded,
+ * 2 s, until none is the empty mark, then marks them empty again), so there is
+ * no fence or flag round trip.  After a QCC_DEV_TIMEOUT the buffers must be
+ * reallocated.  Replaces the NCCL all-reduce plus fp32 cast that
+ * follow a sharded partial; the reference has no distributed path
+ * (integration/freetoken_qcc/low_vram/adapter.py:106-107 refuses TP != 1).
+ */
+QCC_API int qcc_indexed_ffn_decode_allreduce(const void* x, int64_t ldx, int batch, int hidden, const void* packed,
+                                             int64_t n_records, int dtype, const void* ids, int ids_dtype, int n_ids,
+                                             const int32_t* n_ids_dev, const uint8_t* token_mask, void* workspace,
+                                             size_t workspace_bytes, void* y_out, int64_t ldy, int y_dtype,
+                                             const float* y_in, int64_t ld_in, void* const* exchange,
+                                             size_t exchange_bytes, int world, int rank, cudaStream_t stream);
+
 /* Elementwise cast of n fp32 values to dtype (used after a cross-rank sum). */
 QCC_API int qcc_cast_f32(const float* src, void* dst, int64_t n, int dtype, cudaStream_t stream);
 

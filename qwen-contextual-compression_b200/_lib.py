@@ -55,6 +55,16 @@ SIGNATURES = {
                                    _c_void_p]),
     "qcc_gather_records": (_c_int, [_c_void_p, _c_int64, _c_void_p, _c_void_p, _c_void_p, _c_int, _c_void_p,
                                     _c_void_p]),
+    "qcc_exchange_bytes": (_c_size_t, [_c_int, _c_int, _c_int, _c_int]),
+    "qcc_exchange_alloc": (_c_int, [_c_size_t, ctypes.POINTER(_c_void_p)]),
+    "qcc_exchange_free": (_c_int, [_c_void_p]),
+    "qcc_ipc_handle": (_c_int, [_c_void_p, _c_void_p]),
+    "qcc_ipc_open": (_c_int, [_c_void_p, ctypes.POINTER(_c_void_p)]),
+    "qcc_ipc_close": (_c_int, [_c_void_p]),
+    "qcc_indexed_ffn_decode_allreduce": (_c_int, [_c_void_p, _c_int64, _c_int, _c_int, _c_void_p, _c_int64, _c_int,
+                                                  _c_void_p, _c_int, _c_int, _c_void_p, _c_void_p, _c_void_p,
+                                                  _c_size_t, _c_void_p, _c_int64, _c_int, _c_void_p, _c_int64,
+                                                  _c_void_p, _c_size_t, _c_int, _c_int, _c_void_p]),
     "qcc_prefill_workspace_bytes": (_c_size_t, [_c_int64, _c_int]),
     "qcc_prefill_workspace_status_offset": (_c_size_t, []),
     "qcc_indexed_ffn_prefill": (_c_int, [_c_void_p, _c_int64, _c_int, _c_int, _c_void_p, _c_int64, _c_int,

@@ -3,6 +3,8 @@
 
 #include <cuda_runtime.h>
 
+#include <cstring>
+
 #include <algorithm>
 #include <mutex>
 #include <set>
@@ -190,4 +192,63 @@ extern "C" int qcc_cast_f32(const float* src, void* dst, int64_t n, int dtype, c
   qcc::cast_f32_kernel<<<static_cast<unsigned>(blocks), threads, 0, stream>>>(src, dst, n, dtype);
   if (!qcc::launch_ok()) return QCC_ERR_CUDA;
   return QCC_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Cross-rank exchange buffers (setup time: these allocate and map memory).
+// ---------------------------------------------------------------------------
+
+namespace {
+__global__ void fill_u32_kernel(uint32_t* p, size_t n, uint32_t v) {
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x)
+    p[i] = v;
+}
+}  // namespace
+
+// The 256-byte header (launch counter) starts at zero, the column-sum words
+// after it as the empty mark (the bits of -0.0f).
+extern "C" int qcc_exchange_alloc(size_t bytes, void** ptr) {
+  if (ptr == nullptr || bytes <= 256 || bytes % 16 != 0) return QCC_ERR_INVALID_ARGUMENT;
+  *ptr = nullptr;
+  void* p = nullptr;
+  if (!qcc::cuda_ok(cudaMalloc(&p, bytes))) return QCC_ERR_CUDA;
+  qcc::clear_stale_error();
+  fill_u32_kernel<<<64, 256>>>(static_cast<uint32_t*>(p) + 64, (bytes - 256) / 4, 0x80000000u);
+  if (!qcc::launch_ok() || !qcc::cuda_ok(cudaMemset(p, 0, 256)) || !qcc::cuda_ok(cudaDeviceSynchronize())) {
+    cudaFree(p);
+    return QCC_ERR_CUDA;
+  }
+  *ptr = p;
+  return QCC_OK;
+}
+
+extern "C" int qcc_exchange_free(void* ptr) {
+  if (ptr == nullptr) return QCC_OK;
+  return qcc::cuda_ok(cudaFree(ptr)) ? QCC_OK : QCC_ERR_CUDA;
+}
+
+extern "C" int qcc_ipc_handle(void* ptr, void* handle) {
+  if (ptr == nullptr || handle == nullptr) return QCC_ERR_INVALID_ARGUMENT;
+  static_assert(sizeof(cudaIpcMemHandle_t) == QCC_IPC_HANDLE_BYTES, "IPC handle size");
+  cudaIpcMemHandle_t h;
+  if (!qcc::cuda_ok(cudaIpcGetMemHandle(&h, ptr))) return QCC_ERR_CUDA;
+  std::memcpy(handle, &h, sizeof(h));
+  return QCC_OK;
+}
+
+extern "C" int qcc_ipc_open(const void* handle, void** ptr) {
+  if (ptr == nullptr || handle == nullptr) return QCC_ERR_INVALID_ARGUMENT;
+  *ptr = nullptr;
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  void* p = nullptr;
+  if (!qcc::cuda_ok(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess))) return QCC_ERR_CUDA;
+  *ptr = p;
+  return QCC_OK;
+}
+
+extern "C" int qcc_ipc_close(void* ptr) {
+  if (ptr == nullptr) return QCC_OK;
+  return qcc::cuda_ok(cudaIpcCloseMemHandle(ptr)) ? QCC_OK : QCC_ERR_CUDA;
 }

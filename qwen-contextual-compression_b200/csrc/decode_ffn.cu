@@ -37,6 +37,42 @@ constexpr int kMaxGrid = 160;          // CTAs (one per SM) whose partial rows t
 constexpr int kMaxStages = 8;
 constexpr int kMaxThreads = 320;  // 10 warps; hidden 5120 = two 8-element slots per thread
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s bound on any barrier wait
+constexpr int kMaxRanks = 8;
+// Cross-rank exchange buffer: a 256-byte header whose first word counts the
+// launches that used this buffer, then column sums [3 slots][world]
+// [B * hidden_pad / 4] float4, every word initialised to the empty mark (the
+// bits of -0.0f).  A writer stores its sums (with -0.0 turned into +0.0); a
+// reader waits until no word of a sum is the empty mark, then marks it empty
+// again.  The data is its own flag: no fences, no separate flag round trip.
+// Launch e of a buffer uses slot e % 3.  A rank starts launch e + 3 only
+// after finishing launch e + 2, which needed every rank's launch-(e + 2)
+// sums, and each rank wrote those after its own launch e had ended: so every
+// owner has read and re-marked slot e % 3 before any rank writes it again.
+// The counter lives in the buffer, not in the per-stream workspace, so that
+// several layers (buffers) interleaved on one stream each step through the
+// three slots in turn.
+constexpr uint32_t kEmptyMark = 0x80000000u;
+constexpr int kXchgSlots = 3;
+constexpr int kXchgHeader = 256;
+
+// Stores and polls of exchange words: relaxed at system scope, so the store
+// reaches the peer's memory without a fence and every poll reads it anew.
+__device__ __forceinline__ void st_relaxed_sys(uint4* p, uint4 v) {
+  asm volatile("st.relaxed.sys.global.v4.u32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(v.x), "r"(v.y), "r"(v.z),
+               "r"(v.w)
+               : "memory");
+}
+__device__ __forceinline__ uint4 ld_relaxed_sys(const uint4* p) {
+  uint4 v;
+  asm volatile("ld.relaxed.sys.global.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p)
+               : "memory");
+  return v;
+}
+__device__ __forceinline__ bool has_empty_mark(uint4 w) {
+  return w.x == kEmptyMark || w.y == kEmptyMark || w.z == kEmptyMark || w.w == kEmptyMark;
+}
 
 struct DecodeArgs {
   const void* x;
@@ -67,6 +103,12 @@ struct DecodeArgs {
   int id_cap;        // capacity of the shared id cache (>= ids per CTA)
   int64_t ring_bytes;  // stages * record_bytes (16-byte multiple)
   int x_vec;           // x rows are 16-byte aligned with hidden % 8 == 0: vector loads
+  // Cross-rank sum (world > 1): each CTA's column sums go to every rank's
+  // exchange buffer; y is the sum over ranks in rank order.
+  int world;
+  int rank;
+  unsigned int* epoch;            // launch counter in this rank's exchange header (advanced by the last CTA)
+  uint8_t* xchg[kMaxRanks];       // column-sum slots of all ranks' exchange buffers, own included
 };
 
 __device__ __forceinline__ int64_t load_id(const DecodeArgs& a, int j) {
@@ -395,8 +437,11 @@ __global__ void __launch_bounds__(kMaxThreads, 1) indexed_ffn_decode_kernel(cons
   // 3. This CTA's slice of y: columns [blockIdx.x * per, ... + width).  Load
   //    the contiguous [grid][per] block into shared memory (coalesced, all
   //    loads in flight at once), then one warp per column sums the grid rows
-  //    in a fixed order (lane-strided, then a shuffle tree) and writes the
-  //    four outputs in the output dtype.
+  //    in a fixed order (lane-strided, then a shuffle tree).  One rank writes
+  //    the four outputs in the output dtype; with several ranks every CTA
+  //    first sends its column sums to all ranks (plain stores over NVLink into
+  //    their exchange buffers, then a release flag per rank), waits for the
+  //    other ranks' flags for the same slice, and adds the ranks in rank order.
   if (*s_flag) {
     const int c0 = blockIdx.x * per;
     const int width = max(0, min(nvec, c0 + per) - c0);
@@ -419,6 +464,9 @@ __global__ void __launch_bounds__(kMaxThreads, 1) indexed_ffn_decode_kernel(cons
         }
       }
       __syncthreads();
+      const bool multi = a.world > 1;
+      const unsigned int ep = multi ? *reinterpret_cast<volatile unsigned int*>(a.epoch) : 0u;
+      const int slot = static_cast<int>(ep % kXchgSlots);
       for (int col = warp; col < width; col += nwarps) {
         float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
         for (int row = lane; row < grid; row += 32) {
@@ -436,6 +484,57 @@ __global__ void __launch_bounds__(kMaxThreads, 1) indexed_ffn_decode_kernel(cons
           acc.w += __shfl_xor_sync(0xffffffffu, acc.w, off);
         }
         if (lane == 0) {
+          if (multi) {
+            // -0.0 is the empty mark; the sum it stands for is +0.0.
+            const uint4 w = make_uint4(__float_as_uint(acc.x) == kEmptyMark ? 0u : __float_as_uint(acc.x),
+                                       __float_as_uint(acc.y) == kEmptyMark ? 0u : __float_as_uint(acc.y),
+                                       __float_as_uint(acc.z) == kEmptyMark ? 0u : __float_as_uint(acc.z),
+                                       __float_as_uint(acc.w) == kEmptyMark ? 0u : __float_as_uint(acc.w));
+            const int64_t at = (static_cast<int64_t>(slot) * a.world + a.rank) * nvec + c0 + col;
+            for (int q = 0; q < a.world; ++q) st_relaxed_sys(reinterpret_cast<uint4*>(a.xchg[q]) + at, w);
+          } else {
+            const int e0 = (c0 + col) * 4;
+            const int b = e0 / seg;
+            const int h0 = e0 - b * seg;
+            const float vals[4] = {acc.x, acc.y, acc.z, acc.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+              if (h0 + e < a.hidden)
+                store_as(a.y_out, b * a.ldy + h0 + e, a.y_dtype,
+                         vals[e] + (a.y_in != nullptr ? __ldg(a.y_in + b * a.ld_in + h0 + e) : 0.f));
+          }
+        }
+      }
+      if (multi) {
+        // Sum over ranks in rank order, waiting (bounded) for each rank's words.
+        uint4* mine = reinterpret_cast<uint4*>(a.xchg[a.rank]);
+        for (int col = warp; col < width; col += nwarps) {
+          if (lane != 0) continue;
+          float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+          bool ok = true;
+          for (int q = 0; q < a.world; ++q) {
+            uint4* src = mine + (static_cast<int64_t>(slot) * a.world + q) * nvec + c0 + col;
+            uint4 w = ld_relaxed_sys(src);
+            if (has_empty_mark(w)) {
+              const uint64_t start = global_timer_ns();
+              while (true) {
+                w = ld_relaxed_sys(src);
+                if (!has_empty_mark(w)) break;
+                if (global_timer_ns() - start > kWaitLimitNs) {
+                  atomicOr(a.status, QCC_DEV_TIMEOUT);
+                  ok = false;
+                  break;
+                }
+              }
+            }
+            if (!ok) break;
+            acc.x += __uint_as_float(w.x);
+            acc.y += __uint_as_float(w.y);
+            acc.z += __uint_as_float(w.z);
+            acc.w += __uint_as_float(w.w);
+            *src = make_uint4(kEmptyMark, kEmptyMark, kEmptyMark, kEmptyMark);  // ready for launch e + 3
+          }
+          if (!ok) continue;
           const int e0 = (c0 + col) * 4;
           const int b = e0 / seg;
           const int h0 = e0 - b * seg;
@@ -456,6 +555,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1) indexed_ffn_decode_kernel(cons
     if (atomicAdd(a.depart, 1u) == gridDim.x - 1) {
       *a.arrive = 0u;
       *a.depart = 0u;
+      if (a.epoch != nullptr) *a.epoch += 1u;  // every CTA has read it in this launch
     }
   }
 }
@@ -591,8 +691,14 @@ int indexed_ffn_decode(const void* x, int64_t ldx, int batch, int hidden, const 
                        int dtype, const void* ids, int ids_dtype, int n_ids, const int32_t* n_ids_dev,
                        const uint8_t* token_mask, void* workspace, size_t workspace_bytes, void* y_out, int64_t ldy,
                        int y_dtype, const float* y_in, int64_t ld_in, void* activation_out, int64_t lda,
-                       cudaStream_t stream) {
+                       cudaStream_t stream, void* const* xchg, int world, int rank) {
   if (!valid_dtype(dtype) || !valid_dtype(y_dtype)) return QCC_ERR_DTYPE;
+  if (world < 1 || world > kMaxRanks || rank < 0 || rank >= world) return QCC_ERR_SHAPE;
+  if (world > 1) {
+    if (xchg == nullptr) return QCC_ERR_INVALID_ARGUMENT;
+    for (int q = 0; q < world; ++q)
+      if (xchg[q] == nullptr || !aligned16(xchg[q])) return QCC_ERR_INVALID_ARGUMENT;
+  }
   if (y_dtype != dtype && y_dtype != QCC_DTYPE_F32) return QCC_ERR_DTYPE;
   if (ids_dtype != QCC_INDEX_I32 && ids_dtype != QCC_INDEX_I64) return QCC_ERR_DTYPE;
   if (batch < 1 || hidden < 1 || n_records < 0 || n_ids < 0) return QCC_ERR_SHAPE;
@@ -633,7 +739,9 @@ int indexed_ffn_decode(const void* x, int64_t ldx, int batch, int hidden, const 
   // must be resident at once for the grid barrier, which the cooperative
   // launch guarantees.
   int64_t grid = std::min<int64_t>(info.num_sms, kMaxGrid);
-  if (n_ids_dev == nullptr) grid = std::min<int64_t>(grid, std::max(1, n_ids));
+  // Across ranks the grid (and with it every CTA's column slice) must be the
+  // same on every rank, whatever its share of the ids.
+  if (n_ids_dev == nullptr && world == 1) grid = std::min<int64_t>(grid, std::max(1, n_ids));
 
   DecodeArgs args;
   args.x = x;
@@ -665,6 +773,11 @@ int indexed_ffn_decode(const void* x, int64_t ldx, int batch, int hidden, const 
   args.id_cap = id_cap;
   args.ring_bytes = static_cast<int64_t>(shape.ring);
   args.x_vec = (hidden % 8 == 0) && aligned16(x) && ((ldx * dtype_bytes(dtype)) % 16 == 0);
+  args.world = world;
+  args.rank = rank;
+  args.epoch = world > 1 ? static_cast<unsigned int*>(xchg[rank]) : nullptr;
+  for (int q = 0; q < kMaxRanks; ++q)
+    args.xchg[q] = q < world && world > 1 ? static_cast<uint8_t*>(xchg[q]) + kXchgHeader : nullptr;
 
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(grid));
@@ -679,6 +792,12 @@ int indexed_ffn_decode(const void* x, int64_t ldx, int batch, int hidden, const 
   clear_stale_error();
   if (!cuda_ok(cudaLaunchKernelEx(&cfg, fn, args))) return QCC_ERR_CUDA;
   return QCC_OK;
+}
+
+size_t exchange_bytes(int world, int batch, int hidden, int dtype) {
+  if (world < 1 || world > kMaxRanks || batch < 1 || hidden < 1 || !valid_dtype(dtype)) return 0;
+  const size_t nvec = static_cast<size_t>(batch) * hidden_pad(hidden, dtype) / 4;
+  return kXchgHeader + static_cast<size_t>(kXchgSlots) * world * nvec * 16;
 }
 
 }  // namespace qcc
@@ -702,4 +821,22 @@ extern "C" int qcc_indexed_ffn_decode(const void* x, int64_t ldx, int batch, int
   return qcc::indexed_ffn_decode(x, ldx, batch, hidden, packed, n_records, dtype, ids, ids_dtype, n_ids, n_ids_dev,
                                  token_mask, workspace, workspace_bytes, y_out, ldy, y_dtype, y_in, ld_in,
                                  activation_out, lda, stream);
+}
+
+extern "C" size_t qcc_exchange_bytes(int world, int batch, int hidden, int dtype) {
+  return qcc::exchange_bytes(world, batch, hidden, dtype);
+}
+
+extern "C" int qcc_indexed_ffn_decode_allreduce(const void* x, int64_t ldx, int batch, int hidden, const void* packed,
+                                                int64_t n_records, int dtype, const void* ids, int ids_dtype,
+                                                int n_ids, const int32_t* n_ids_dev, const uint8_t* token_mask,
+                                                void* workspace, size_t workspace_bytes, void* y_out, int64_t ldy,
+                                                int y_dtype, const float* y_in, int64_t ld_in,
+                                                void* const* exchange, size_t exchange_bytes, int world, int rank,
+                                                cudaStream_t stream) {
+  if (world < 1 || world > 8 || rank < 0 || rank >= world) return QCC_ERR_SHAPE;
+  if (world > 1 && exchange_bytes < qcc::exchange_bytes(world, batch, hidden, dtype)) return QCC_ERR_WORKSPACE;
+  return qcc::indexed_ffn_decode(x, ldx, batch, hidden, packed, n_records, dtype, ids, ids_dtype, n_ids, n_ids_dev,
+                                 token_mask, workspace, workspace_bytes, y_out, ldy, y_dtype, y_in, ld_in, nullptr, 0,
+                                 stream, exchange, world, rank);
 }

@@ -114,7 +114,7 @@ class IndexedSparseFFN:
     def forward(self, x: torch.Tensor, ids: torch.Tensor, *, token_mask: torch.Tensor | None = None,
                 n_ids_dev: torch.Tensor | None = None, out: torch.Tensor | None = None,
                 out_dtype: torch.dtype | None = None, activation: torch.Tensor | None = None,
-                accumulate: torch.Tensor | None = None) -> torch.Tensor:
+                accumulate: torch.Tensor | None = None, exchange=None) -> torch.Tensor:
         """y [B, H] for x [B, H] (or [H] -> [H]) and the 1-D selected-id list ``ids``.
 
         token_mask: optional uint8 [len(ids)], bit b = token b uses record j.
@@ -122,6 +122,8 @@ class IndexedSparseFFN:
         out_dtype:  x.dtype (default) or torch.float32 (unrounded partial sums).
         activation: optional [B, len(ids)] tensor in x.dtype receiving a_j.
         accumulate: optional fp32 [B, H] added before the final rounding.
+        exchange:   optional cross-rank exchange (``sharded.PeerExchange``): y is
+                    then the sum of every rank's partial over this rank's shard.
         """
         squeeze = x.dim() == 1
         if squeeze:
@@ -158,6 +160,17 @@ class IndexedSparseFFN:
                 # after the kernel that reads it.
                 mask_ptr = torch.bitwise_right_shift(token_mask, start).data_ptr()
             acc_ptr = None if accumulate is None else accumulate.data_ptr() + start * acc_row
+            if exchange is not None:
+                if a_ptr is not None:
+                    raise ValueError("activation output is not available with a cross-rank exchange")
+                status = lib.qcc_indexed_ffn_decode_allreduce(
+                    x_ptr + start * x_row, x.stride(0), chunk, plan.hidden, plan.packed_ptr, plan.n_records,
+                    plan.code, ids.data_ptr(), plan.ids_code, n_ids, count_ptr, mask_ptr, ws.ptr, ws.nbytes,
+                    out_ptr + start * out_row, out.stride(0), plan.y_code, acc_ptr, acc_ld, exchange.pointers,
+                    exchange.nbytes, exchange.world, exchange.rank, stream)
+                if status:
+                    _lib.check(status, "qcc_indexed_ffn_decode_allreduce")
+                continue
             status = lib.qcc_indexed_ffn_decode(
                 x_ptr + start * x_row, x.stride(0), chunk, plan.hidden, plan.packed_ptr, plan.n_records, plan.code,
                 ids.data_ptr(), plan.ids_code, n_ids, count_ptr, mask_ptr, ws.ptr, ws.nbytes,

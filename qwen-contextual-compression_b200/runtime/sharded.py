@@ -3,10 +3,13 @@
 Rank r of P owns the contiguous records [r*N//P, (r+1)*N//P).  Every rank
 holds the same global selected ids (the selector is deterministic and
 replicated), keeps the ones inside its range, rebased (qcc_build_union, one
-small launch), runs the fused kernel with an fp32 partial output, and the P
-partials are summed with an NCCL all-reduce on the compute stream before a
-cast to the weight dtype.  Only y (hidden fp32 values per token, 20 KB at
-hidden 5120) crosses NVLink.  The reference has no distributed path
+small launch), and runs the fused kernel on them.  The sum over ranks is
+either fused into that kernel (``allreduce="fused"``, the default: each CTA
+stores its column sums into every rank's exchange buffer over NVLink and adds
+the ranks' sums in rank order -- no NCCL call, no extra launch) or an NCCL
+all-reduce of the fp32 partials followed by a cast (``allreduce="nccl"``).
+Only y (hidden fp32 values per token, 20 KB at hidden 5120) crosses NVLink.
+The reference has no distributed path
 (integration/freetoken_qcc/low_vram/adapter.py:106-107 refuses TP != 1).
 """
 from __future__ import annotations
@@ -26,15 +29,77 @@ def shard_range(intermediate: int, world: int, rank: int) -> tuple[int, int]:
     return intermediate * rank // world, intermediate * (rank + 1) // world
 
 
+class PeerExchange:
+    """The exchange buffers of all ranks of a process group, mapped into this process.
+
+    Each rank allocates one buffer (``qcc_exchange_bytes``), shares its CUDA
+    IPC handle through the process group, and maps the other ranks' buffers.
+    Collective: every rank of the group constructs it.
+    """
+
+    def __init__(self, group, device: torch.device, batch: int, hidden: int, dtype: torch.dtype):
+        import ctypes
+        import torch.distributed as dist
+
+        lib = _lib.library()
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.nbytes = int(lib.qcc_exchange_bytes(self.world, batch, hidden, _lib.dtype_code(dtype)))
+        if self.nbytes == 0:
+            raise ValueError("qcc_exchange_bytes rejected the world / batch / hidden")
+        with torch.cuda.device(device):
+            local = ctypes.c_void_p()
+            _lib.check(lib.qcc_exchange_alloc(self.nbytes, ctypes.byref(local)), "qcc_exchange_alloc")
+            self._local = local.value
+            handle = (ctypes.c_uint8 * 64)()
+            _lib.check(lib.qcc_ipc_handle(self._local, handle), "qcc_ipc_handle")
+            mine = torch.tensor(list(handle), dtype=torch.uint8, device=device)
+            gathered = torch.empty(self.world * 64, dtype=torch.uint8, device=device)
+            dist.all_gather_into_tensor(gathered, mine, group=group)
+            rows = gathered.view(self.world, 64).cpu()
+            self._opened = []
+            ptrs = []
+            for q in range(self.world):
+                if q == self.rank:
+                    ptrs.append(self._local)
+                    continue
+                h = (ctypes.c_uint8 * 64)(*rows[q].tolist())
+                p = ctypes.c_void_p()
+                _lib.check(lib.qcc_ipc_open(h, ctypes.byref(p)), "qcc_ipc_open")
+                self._opened.append(p.value)
+                ptrs.append(p.value)
+        self.pointers = (ctypes.c_void_p * self.world)(*ptrs)
+        self.device = device
+
+    def close(self) -> None:
+        lib = _lib.library()
+        with torch.cuda.device(self.device):
+            for p in self._opened:
+                lib.qcc_ipc_close(p)
+            self._opened = []
+            if self._local:
+                lib.qcc_exchange_free(self._local)
+                self._local = None
+
+
 class ShardedIndexedFFN:
     """One rank's slice of an indexed sparse FFN layer plus the cross-rank sum."""
 
-    def __init__(self, weights: PackedFFNWeights, group=None):
+    def __init__(self, weights: PackedFFNWeights, group=None, allreduce: str = "fused",
+                 exchange: PeerExchange | None = None):
+        if allreduce not in ("fused", "nccl"):
+            raise ValueError("allreduce must be 'fused' or 'nccl'")
         self.weights = weights
         self.engine = IndexedSparseFFN(weights)
         self.group = group
         self.begin = weights.record_offset
         self.end = weights.record_offset + weights.n_records
+        self.allreduce = allreduce if group is not None else "nccl"
+        self._own_exchange = False
+        self.exchange = exchange
+        if self.allreduce == "fused" and self.exchange is None:
+            self.exchange = PeerExchange(group, weights.device, self.engine.max_batch, weights.hidden, weights.dtype)
+            self._own_exchange = True
 
     def partial(self, x: torch.Tensor, ids: torch.Tensor) -> torch.Tensor:
         """fp32 partial y of this rank's records; ids are global ([K] shared or [B, K] per token)."""
@@ -52,6 +117,15 @@ class ShardedIndexedFFN:
         return self.forward(x, ids)
 
     def forward(self, x: torch.Tensor, ids: torch.Tensor) -> torch.Tensor:
+        if self.allreduce == "fused":
+            rows = ids if ids.ndim == 2 else ids.unsqueeze(0)
+            if rows.dtype != torch.int32:
+                rows = rows.to(torch.int32)
+            local, mask, count = build_union(rows.contiguous(), self.begin, self.end)
+            x2 = x if x.ndim == 2 else x.unsqueeze(0)
+            y = self.engine(x2, local, token_mask=mask if ids.ndim == 2 else None, n_ids_dev=count,
+                            exchange=self.exchange)
+            return y if x.ndim == 2 else y.squeeze(0)
         y32 = self.partial(x, ids)
         if self.group is not None:
             torch.distributed.all_reduce(y32, group=self.group)
@@ -62,4 +136,7 @@ class ShardedIndexedFFN:
         return out if x.ndim == 2 else out.squeeze(0)
 
     def close(self) -> None:
+        if self._own_exchange and self.exchange is not None:
+            self.exchange.close()
+        self.exchange = None
         self.engine = None

@@ -1,9 +1,12 @@
-"""Intermediate-dimension sharding across real GPUs (NCCL), when at least two are visible.
+"""Intermediate-dimension sharding across real GPUs, when at least two are visible.
 
-Each rank packs only its record range, keeps its part of the global ids and
-adds its fp32 partial through an NCCL all-reduce; the result must match the
-single-GPU kernel and the oracle.  Runs as spawned child processes with a
-short process-group timeout; skipped on machines with one GPU.
+Each rank packs only its record range and keeps its part of the global ids.
+The cross-rank sum is either fused into the decode kernel (exchange buffers
+over NVLink, CUDA IPC) or an NCCL all-reduce of fp32 partials; both must match
+the oracle, the fused sum must be identical on every rank (rank-ordered) and
+stable across repeated calls (rotating exchange slots).  Runs as spawned
+child processes with a short process-group timeout, NVLS off; skipped on
+machines with one GPU.
 """
 from __future__ import annotations
 
@@ -43,12 +46,26 @@ def _rank(rank: int, world: int, port: int, queue) -> None:
         hidden, n = 2048, 8192
         begin, end = shard_range(n, world, rank)
         layer = workloads.decode_layer(hidden=hidden, intermediate=n, device=device, seed=5, record_range=(begin, end))
-        ffn = ShardedIndexedFFN(PackedFFNWeights(layer.packed, hidden, end - begin, begin, n), group=dist.group.WORLD)
+        weights = PackedFFNWeights(layer.packed, hidden, end - begin, begin, n)
+        fused = ShardedIndexedFFN(weights, group=dist.group.WORLD, allreduce="fused")
+        nccl = ShardedIndexedFFN(weights, group=dist.group.WORLD, allreduce="nccl")
         k = workloads.retention_k(n, 0.25)
         ids = workloads.decode_ids(n, k, token=4).to(device)
         x = workloads.decode_x(hidden=hidden).to(device)
-        y = ffn(x, ids)
+        y = fused(x, ids)
+        y_nccl = nccl(x, ids)
+        ys = [fused(x, ids) for _ in range(50)]  # rotating exchange slots, graph-free loop
         torch.cuda.synchronize(device)
+        stable = all(torch.equal(y, yi) for yi in ys)
+        other = torch.empty_like(y)
+        dist.broadcast(other if rank else y.clone(), src=0)
+        if rank:
+            other_equal = torch.equal(other, y)
+        else:
+            other_equal = True
+        flags = torch.tensor([int(stable), int(other_equal)], device=device)
+        dist.all_reduce(flags, op=dist.ReduceOp.MIN)
+        fused.engine.check()
         # Gather the full layer on rank 0 for the oracle (small layer).
         parts = [torch.empty_like(layer.packed) if r != rank else layer.packed for r in range(world)]
         sizes = [shard_range(n, world, r) for r in range(world)]
@@ -61,8 +78,11 @@ def _rank(rank: int, world: int, port: int, queue) -> None:
             full = torch.cat(gathered).cpu()
             gate, up, down = full[:, :hidden], full[:, hidden:2 * hidden], full[:, 2 * hidden:].t()
             expected = offn.sparse_ffn_f64(x.cpu(), ids.cpu(), gate, up, down)
-            queue.put(offn.rel_l2(y.double().cpu().numpy(), expected))
+            queue.put((offn.rel_l2(y.double().cpu().numpy(), expected),
+                       offn.rel_l2(y_nccl.double().cpu().numpy(), expected), flags.tolist()))
         del parts
+        fused.close()
+        nccl.close()
     finally:
         dist.destroy_process_group()
 
@@ -75,8 +95,9 @@ def test_two_rank_sharded_layer_matches_oracle():
     procs = [ctx.Process(target=_rank, args=(r, 2, port, queue)) for r in range(2)]
     for p in procs:
         p.start()
-    err = queue.get(timeout=300)
+    err_fused, err_nccl, flags = queue.get(timeout=300)
     for p in procs:
         p.join(timeout=120)
         assert p.exitcode == 0
-    assert err <= 1e-2
+    assert err_fused <= 1e-2 and err_nccl <= 1e-2
+    assert flags == [1, 1], "fused sum differs between ranks or between repeated calls"
