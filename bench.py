@@ -23,9 +23,10 @@ K*3*H*2 + x + ids(int32) + y = 133,731,328 B.
                  cores, a bounded sample of tokens.
 
 N > 1 (torchrun, one process per GPU): the intermediate dimension is split
-into N contiguous record ranges; every rank holds the same global ids, keeps
-its range (qcc_build_union) and runs the fused kernel on it; the sum over
-ranks is fused into that kernel's epilogue (column sums stored into every
+into N contiguous record ranges; every rank holds the same global ascending
+ids and runs the fused kernel on them with its range (the kernel finds the
+run of ids inside the range and rebases them); the sum over ranks is fused
+into that kernel's epilogue (column sums stored into every
 rank's exchange buffer over NVLink, added in rank order), so y comes out in
 bf16 on every rank with no NCCL call.  Total work per step is fixed, so
 scaling is "strong".
@@ -477,7 +478,7 @@ def run_ours(args) -> None:
         exchange = PeerExchange(group, device, 1, HIDDEN, torch.bfloat16)
         engines = [ShardedIndexedFFN(PackedFFNWeights(l.packed, HIDDEN, end - begin, begin, INTERMEDIATE),
                                      group=group, allreduce="fused", exchange=exchange) for l in layers]
-        launches_per_step = 2  # shard filter, fused FFN with the cross-rank sum in its epilogue
+        launches_per_step = 1  # fused FFN: shard range, records, cross-rank sum in its epilogue
     engine = engines[0]
     layer = layers[0]
 
@@ -506,9 +507,9 @@ def run_ours(args) -> None:
             step_call(engines[i % LAYERS], x, ids_all[i], out_buf)
 
     # Timed: the K steps back to back in one CUDA graph, CUDA events on the
-    # launching stream around the replay.  With N > 1 the graph also holds the
-    # NCCL all-reduce of every step (every rank captures the same sequence);
-    # it is released before the process group is destroyed.
+    # launching stream around the replay.  With N > 1 every rank captures the
+    # same sequence of fused launches (their exchange slots rotate in step);
+    # the graph is released before the process group is destroyed.
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph, stream=side):
         run_steps(args.warmup, args.steps)

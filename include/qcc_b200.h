@@ -283,6 +283,13 @@ QCC_API int qcc_ipc_close(void* ptr);
  * qcc_indexed_ffn_decode on this rank's record shard with the sum over the
  * world ranks fused into its epilogue: y_out (on every rank) =
  *   sum over ranks q in rank order of rank q's partial, + y_in.
+ * id_begin >= 0: ids is the GLOBAL ascending id list shared by the batch's
+ * tokens, and this rank uses the ids in [id_begin, id_end) rebased by
+ * id_begin (packed holds records id_begin..id_end-1); the kernel finds that
+ * run itself, so no separate union / rebase launch precedes it.  id_begin < 0:
+ * ids are already local to packed (e.g. from qcc_build_union with a token
+ * mask).  world 1 is allowed (no exchange; exchange may be NULL).  packed may
+ * be NULL when n_records is 0 (an empty shard).
  * exchange: host array of the world ranks' exchange buffers (exchange[rank]
  * is this rank's own; the others are peer mappings from qcc_ipc_open),
  * each exchange_bytes large and initialised by qcc_exchange_alloc.  Every
@@ -299,8 +306,9 @@ QCC_API int qcc_indexed_ffn_decode_allreduce(const void* x, int64_t ldx, int bat
                                              int64_t n_records, int dtype, const void* ids, int ids_dtype, int n_ids,
                                              const int32_t* n_ids_dev, const uint8_t* token_mask, void* workspace,
                                              size_t workspace_bytes, void* y_out, int64_t ldy, int y_dtype,
-                                             const float* y_in, int64_t ld_in, void* const* exchange,
-                                             size_t exchange_bytes, int world, int rank, cudaStream_t stream);
+                                             const float* y_in, int64_t ld_in, int64_t id_begin, int64_t id_end,
+                                             void* const* exchange, size_t exchange_bytes, int world, int rank,
+                                             cudaStream_t stream);
 
 /* Elementwise cast of n fp32 values to dtype (used after a cross-rank sum). */
 QCC_API int qcc_cast_f32(const float* src, void* dst, int64_t n, int dtype, cudaStream_t stream);

@@ -64,7 +64,8 @@ SIGNATURES = {
     "qcc_indexed_ffn_decode_allreduce": (_c_int, [_c_void_p, _c_int64, _c_int, _c_int, _c_void_p, _c_int64, _c_int,
                                                   _c_void_p, _c_int, _c_int, _c_void_p, _c_void_p, _c_void_p,
                                                   _c_size_t, _c_void_p, _c_int64, _c_int, _c_void_p, _c_int64,
-                                                  _c_void_p, _c_size_t, _c_int, _c_int, _c_void_p]),
+                                                  _c_int64, _c_int64, _c_void_p, _c_size_t, _c_int, _c_int,
+                                                  _c_void_p]),
     "qcc_prefill_workspace_bytes": (_c_size_t, [_c_int64, _c_int]),
     "qcc_prefill_workspace_status_offset": (_c_size_t, []),
     "qcc_indexed_ffn_prefill": (_c_int, [_c_void_p, _c_int64, _c_int, _c_int, _c_void_p, _c_int64, _c_int,

@@ -28,6 +28,10 @@
 #include "qcc_common.cuh"
 #include "qcc_host.h"
 
+#ifndef QCC_DECODE_PDL
+#define QCC_DECODE_PDL 0
+#endif
+
 namespace qcc {
 
 namespace {
@@ -107,6 +111,11 @@ struct DecodeArgs {
   // exchange buffer; y is the sum over ranks in rank order.
   int world;
   int rank;
+  // Shard range (id_lo >= 0): the ids are global and ascending, and only
+  // those in [id_lo, id_hi) -- one contiguous run of the list -- are used,
+  // rebased by id_lo.  id_lo < 0: the ids are already local.
+  int64_t id_lo;
+  int64_t id_hi;
   unsigned int* epoch;            // launch counter in this rank's exchange header (advanced by the last CTA)
   uint8_t* xchg[kMaxRanks];       // column-sum slots of all ranks' exchange buffers, own included
 };
@@ -165,11 +174,43 @@ __global__ void __launch_bounds__(kMaxThreads, 1) indexed_ffn_decode_kernel(cons
   int32_t* s_ids = s_flag + 4;
   uint8_t* s_bits = reinterpret_cast<uint8_t*>(s_ids + a.id_cap);
 
+#if QCC_DECODE_PDL
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+#endif
   // This CTA's share of the id list.
   int n = a.n_ids;
   if (a.n_ids_dev != nullptr) n = min(n, max(0, __ldg(a.n_ids_dev)));
-  const int begin = static_cast<int>((static_cast<int64_t>(n) * blockIdx.x) / gridDim.x);
-  const int end = static_cast<int>((static_cast<int64_t>(n) * (blockIdx.x + 1)) / gridDim.x);
+  int first = 0;
+  const int64_t rebase = a.id_lo >= 0 ? a.id_lo : 0;
+  if (a.id_lo >= 0) {
+    // The ids in [id_lo, id_hi) of an ascending list are the run
+    // [#ids < id_lo, #ids < id_hi): count both in one coalesced pass (every
+    // load in flight at once) and a block reduction.
+    unsigned int below_lo = 0, below_hi = 0;
+    for (int i = tid; i < n; i += nthreads) {
+      const int64_t id = load_id(a, i);
+      below_lo += id < a.id_lo ? 1u : 0u;
+      below_hi += id < a.id_hi ? 1u : 0u;
+    }
+    below_lo = __reduce_add_sync(0xffffffffu, below_lo);
+    below_hi = __reduce_add_sync(0xffffffffu, below_hi);
+    unsigned int* s_count = reinterpret_cast<unsigned int*>(s_red);  // free until the pipeline starts
+    if (lane == 0) {
+      s_count[2 * warp] = below_lo;
+      s_count[2 * warp + 1] = below_hi;
+    }
+    __syncthreads();
+    unsigned int lo = 0, hi = 0;
+    for (int w = 0; w < nwarps; ++w) {
+      lo += s_count[2 * w];
+      hi += s_count[2 * w + 1];
+    }
+    first = static_cast<int>(lo);
+    n = static_cast<int>(hi) - first;
+  }
+  const int begin = first + static_cast<int>((static_cast<int64_t>(n) * blockIdx.x) / gridDim.x);
+  const int end = first + static_cast<int>((static_cast<int64_t>(n) * (blockIdx.x + 1)) / gridDim.x);
   const int cnt = end - begin;
 
   const uint64_t policy = policy_evict_first();
@@ -188,7 +229,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1) indexed_ffn_decode_kernel(cons
     }
   };
   auto cache_id = [&](int i) {  // id (or -1 when out of range) and token bits of local record i
-    const int64_t id = load_id(a, begin + i);
+    const int64_t id = load_id(a, begin + i) - rebase;
     const bool in_range = id >= 0 && id < a.n_records;
     if (!in_range) atomicOr(a.status, QCC_DEV_ID_RANGE);
     s_ids[i] = in_range ? static_cast<int32_t>(id) : -1;
@@ -229,7 +270,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1) indexed_ffn_decode_kernel(cons
   int64_t first_ids[kMaxStages];
   if (tid == 0) {
 #pragma unroll
-    for (int i = 0; i < kMaxStages; ++i) first_ids[i] = i < pre ? load_id(a, begin + i) : -1;
+    for (int i = 0; i < kMaxStages; ++i) first_ids[i] = i < pre ? load_id(a, begin + i) - rebase : -1;
   }
   for (int i = tid; i < cnt; i += nthreads) cache_id(i);
   if (tid == 0) {
@@ -691,9 +732,11 @@ int indexed_ffn_decode(const void* x, int64_t ldx, int batch, int hidden, const 
                        int dtype, const void* ids, int ids_dtype, int n_ids, const int32_t* n_ids_dev,
                        const uint8_t* token_mask, void* workspace, size_t workspace_bytes, void* y_out, int64_t ldy,
                        int y_dtype, const float* y_in, int64_t ld_in, void* activation_out, int64_t lda,
-                       cudaStream_t stream, void* const* xchg, int world, int rank) {
+                       cudaStream_t stream, void* const* xchg, int world, int rank, int64_t id_lo,
+                       int64_t id_hi) {
   if (!valid_dtype(dtype) || !valid_dtype(y_dtype)) return QCC_ERR_DTYPE;
   if (world < 1 || world > kMaxRanks || rank < 0 || rank >= world) return QCC_ERR_SHAPE;
+  if (id_lo >= 0 && id_hi < id_lo) return QCC_ERR_SHAPE;
   if (world > 1) {
     if (xchg == nullptr) return QCC_ERR_INVALID_ARGUMENT;
     for (int q = 0; q < world; ++q)
@@ -706,7 +749,9 @@ int indexed_ffn_decode(const void* x, int64_t ldx, int batch, int hidden, const 
   if (ldx < hidden || ldy < hidden || (activation_out != nullptr && lda < n_ids)) return QCC_ERR_SHAPE;
   if (y_in != nullptr && ld_in < hidden) return QCC_ERR_SHAPE;
   if (x == nullptr || y_out == nullptr || workspace == nullptr) return QCC_ERR_INVALID_ARGUMENT;
-  if (n_ids > 0 && (ids == nullptr || packed == nullptr)) return QCC_ERR_INVALID_ARGUMENT;
+  // An empty shard (n_records 0, e.g. an empty slice whose pointer is NULL)
+  // reads no record: every id is outside it.
+  if (n_ids > 0 && (ids == nullptr || (packed == nullptr && n_records > 0))) return QCC_ERR_INVALID_ARGUMENT;
   if (workspace_bytes < decode_workspace_bytes(batch, hidden, dtype)) return QCC_ERR_WORKSPACE;
   if (!aligned16(packed) || !aligned16(workspace)) return QCC_ERR_ALIGNMENT;
 
@@ -775,6 +820,8 @@ int indexed_ffn_decode(const void* x, int64_t ldx, int batch, int hidden, const 
   args.x_vec = (hidden % 8 == 0) && aligned16(x) && ((ldx * dtype_bytes(dtype)) % 16 == 0);
   args.world = world;
   args.rank = rank;
+  args.id_lo = id_lo >= 0 ? id_lo : -1;
+  args.id_hi = id_lo >= 0 ? id_hi : -1;
   args.epoch = world > 1 ? static_cast<unsigned int*>(xchg[rank]) : nullptr;
   for (int q = 0; q < kMaxRanks; ++q)
     args.xchg[q] = q < world && world > 1 ? static_cast<uint8_t*>(xchg[q]) + kXchgHeader : nullptr;
@@ -784,11 +831,20 @@ int indexed_ffn_decode(const void* x, int64_t ldx, int batch, int hidden, const 
   cfg.blockDim = dim3(static_cast<unsigned>(shape.threads));
   cfg.dynamicSmemBytes = shape.smem;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeCooperative;
   attr[0].val.cooperative = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
+#if QCC_DECODE_PDL
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.numAttrs = 2;
+#if QCC_DECODE_PDL == 2
+  attr[0] = attr[1];
+  cfg.numAttrs = 1;
+#endif
+#endif
   clear_stale_error();
   if (!cuda_ok(cudaLaunchKernelEx(&cfg, fn, args))) return QCC_ERR_CUDA;
   return QCC_OK;
@@ -831,12 +887,12 @@ extern "C" int qcc_indexed_ffn_decode_allreduce(const void* x, int64_t ldx, int 
                                                 int64_t n_records, int dtype, const void* ids, int ids_dtype,
                                                 int n_ids, const int32_t* n_ids_dev, const uint8_t* token_mask,
                                                 void* workspace, size_t workspace_bytes, void* y_out, int64_t ldy,
-                                                int y_dtype, const float* y_in, int64_t ld_in,
-                                                void* const* exchange, size_t exchange_bytes, int world, int rank,
-                                                cudaStream_t stream) {
+                                                int y_dtype, const float* y_in, int64_t ld_in, int64_t id_begin,
+                                                int64_t id_end, void* const* exchange, size_t exchange_bytes,
+                                                int world, int rank, cudaStream_t stream) {
   if (world < 1 || world > 8 || rank < 0 || rank >= world) return QCC_ERR_SHAPE;
   if (world > 1 && exchange_bytes < qcc::exchange_bytes(world, batch, hidden, dtype)) return QCC_ERR_WORKSPACE;
   return qcc::indexed_ffn_decode(x, ldx, batch, hidden, packed, n_records, dtype, ids, ids_dtype, n_ids, n_ids_dev,
                                  token_mask, workspace, workspace_bytes, y_out, ldy, y_dtype, y_in, ld_in, nullptr, 0,
-                                 stream, exchange, world, rank);
+                                 stream, exchange, world, rank, id_begin, id_end);
 }

@@ -28,8 +28,8 @@
 //  activation (phase 1) or the output (phase 2).
 //
 // Operands move by tiled TMA (128-byte swizzle, no multicast) through a 4-stage
-// shared-memory ring; one thread loads the weight boxes and one the
-// activation boxes (both arrive on the stage's barrier), one thread issues the
+// shared-memory ring; two threads (in two warps) load the weight boxes and one
+// the activation boxes (all three arrive on the stage's barrier), one thread issues the
 // MMAs, four warps read TMEM (two 256-column accumulator buffers, so the
 // epilogue of one unit overlaps the MMAs of the next).  Every wait is bounded (2 s) and reports
 // QCC_DEV_TIMEOUT through the workspace status word.
@@ -57,9 +57,15 @@ constexpr int kHRange = 256;              // hidden outputs per down unit (MMA N
 constexpr int kMaxTiles = 4;
 constexpr int kGroupTokens = kTile * kMaxTiles;
 constexpr int kStages = 4;
-constexpr int kThreads = 224;             // warp 0: weight TMA, warp 1: MMA, warps 2-5: TMEM readers, warp 6: activation TMA
-constexpr int kActWarp = 6;               // issues the x / activation boxes (one thread issues ~5 M TMA copies/s)
+// warp 0: weight TMA (first half of a stage's weight boxes), warp 1: MMA,
+// warps 2-5: TMEM readers, warp 6: activation TMA, warp 7: weight TMA (second
+// half).  One issuing thread reaches only ~5 M tiled TMA copies/s, so a step's
+// boxes are spread over three threads in different warps.
+constexpr int kThreads = 256;
+constexpr int kActWarp = 6;
+constexpr int kWeightWarp2 = 7;
 constexpr int kFirstReader = 2, kReaders = 4;  // warps 2-5 read TMEM (warp w: lanes 32*(w%4) .. +31)
+constexpr int kLoaders = 3;                    // arrivals on a stage's full barrier
 constexpr int kPlanThreads = 1024;
 constexpr uint32_t kBox64 = 64 * 128;     // [64 rows x 64 elements] of 16-bit: 8 KB
 constexpr uint32_t kBox128 = 128 * 128;   // [128 rows x 64 elements]: 16 KB
@@ -114,6 +120,8 @@ struct Control {
 static_assert(sizeof(Control) <= kControlBytes, "control block");
 static_assert(offsetof(Control, r) % 16 == 0, "the ranges record is copied with 16-byte accesses");
 static_assert(kActWarp >= kFirstReader + kReaders && kActWarp * 32 < kThreads, "warp roles");
+static_assert(kWeightWarp2 >= kFirstReader + kReaders && kWeightWarp2 != kActWarp && kWeightWarp2 * 32 < kThreads,
+              "warp roles");
 
 struct PrefillArgs {
   int32_t* header;
@@ -501,7 +509,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
-      mbar_init(&ctl->full[s], 2);  // the two loading threads each arrive with their bytes
+      mbar_init(&ctl->full[s], kLoaders);  // each loading thread arrives with its bytes
       mbar_init(&ctl->empty[s], 1);
     }
     for (int j = 0; j < 2; ++j) {
@@ -572,19 +580,40 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int s = it % kStages;
           ok = wait_phase(&ctl->empty[s], ((it / kStages) & 1u) ^ 1u, abort_flag, status) ? 1 : 0;
           if (ok) {
-            // B operand: gate and up rows of the unit's blocks, 128 rows per block.
+            // B operand: gate and up rows of the unit's first block (128 rows);
+            // warp kWeightWarp2 loads the second block of a pair.
             uint8_t* st = smem + s * kStageBytes + kBox128;
-            mbar_arrive_expect_tx(&ctl->full[s], nb * kBox128);
-            for (int jb = 0; jb < nb; ++jb) {
-              const int b = unit_block(unit, jb);
-              tma_load_3d(st + jb * kBox128, &tm_records, kc * kChunk, 0, b * kBlock, &ctl->full[s]);
-              tma_load_3d(st + jb * kBox128 + kBox64, &tm_records, kc * kChunk, 1, b * kBlock, &ctl->full[s]);
-            }
+            mbar_arrive_expect_tx(&ctl->full[s], kBox128);
+            const int b = unit_block(unit, 0);
+            tma_load_3d(st, &tm_records, kc * kChunk, 0, b * kBlock, &ctl->full[s]);
+            tma_load_3d(st + kBox64, &tm_records, kc * kChunk, 1, b * kBlock, &ctl->full[s]);
           }
         }
         if (!__shfl_sync(0xffffffffu, ok, 0)) {
           stop = true;
           break;
+        }
+      }
+    }
+  } else if (warp == kWeightWarp2 && lane == 0) {
+    // Second weight loader: the gate and up rows of a pair's second block;
+    // for a single-block unit it only arrives.
+    for (int si = 0, u; (u = seg_unit(ctl->r, 0, si, n_units)) >= 0 && !*abort_flag; ++si) {
+      int ks, ke;
+      if (!segment(u, ctl->r.lo_u[0], ctl->r.lo_k[0], ctl->r.hi_u[0], ctl->r.hi_k[0], a.n_chunks, &ks, &ke)) continue;
+      const int unit = a.units[u];
+      const bool pair = unit_blocks(unit) == 2;
+      const int b = pair ? unit_block(unit, 1) : 0;
+      for (int kc = ks; kc < ke; ++kc, ++it) {
+        const int s = it % kStages;
+        if (!wait_phase(&ctl->empty[s], ((it / kStages) & 1u) ^ 1u, abort_flag, status)) break;
+        if (pair) {
+          uint8_t* st = smem + s * kStageBytes + 2 * kBox128;
+          mbar_arrive_expect_tx(&ctl->full[s], kBox128);
+          tma_load_3d(st, &tm_records, kc * kChunk, 0, b * kBlock, &ctl->full[s]);
+          tma_load_3d(st + kBox64, &tm_records, kc * kChunk, 1, b * kBlock, &ctl->full[s]);
+        } else {
+          mbar_arrive(&ctl->full[s]);
         }
       }
     }
@@ -746,9 +775,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int s = it % kStages;
           ok = wait_phase(&ctl->empty[s], ((it / kStages) & 1u) ^ 1u, abort_flag, status) ? 1 : 0;
           if (ok) {
+            // Down rows, hidden columns [r*256, r*256 + 128); warp kWeightWarp2
+            // loads the other 128.
             uint8_t* st = smem + s * kStageBytes;
-            mbar_arrive_expect_tx(&ctl->full[s], 4 * kBox64);
-            for (int qq = 0; qq < 4; ++qq)
+            mbar_arrive_expect_tx(&ctl->full[s], 2 * kBox64);
+            for (int qq = 0; qq < 2; ++qq)
               tma_load_3d(st + kBox128 + qq * kBox64, &tm_records, r * kHRange + qq * 64, 2, b * kBlock,
                           &ctl->full[s]);
           }
@@ -760,6 +791,24 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
     if (lane == 0) drain_loads(ctl, it);
+  } else if (warp == kWeightWarp2 && lane == 0) {
+    int si = 0;
+    for (int sv = 0, v; (v = seg_unit(ctl->r, 1, sv, n_down)) >= 0 && !*abort_flag; ++sv) {
+      const int t = v % a.n_tiles, r = v / a.n_tiles;
+      int ks, ke;
+      if (!segment(v, ctl->r.lo_u[1], ctl->r.lo_k[1], ctl->r.hi_u[1], ctl->r.hi_k[1], a.header[kHdrTileCount + t], &ks,
+                   &ke))
+        continue;
+      for (int step = ks; step < ke; ++step, ++it, ++si) {
+        const int b = si < staged ? (ctl->steps[si] & 0xFFFF) : a.tile_list[t * a.n_blocks + step];
+        const int s = it % kStages;
+        if (!wait_phase(&ctl->empty[s], ((it / kStages) & 1u) ^ 1u, abort_flag, status)) break;
+        uint8_t* st = smem + s * kStageBytes;
+        mbar_arrive_expect_tx(&ctl->full[s], 2 * kBox64);
+        for (int qq = 2; qq < 4; ++qq)
+          tma_load_3d(st + kBox128 + qq * kBox64, &tm_records, r * kHRange + qq * 64, 2, b * kBlock, &ctl->full[s]);
+      }
+    }
   } else if (warp == kActWarp && lane == 0) {
     int si = 0;
     for (int sv = 0, v; (v = seg_unit(ctl->r, 1, sv, n_down)) >= 0 && !*abort_flag; ++sv) {

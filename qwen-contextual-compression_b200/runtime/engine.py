@@ -114,7 +114,8 @@ class IndexedSparseFFN:
     def forward(self, x: torch.Tensor, ids: torch.Tensor, *, token_mask: torch.Tensor | None = None,
                 n_ids_dev: torch.Tensor | None = None, out: torch.Tensor | None = None,
                 out_dtype: torch.dtype | None = None, activation: torch.Tensor | None = None,
-                accumulate: torch.Tensor | None = None, exchange=None) -> torch.Tensor:
+                accumulate: torch.Tensor | None = None, exchange=None,
+                id_range: tuple[int, int] | None = None) -> torch.Tensor:
         """y [B, H] for x [B, H] (or [H] -> [H]) and the 1-D selected-id list ``ids``.
 
         token_mask: optional uint8 [len(ids)], bit b = token b uses record j.
@@ -124,6 +125,9 @@ class IndexedSparseFFN:
         accumulate: optional fp32 [B, H] added before the final rounding.
         exchange:   optional cross-rank exchange (``sharded.PeerExchange``): y is
                     then the sum of every rank's partial over this rank's shard.
+        id_range:   optional (begin, end): ``ids`` is the global ascending id
+                    list and only its ids in [begin, end), rebased by begin,
+                    select records of this engine (the kernel finds the run).
         """
         squeeze = x.dim() == 1
         if squeeze:
@@ -160,14 +164,19 @@ class IndexedSparseFFN:
                 # after the kernel that reads it.
                 mask_ptr = torch.bitwise_right_shift(token_mask, start).data_ptr()
             acc_ptr = None if accumulate is None else accumulate.data_ptr() + start * acc_row
-            if exchange is not None:
+            if exchange is not None or id_range is not None:
                 if a_ptr is not None:
-                    raise ValueError("activation output is not available with a cross-rank exchange")
+                    raise ValueError("activation output is not available with a cross-rank exchange or id range")
+                id_begin, id_end = id_range if id_range is not None else (-1, -1)
+                if id_range is not None and not 0 <= id_begin <= id_end:
+                    raise ValueError("id_range must satisfy 0 <= begin <= end")
+                world, rank = (exchange.world, exchange.rank) if exchange is not None else (1, 0)
                 status = lib.qcc_indexed_ffn_decode_allreduce(
                     x_ptr + start * x_row, x.stride(0), chunk, plan.hidden, plan.packed_ptr, plan.n_records,
                     plan.code, ids.data_ptr(), plan.ids_code, n_ids, count_ptr, mask_ptr, ws.ptr, ws.nbytes,
-                    out_ptr + start * out_row, out.stride(0), plan.y_code, acc_ptr, acc_ld, exchange.pointers,
-                    exchange.nbytes, exchange.world, exchange.rank, stream)
+                    out_ptr + start * out_row, out.stride(0), plan.y_code, acc_ptr, acc_ld, id_begin, id_end,
+                    exchange.pointers if exchange is not None else None,
+                    exchange.nbytes if exchange is not None else 0, world, rank, stream)
                 if status:
                     _lib.check(status, "qcc_indexed_ffn_decode_allreduce")
                 continue

@@ -2,8 +2,10 @@
 
 Rank r of P owns the contiguous records [r*N//P, (r+1)*N//P).  Every rank
 holds the same global selected ids (the selector is deterministic and
-replicated), keeps the ones inside its range, rebased (qcc_build_union, one
-small launch), and runs the fused kernel on them.  The sum over ranks is
+replicated, its output ascending) and keeps the ones inside its range,
+rebased: for one id list shared by all tokens the decode kernel finds that
+run itself; per-token id rows first go through qcc_build_union (one small
+launch: union plus token mask).  The sum over ranks is
 either fused into that kernel (``allreduce="fused"``, the default: each CTA
 stores its column sums into every rank's exchange buffer over NVLink and adds
 the ranks' sums in rank order -- no NCCL call, no extra launch) or an NCCL
@@ -117,6 +119,11 @@ class ShardedIndexedFFN:
         return self.forward(x, ids)
 
     def forward(self, x: torch.Tensor, ids: torch.Tensor) -> torch.Tensor:
+        if self.allreduce == "fused" and ids.ndim == 1:
+            # One id list for every token: the kernel finds this shard's run.
+            x2 = x if x.ndim == 2 else x.unsqueeze(0)
+            y = self.engine(x2, ids, exchange=self.exchange, id_range=(self.begin, self.end))
+            return y if x.ndim == 2 else y.squeeze(0)
         if self.allreduce == "fused":
             rows = ids if ids.ndim == 2 else ids.unsqueeze(0)
             if rows.dtype != torch.int32:
