@@ -264,7 +264,70 @@ def measure_selector(engine, x, device, stream, side) -> dict:
     out["select_union_ffn_us_batch8"] = round(graph_time_us(step8, steps, stream, side), 2)
     union, _, count = build_union(select_topk(scores8[0], k), 0, INTERMEDIATE)
     out["union_records_batch8"] = int(count.item())
+    out["score_select"] = measure_score_select(engine, x, device, stream, side)
     return out
+
+
+def selector_predictor(seed: int = 7) -> dict:
+    """A residual latent predictor with the reference CudaSelector's shape (hidden 5120, latent 32)."""
+    g = torch.Generator().manual_seed(seed)
+    latent = 32
+    return {"enc_w": torch.randn(latent, HIDDEN, generator=g) * 0.02, "enc_b": torch.randn(latent, generator=g) * 0.1,
+            "fc1_w": torch.randn(latent, latent, generator=g) * 0.2, "fc1_b": torch.randn(latent, generator=g) * 0.1,
+            "fc2_w": torch.randn(latent, latent, generator=g) * 0.2, "fc2_b": torch.randn(latent, generator=g) * 0.1,
+            "ln_w": 1 + 0.1 * torch.randn(latent, generator=g), "ln_b": 0.1 * torch.randn(latent, generator=g),
+            "out_w": torch.randn(INTERMEDIATE, latent, generator=g) * 0.2,
+            "out_b": torch.randn(INTERMEDIATE, generator=g) * 0.1}
+
+
+def measure_score_select(engine, x, device, stream, side) -> dict:
+    """The fused score producer + top-K (the reference's runtime selector in one launch).
+
+    Predictor: residual, hidden 5120, latent 32, 17408 neurons, bf16 weights
+    (runtime/cuda_selector.py's shape); k = N // 2 (CudaSelector) and K/N = 0.2.
+    Also selector + fused FFN from x, and the reference's path (predictor as
+    torch ops + torch.topk) on the host cores.
+    """
+    from qcc_b200.runtime.cuda_selector import FusedScoreSelector
+
+    params = selector_predictor()
+    steps = 20
+    xs = torch.randn(steps, 1, HIDDEN, generator=torch.Generator().manual_seed(8)).to(device, torch.bfloat16)
+    out = {"predictor": "residual, hidden 5120, latent 32, N 17408, bf16 weights, fp32 arithmetic"}
+    for name, k in (("k_half", INTERMEDIATE // 2), ("k_r0.2", workloads.retention_k(INTERMEDIATE, 0.2))):
+        sel = FusedScoreSelector(params, kind=0, k=k, dtype=torch.bfloat16, device=device)
+        out[f"us_batch1_{name}"] = round(graph_time_us(lambda i: sel.run(xs[i], want_scores=False), steps, stream,
+                                                       side), 2)
+        if name == "k_r0.2":
+            y1 = torch.empty((1, HIDDEN), dtype=torch.bfloat16, device=device)
+            out["select_ffn_us_batch1_r0.2"] = round(graph_time_us(
+                lambda i: engine(xs[i], sel.run(xs[i], want_scores=False)[1][0], out=y1), steps, stream, side), 2)
+        sel.check()
+    return out
+
+
+def score_select_cpu_sample(seconds: float) -> dict:
+    """The reference's runtime selector on the host: predictor forward + torch.topk (fp32)."""
+    from oracle import predictor as opred  # CPU baseline leg only
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    params = selector_predictor()
+    x = torch.randn(1, HIDDEN, generator=torch.Generator().manual_seed(8))
+    k = INTERMEDIATE // 2
+    times = []
+    start = time.perf_counter()
+    with torch.inference_mode():
+        for _ in range(3):
+            opred.torch_runtime_selector(x, params, k)
+        while time.perf_counter() - start < seconds or len(times) < 20:
+            t0 = time.perf_counter()
+            opred.torch_runtime_selector(x, params, k)
+            times.append(time.perf_counter() - t0)
+            if len(times) >= 2000:
+                break
+    return {"us_batch1_k_half": round(statistics.median(times) * 1e6, 2), "cores": threads, "kind": "port",
+            "sample": f"{len(times)} calls, median, fp32 torch ops ({host_description()})"}
 
 
 def measure_prefill(device, stream, side, cpu_seconds: float) -> dict:
@@ -600,6 +663,8 @@ def run_ours(args) -> None:
     selector = None
     if not args.no_selector and world == 1:
         selector = measure_selector(engines[0], x, device, stream, side)
+        if not args.no_cpu_baseline:
+            selector["score_select"]["cpu_baseline"] = score_select_cpu_sample(3.0)
     offload = None
     if not args.no_offload and world == 1:
         offload = measure_offload(device, args.offload_tokens)

@@ -314,6 +314,40 @@ QCC_API int qcc_indexed_ffn_decode_allreduce(const void* x, int64_t ldx, int bat
 QCC_API int qcc_cast_f32(const float* src, void* dst, int64_t n, int dtype, cudaStream_t stream);
 
 /* ---------------------------------------------------------------------------
+ * Fused score producer + top-K (the runtime selector).
+ *
+ * Replaces runtime/cuda_selector.py:30-40 (latent_kernel + head_kernel, then
+ * torch.topk(scores, k, sorted=False)) and the scoring of
+ * runtime/selector.py:15-38 with one cooperative launch.  For each row b of x
+ * [batch, hidden] (row stride ldx, elements):
+ *   kind 0, ResidualFactorizedPredictor (predictor/models.py:17-36):
+ *     r = silu(enc_w x + enc_b); u = silu(fc1_w r + fc1_b);
+ *     v = fc2_w u + fc2_b + r;  z = LayerNorm(v; ln_eps) * ln_w + ln_b
+ *   kind 1, FactorizedPredictor (predictor/models.py:6-14): z = enc_w x + enc_b
+ *   scores = out_w z + out_b;
+ *   ids[b * ld_ids + 0..k-1] = the k largest scores, ascending, ties to the
+ *   lower index (the rule of qcc_select_topk).
+ * Weights are nn.Linear layouts ([out, in], row-major), all in dtype, like x;
+ * enc_w [latent, hidden] with the input normalisation folded in (enc_b =
+ * -(enc_w) mean after dividing by std, runtime/selector.py:33-35); fc1_w,
+ * fc2_w [latent, latent]; out_w [n_out, latent].  Every bias and ln_w / ln_b
+ * may be NULL (zero / one).  Arithmetic is fp32.  scores, when not NULL,
+ * receives the fp32 scores [batch, ld_scores].  latent <= 256.
+ * The workspace (qcc_selector_workspace_bytes, zeroed once with
+ * qcc_workspace_init) is left zeroed by every call; its status word is at
+ * offset 0 (QCC_DEV_TIMEOUT: re-initialise it).  Rows beyond 32 run as
+ * further launches on the same stream.
+ * ------------------------------------------------------------------------- */
+QCC_API size_t qcc_selector_workspace_bytes(int batch, int hidden, int latent, int n_out);
+
+QCC_API int qcc_selector_scores_topk(const void* x, int64_t ldx, int batch, int hidden, int latent, int n_out,
+                                     int kind, int dtype, const void* enc_w, const void* enc_b, const void* fc1_w,
+                                     const void* fc1_b, const void* fc2_w, const void* fc2_b, const void* ln_w,
+                                     const void* ln_b, float ln_eps, const void* out_w, const void* out_b, int k,
+                                     int32_t* ids, int64_t ld_ids, float* scores, int64_t ld_scores,
+                                     void* workspace, size_t workspace_bytes, cudaStream_t stream);
+
+/* ---------------------------------------------------------------------------
  * Block-sparse prefill.
  *
  * Replaces, for a prefill of n_tokens rows, the per-tile loop of

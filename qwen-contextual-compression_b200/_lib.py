@@ -66,6 +66,12 @@ SIGNATURES = {
                                                   _c_size_t, _c_void_p, _c_int64, _c_int, _c_void_p, _c_int64,
                                                   _c_int64, _c_int64, _c_void_p, _c_size_t, _c_int, _c_int,
                                                   _c_void_p]),
+    "qcc_selector_workspace_bytes": (_c_size_t, [_c_int, _c_int, _c_int, _c_int]),
+    "qcc_selector_scores_topk": (_c_int, [_c_void_p, _c_int64, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int,
+                                          _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p,
+                                          _c_void_p, _c_void_p, ctypes.c_float, _c_void_p, _c_void_p, _c_int,
+                                          _c_void_p, _c_int64, _c_void_p, _c_int64, _c_void_p, _c_size_t,
+                                          _c_void_p]),
     "qcc_prefill_workspace_bytes": (_c_size_t, [_c_int64, _c_int]),
     "qcc_prefill_workspace_status_offset": (_c_size_t, []),
     "qcc_indexed_ffn_prefill": (_c_int, [_c_void_p, _c_int64, _c_int, _c_int, _c_void_p, _c_int64, _c_int,

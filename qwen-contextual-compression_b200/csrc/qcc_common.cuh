@@ -211,6 +211,44 @@ __device__ __forceinline__ int block_exclusive_scan(int v, int* scratch, int* to
   return before;
 }
 
+// Order-preserving 32-bit key of a score: larger score, larger key.  -0.0
+// and +0.0 share a key; every NaN maps to the largest key (it ranks first,
+// as in torch.topk).
+__device__ __forceinline__ uint32_t score_key(float f) {
+  uint32_t u = __float_as_uint(f);
+  if (f != f) return 0xFFFFFFFFu;
+  if ((u & 0x7FFFFFFFu) == 0u) u = 0u;
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+// Finds the bin holding the rem-th largest element of a histogram whose bins
+// are visited from the highest down.  Thread t holds PER consecutive bins, its
+// highest one first, so an exclusive scan in thread order counts the elements
+// in all higher bins.  Writes the bin and rem minus the elements above it.
+// Requires 1 <= rem <= total count and nbins == PER * blockDim.x.  Contains
+// __syncthreads (block_exclusive_scan).
+template <int PER>
+__device__ __forceinline__ void find_bin(const int* hist, int rem, int* scratch, int* out_bin, int* out_rem) {
+  const int top = PER * static_cast<int>(blockDim.x) - 1 - PER * static_cast<int>(threadIdx.x);
+  int c[PER];
+  int s = 0;
+#pragma unroll
+  for (int j = 0; j < PER; ++j) {
+    c[j] = hist[top - j];
+    s += c[j];
+  }
+  int total;
+  int above = block_exclusive_scan(s, scratch, &total);
+#pragma unroll
+  for (int j = 0; j < PER; ++j) {
+    if (above < rem && above + c[j] >= rem) {
+      *out_bin = top - j;
+      *out_rem = rem - above;
+    }
+    above += c[j];
+  }
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);

@@ -36,40 +36,6 @@ constexpr int kDigitBins = 1 << 10;                        // key bits 19..10, t
 constexpr int kCandidateCap = kDigit1Bins - kDigitBins;   // candidate keys that fit beside a 10-bit histogram
 constexpr int kLoadRound = 8;                              // loads in flight per thread
 
-__device__ __forceinline__ uint32_t score_key(float f) {
-  uint32_t u = __float_as_uint(f);
-  if (f != f) return 0xFFFFFFFFu;          // NaN ranks largest
-  if ((u & 0x7FFFFFFFu) == 0u) u = 0u;     // -0.0 == +0.0
-  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
-}
-
-// Finds the bin holding the rem-th largest element of a histogram whose bins
-// are visited from the highest down.  Thread t holds PER consecutive bins, its
-// highest one first, so an exclusive scan in thread order counts the elements
-// in all higher bins.  Writes the bin and rem minus the elements above it.
-// Requires 1 <= rem <= total count and nbins == PER * blockDim.x.
-template <int PER>
-__device__ __forceinline__ void find_bin(const int* hist, int rem, int* scratch, int* out_bin, int* out_rem) {
-  const int top = PER * static_cast<int>(blockDim.x) - 1 - PER * static_cast<int>(threadIdx.x);
-  int c[PER];
-  int s = 0;
-#pragma unroll
-  for (int j = 0; j < PER; ++j) {
-    c[j] = hist[top - j];
-    s += c[j];
-  }
-  int total;
-  int above = block_exclusive_scan(s, scratch, &total);
-#pragma unroll
-  for (int j = 0; j < PER; ++j) {
-    if (above < rem && above + c[j] >= rem) {
-      *out_bin = top - j;
-      *out_rem = rem - above;
-    }
-    above += c[j];
-  }
-}
-
 __global__ void __launch_bounds__(kSelectThreads, 1)
     select_topk_kernel(const float* __restrict__ scores, int64_t ld_scores, int n, int k, int32_t* __restrict__ ids,
                        int64_t ld_ids) {

@@ -7,7 +7,9 @@ Run in a container where robjlyons/qwen-contextual-compression is checked out
 
 Every expected output below is produced by the reference's own functions
 (runtime.ffn, oracle.importance, oracle.sparse_ffn, end_to_end.oracle_sparse_mlp,
-runtime.temporal); inputs are small seeded tensors.  The GPU box never runs
+runtime.temporal, runtime.selector with predictor.models); inputs are small
+seeded tensors.  ``python tests/golden/make_golden.py predictor_cases``
+regenerates one fixture only.  The GPU box never runs
 this script: it only reads the committed .npz / .json files.
 """
 from __future__ import annotations
@@ -30,6 +32,9 @@ from oracle.importance import block_topk_indices, importance_scores, topk_indice
 from oracle.sparse_ffn import reconstruct  # noqa: E402  (reference)
 from end_to_end.oracle_sparse_mlp import OracleSparseMLP  # noqa: E402  (reference)
 from runtime.temporal import neuron_payload, simulate_lru_cache  # noqa: E402  (reference)
+from runtime.selector import FoldedRuntimeSelector, RuntimeSelector  # noqa: E402  (reference)
+from predictor.models import FactorizedPredictor, ResidualFactorizedPredictor  # noqa: E402  (reference)
+from predictor.candidate_reranker import retention_count  # noqa: E402  (reference)
 
 import qcc_b200.workloads as workloads  # noqa: E402  (seeded input generators of this repo)
 
@@ -204,7 +209,48 @@ def c1_case(tokens: int = 4) -> dict:
                                                      down[100, 2000].item()])}
 
 
+def predictor_cases() -> dict:
+    """Scores and selections of the reference's runtime selector (runtime/selector.py:15-38)."""
+    out = {}
+    shapes = {"residual": (ResidualFactorizedPredictor, 48, 300, 32), "residual_ref_test": (ResidualFactorizedPredictor, 7, 20, 32),
+              "residual_l64": (ResidualFactorizedPredictor, 96, 400, 64), "factorized": (FactorizedPredictor, 48, 300, 64)}
+    for i, (name, (cls, h, n, latent)) in enumerate(shapes.items()):
+        torch.manual_seed(40 + i)
+        model = cls(h, n, latent).eval()
+        with torch.no_grad():  # non-trivial LayerNorm affine and biases
+            for prm in model.parameters():
+                prm.add_(0.05 * torch.randn_like(prm))
+        mean, std = torch.randn(h), torch.rand(h) + .2
+        x = torch.randn(4, h)
+        base = RuntimeSelector(model, mean, std, .5)
+        folded = FoldedRuntimeSelector(model, mean, std, .5, torch.float32)
+        with torch.no_grad():
+            scores = base.scores(x)
+            folded_scores = folded.scores(x)
+        k = retention_count(n, .5)
+        for key, t in model.state_dict().items():
+            out[f"{name}/w/{key}"] = t.numpy()
+        out[f"{name}/mean"], out[f"{name}/std"], out[f"{name}/x"] = mean.numpy(), std.numpy(), x.numpy()
+        out[f"{name}/scores"], out[f"{name}/folded_scores"] = scores.numpy(), folded_scores.numpy()
+        out[f"{name}/k"] = np.array(k)
+        out[f"{name}/ids"] = torch.sort(scores, dim=-1, descending=True, stable=True).indices[:, :k].sort(
+            dim=-1).values.numpy().astype(np.int32)
+        out[f"{name}/ln_eps"] = np.array(getattr(getattr(model, "layer_norm", None), "eps", 1e-5))
+    return out
+
+
+FIXTURES = {"ffn_cases": ffn_cases, "select_cases": select_cases, "oracle_mlp": oracle_mlp_cases,
+            "c1_oracle": c1_case, "predictor_cases": predictor_cases}
+
+
 def main() -> None:
+    only = [a for a in sys.argv[1:] if not a.startswith("-")]
+    if only:  # regenerate just these fixtures
+        for name in only:
+            np.savez_compressed(HERE / f"{name}.npz", **FIXTURES[name]())
+            print(name, (HERE / f"{name}.npz").stat().st_size)
+        return
+    np.savez_compressed(HERE / "predictor_cases.npz", **predictor_cases())
     np.savez_compressed(HERE / "ffn_cases.npz", **ffn_cases())
     np.savez_compressed(HERE / "select_cases.npz", **select_cases())
     np.savez_compressed(HERE / "oracle_mlp.npz", **oracle_mlp_cases())
@@ -213,7 +259,8 @@ def main() -> None:
     (HERE / "PROVENANCE.json").write_text(json.dumps({
         "generator": "tests/golden/make_golden.py", "torch": torch.__version__, "numpy": np.__version__,
         "reference": "robjlyons/qwen-contextual-compression (runtime/ffn.py, oracle/importance.py, "
-                     "oracle/sparse_ffn.py, end_to_end/oracle_sparse_mlp.py, runtime/temporal.py)"}, indent=1))
+                     "oracle/sparse_ffn.py, end_to_end/oracle_sparse_mlp.py, runtime/temporal.py, "
+                     "runtime/selector.py, predictor/models.py)"}, indent=1))
     for path in sorted(HERE.glob("*.npz")):
         print(path.name, path.stat().st_size)
 
