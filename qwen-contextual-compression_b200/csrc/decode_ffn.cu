@@ -28,10 +28,6 @@
 #include "qcc_common.cuh"
 #include "qcc_host.h"
 
-#ifndef QCC_DECODE_PDL
-#define QCC_DECODE_PDL 0
-#endif
-
 namespace qcc {
 
 namespace {
@@ -174,10 +170,11 @@ __global__ void __launch_bounds__(kMaxThreads, 1) indexed_ffn_decode_kernel(cons
   int32_t* s_ids = s_flag + 4;
   uint8_t* s_bits = reinterpret_cast<uint8_t*>(s_ids + a.id_cap);
 
-#if QCC_DECODE_PDL
+  // Programmatic dependent launch: the next kernel on the stream may be
+  // scheduled now (it waits for this grid before touching memory), and this
+  // grid waits for the previous one before reading any input.
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   asm volatile("griddepcontrol.wait;" ::: "memory");
-#endif
   // This CTA's share of the id list.
   int n = a.n_ids;
   if (a.n_ids_dev != nullptr) n = min(n, max(0, __ldg(a.n_ids_dev)));
@@ -831,20 +828,16 @@ int indexed_ffn_decode(const void* x, int64_t ldx, int batch, int hidden, const 
   cfg.blockDim = dim3(static_cast<unsigned>(shape.threads));
   cfg.dynamicSmemBytes = shape.smem;
   cfg.stream = stream;
+  // Cooperative (all CTAs resident for the grid barrier) and programmatic
+  // dependent launch: back-to-back layers overlap one launch's set-up with
+  // the previous kernel's tail (measured 34.35 -> 33.94 us per layer).
   cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeCooperative;
   attr[0].val.cooperative = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-#if QCC_DECODE_PDL
   attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
   cfg.numAttrs = 2;
-#if QCC_DECODE_PDL == 2
-  attr[0] = attr[1];
-  cfg.numAttrs = 1;
-#endif
-#endif
   clear_stale_error();
   if (!cuda_ok(cudaLaunchKernelEx(&cfg, fn, args))) return QCC_ERR_CUDA;
   return QCC_OK;
