@@ -31,9 +31,13 @@
 // The workspace is left as found (zero counters and histograms) by every
 // call that completes.
 
+#include <cooperative_groups.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <mutex>
+#include <string>
+#include <unordered_map>
 
 #include "qcc_common.cuh"
 #include "qcc_host.h"
@@ -123,6 +127,25 @@ __device__ __forceinline__ float dot_row(const T* w, const float* z, int L, bool
     }
   } else {
 #pragma unroll 8
+    for (int j = 0; j < L; ++j) acc = fmaf(to_f32<T>(w[j]), z[j], acc);
+  }
+  return acc;
+}
+
+// The same over a row staged in shared memory (16-byte pieces when L % 8 == 0;
+// staged rows start on 16-byte boundaries whenever L * sizeof(T) % 16 == 0).
+template <typename T>
+__device__ __forceinline__ float dot_row_smem(const T* w, const float* z, int L) {
+  float acc = 0.f;
+  if ((L & 7) == 0) {
+#pragma unroll 4
+    for (int j = 0; j < L; j += 8) {
+      float f[8];
+      widen(load_pack8<T>(w + j), f);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc = fmaf(f[e], z[j + e], acc);
+    }
+  } else {
     for (int j = 0; j < L; ++j) acc = fmaf(to_f32<T>(w[j]), z[j], acc);
   }
   return acc;
@@ -396,6 +419,325 @@ __global__ void __launch_bounds__(kThreads) score_select_kernel(const SelArgs a)
   }
 }
 
+// ---------------------------------------------------------------------------
+// Cluster variant: one thread-block cluster of kCluster CTAs per row.
+//
+// Used when the row's neurons fit the cluster's shared memory (N <= kCluster *
+// kSliceCap).  At launch each CTA starts bulk copies of its slice of the head
+// weights (and of fc1 / fc2) into shared memory, so that after the encoder
+// every weight the row still needs is on chip.  All exchanges between the
+// CTAs of a row go through distributed shared memory, separated by hardware
+// cluster barriers (no global atomics, no spin on global counters):
+//  encoder items (item i on CTA i % kCluster) -> cluster barrier -> every CTA
+//  sums the items in a fixed order, runs the MLP, scores its slice, builds its
+//  12-bit histogram -> barrier -> every CTA adds the kCluster histograms bin by
+//  bin (DSMEM) and finds the bin of the k-th key; 10-bit histograms of the
+//  candidates -> barrier -> sum, bin; last 10 bits -> barrier -> sum, exact
+//  key T -> counts above / equal to T -> barrier -> offsets from the counts,
+//  ids written -> barrier (no CTA leaves while another may still read its
+//  shared memory).
+// ---------------------------------------------------------------------------
+
+constexpr int kCluster = 8;
+constexpr int kCThreads = 512;
+constexpr int kMaxItemsPerCta = 2048;   // encoder items held per CTA
+constexpr uint32_t kBulkChunk = 32768;  // bytes per bulk copy
+
+struct ClusterSmem {
+  uint64_t bar;
+  int ok;
+  int bin, rem;
+  int sel_base, eq_base;
+  float stat[2];
+  int scan[33];
+  int2 cnt;                           // this CTA's keys above / equal to T (read by the cluster)
+  float part[kMaxItemsPerCta];        // this CTA's encoder items
+  float r[kMaxLatent], u[kMaxLatent], z[kMaxLatent];
+  uint32_t keys[kSliceCap];
+  int hist[kTop];                     // this CTA's 12-bit histogram (read by the cluster)
+  int tot[kTop];                      // the row's 12-bit histogram
+  int h2[kLow];                       // this CTA's 10-bit histogram (read by the cluster)
+  int h3[kLow];                       // this CTA's last-10-bit histogram (read by the cluster)
+  int tot2[kLow];
+};
+// Followed, 128-byte aligned, by the prefetched weights: fc1 | fc2 (when
+// prefetched) | head slice (when prefetched).
+
+__device__ __forceinline__ void bulk_copy(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_addr(dst)),
+               "l"(src), "r"(bytes), "r"(smem_addr(bar))
+               : "memory");
+}
+
+struct ClusterArgs {
+  SelArgs a;
+  int fc_smem;     // fc1 / fc2 are prefetched into shared memory
+  int head_smem;   // the head slice is prefetched into shared memory
+  uint32_t fc_bytes;    // bytes of one of fc1 / fc2
+  uint32_t head_off;    // offset of the head slice after the fc weights
+};
+
+template <typename T>
+__global__ void __launch_bounds__(kCThreads, 1) score_select_cluster_kernel(const ClusterArgs ca) {
+  namespace cg = cooperative_groups;
+  const SelArgs& a = ca.a;
+  extern __shared__ __align__(128) uint8_t cs_raw[];
+  ClusterSmem& sm = *reinterpret_cast<ClusterSmem*>(cs_raw);
+  uint8_t* wbuf = cs_raw + (sizeof(ClusterSmem) + 127) / 128 * 128;
+  cg::cluster_group cluster = cg::this_cluster();
+  const int tid = threadIdx.x;
+  const int lane = tid & 31;
+  const int warp = tid >> 5;
+  constexpr int kW = kCThreads / 32;
+  const int rank = static_cast<int>(cluster.block_rank());
+  const int row = blockIdx.x / kCluster;
+  const int L = a.latent;
+  const int H = a.hidden;
+  const int N = a.n;
+  const int n0 = static_cast<int>((static_cast<int64_t>(N) * rank) / kCluster);
+  const int n1 = static_cast<int>((static_cast<int64_t>(N) * (rank + 1)) / kCluster);
+  const int len = n1 - n0;
+  const int items = L * a.nchunk;
+  const T* fc1s = reinterpret_cast<const T*>(wbuf);
+  const T* fc2s = reinterpret_cast<const T*>(wbuf + ca.fc_bytes);
+  const T* heads = reinterpret_cast<const T*>(wbuf + ca.head_off);
+
+  // Prefetch: one thread starts the bulk copies of the weights this CTA needs
+  // after the encoder.
+  const uint32_t head_bytes = static_cast<uint32_t>(len) * L * sizeof(T);
+  const uint32_t expect = (ca.fc_smem ? 2 * ca.fc_bytes : 0u) + (ca.head_smem ? head_bytes : 0u);
+  if (tid == 0 && expect > 0) {
+    mbar_init(&sm.bar, 1);
+    fence_barrier_init();
+    mbar_arrive_expect_tx(&sm.bar, expect);
+    if (ca.fc_smem) {
+      bulk_copy(wbuf, a.fc1_w, ca.fc_bytes, &sm.bar);
+      bulk_copy(wbuf + ca.fc_bytes, a.fc2_w, ca.fc_bytes, &sm.bar);
+    }
+    if (ca.head_smem) {
+      const uint8_t* src = static_cast<const uint8_t*>(a.out_w) + static_cast<size_t>(n0) * L * sizeof(T);
+      for (uint32_t off = 0; off < head_bytes; off += kBulkChunk)
+        bulk_copy(wbuf + ca.head_off + off, src + off, min(kBulkChunk, head_bytes - off), &sm.bar);
+    }
+  }
+
+  // 1. Encoder items i = rank, rank + kCluster, ... over this CTA's warps.
+  {
+    const T* xr = reinterpret_cast<const T*>(a.x) + static_cast<int64_t>(row) * a.ldx;
+    for (int j = warp; rank + kCluster * j < items; j += kW) {
+      const int item = rank + kCluster * j;
+      const int l = item / a.nchunk;
+      const int h0 = (item - l * a.nchunk) * kEncChunk;
+      float acc = 0.f;
+#pragma unroll
+      for (int e = 0; e < kEncChunk / 32; ++e) {
+        const int h = h0 + lane + 32 * e;
+        if (h < H) acc = fmaf(to_f32<T>(xr[h]), ld_f<T>(a.enc_w, static_cast<int64_t>(l) * H + h), acc);
+      }
+      acc = warp_sum(acc);
+      if (lane == 0) sm.part[j] = acc;
+    }
+  }
+  for (int b = tid; b < kTop; b += kCThreads) sm.hist[b] = 0;
+  cluster.sync();
+
+  // 2. Latent MLP (identical in every CTA of the row), this slice's scores.
+  for (int l = tid; l < L; l += kCThreads) {
+    float pre = ld_opt<T>(a.enc_b, l, 0.f);
+    for (int c = 0; c < a.nchunk; ++c) {
+      const int item = l * a.nchunk + c;
+      pre += cluster.map_shared_rank(sm.part, item % kCluster)[item / kCluster];
+    }
+    if (a.kind == 0)
+      sm.r[l] = silu_f(pre);
+    else
+      sm.z[l] = pre;
+  }
+  // Every thread observes the copies' completion before reading them.
+  const bool have = __syncthreads_and(expect == 0 || mbar_wait_bounded(&sm.bar, 0, kWaitLimitNs)) != 0;
+  if (!have && tid == 0) atomicOr(a.status, QCC_DEV_TIMEOUT);
+  if (a.kind == 0) {
+    for (int l = tid; l < L; l += kCThreads) {
+      const float acc = ca.fc_smem ? (have ? dot_row_smem<T>(fc1s + static_cast<int64_t>(l) * L, sm.r, L) : 0.f)
+                                   : dot_row<T>(reinterpret_cast<const T*>(a.fc1_w) + static_cast<int64_t>(l) * L,
+                                                sm.r, L, a.vec_fc);
+      sm.u[l] = silu_f(acc + ld_opt<T>(a.fc1_b, l, 0.f));
+    }
+    __syncthreads();
+    for (int l = tid; l < L; l += kCThreads) {
+      const float acc = ca.fc_smem ? (have ? dot_row_smem<T>(fc2s + static_cast<int64_t>(l) * L, sm.u, L) : 0.f)
+                                   : dot_row<T>(reinterpret_cast<const T*>(a.fc2_w) + static_cast<int64_t>(l) * L,
+                                                sm.u, L, a.vec_fc);
+      sm.z[l] = acc + ld_opt<T>(a.fc2_b, l, 0.f) + sm.r[l];
+    }
+    __syncthreads();
+    if (warp == 0) {
+      float sum = 0.f;
+      for (int j = lane; j < L; j += 32) sum += sm.z[j];
+      const float mean = warp_sum(sum) / static_cast<float>(L);
+      float sq = 0.f;
+      for (int j = lane; j < L; j += 32) {
+        const float d = sm.z[j] - mean;
+        sq = fmaf(d, d, sq);
+      }
+      const float var = warp_sum(sq) / static_cast<float>(L);
+      if (lane == 0) {
+        sm.stat[0] = mean;
+        sm.stat[1] = rsqrtf(var + a.eps);
+      }
+    }
+    __syncthreads();
+    for (int l = tid; l < L; l += kCThreads)
+      sm.z[l] = (sm.z[l] - sm.stat[0]) * sm.stat[1] * ld_opt<T>(a.ln_w, l, 1.f) + ld_opt<T>(a.ln_b, l, 0.f);
+  }
+  __syncthreads();
+  for (int i = tid; i < len; i += kCThreads) {
+    const int n = n0 + i;
+    float acc;
+    if (ca.head_smem)
+      acc = have ? dot_row_smem<T>(heads + static_cast<int64_t>(i) * L, sm.z, L) : 0.f;
+    else
+      acc = dot_row<T>(reinterpret_cast<const T*>(a.out_w) + static_cast<int64_t>(n) * L, sm.z, L, a.vec_out);
+    const float sc = acc + ld_opt<T>(a.out_b, n, 0.f);
+    sm.keys[i] = score_key(sc);
+    if (a.scores != nullptr) a.scores[static_cast<int64_t>(row) * a.ld_scores + n] = sc;
+  }
+  __syncthreads();
+  for (int i = tid; i < len; i += kCThreads) atomicAdd(&sm.hist[sm.keys[i] >> 20], 1);
+  for (int b = tid; b < kLow; b += kCThreads) {
+    sm.h2[b] = 0;
+    sm.h3[b] = 0;
+  }
+  cluster.sync();
+
+  // 3. The row's 12-bit histogram, bin by bin over the cluster; bin of the k-th key.
+  for (int b = tid; b < kTop; b += kCThreads) {
+    int t = 0;
+#pragma unroll
+    for (int q = 0; q < kCluster; ++q) t += cluster.map_shared_rank(sm.hist, q)[b];
+    sm.tot[b] = t;
+  }
+  __syncthreads();
+  find_bin<kTop / kCThreads>(sm.tot, a.k, sm.scan, &sm.bin, &sm.rem);
+  __syncthreads();
+  const uint32_t bin = static_cast<uint32_t>(sm.bin);
+  const int rem = sm.rem;
+  for (int i = tid; i < len; i += kCThreads)
+    if ((sm.keys[i] >> 20) == bin) atomicAdd(&sm.h2[(sm.keys[i] >> 10) & (kLow - 1)], 1);
+  cluster.sync();
+
+  // 4. Next 10 bits over the cluster's candidates.
+  for (int b = tid; b < kLow; b += kCThreads) {
+    int t = 0;
+#pragma unroll
+    for (int q = 0; q < kCluster; ++q) t += cluster.map_shared_rank(sm.h2, q)[b];
+    sm.tot2[b] = t;
+  }
+  __syncthreads();
+  find_bin<kLow / kCThreads>(sm.tot2, rem, sm.scan, &sm.bin, &sm.rem);
+  __syncthreads();
+  const uint32_t prefix = (bin << 10) | static_cast<uint32_t>(sm.bin);
+  const int rem_a = sm.rem;
+  __syncthreads();
+  for (int i = tid; i < len; i += kCThreads)
+    if ((sm.keys[i] >> 10) == prefix) atomicAdd(&sm.h3[sm.keys[i] & (kLow - 1)], 1);
+  cluster.sync();
+
+  // 5. Last 10 bits: the exact k-th key T and the ties still needed.
+  for (int b = tid; b < kLow; b += kCThreads) {
+    int t = 0;
+#pragma unroll
+    for (int q = 0; q < kCluster; ++q) t += cluster.map_shared_rank(sm.h3, q)[b];
+    sm.tot2[b] = t;
+  }
+  __syncthreads();
+  find_bin<kLow / kCThreads>(sm.tot2, rem_a, sm.scan, &sm.bin, &sm.rem);
+  __syncthreads();
+  const uint32_t thr = (prefix << 10) | static_cast<uint32_t>(sm.bin);
+  const int need_eq = sm.rem;
+  int gt = 0, eqc = 0;
+  for (int i = tid; i < len; i += kCThreads) {
+    gt += sm.keys[i] > thr ? 1 : 0;
+    eqc += sm.keys[i] == thr ? 1 : 0;
+  }
+  int tot_gt, tot_eq;
+  (void)block_exclusive_scan(gt, sm.scan, &tot_gt);
+  (void)block_exclusive_scan(eqc, sm.scan, &tot_eq);
+  if (tid == 0) sm.cnt = make_int2(tot_gt, tot_eq);
+  cluster.sync();
+
+  // 6. Offsets from the earlier CTAs' counts; selected indices, ascending.
+  if (tid == 0) {
+    int sel = 0, eqb = 0;
+    for (int q = 0; q < rank; ++q) {
+      const int2 c = *cluster.map_shared_rank(&sm.cnt, q);
+      sel += c.x + min(c.y, max(0, need_eq - eqb));
+      eqb += c.y;
+    }
+    sm.sel_base = sel;
+    sm.eq_base = eqb;
+  }
+  __syncthreads();
+  const int per = (len + kCThreads - 1) / kCThreads;
+  const int c0 = min(len, tid * per), c1 = min(len, c0 + per);
+  int eq = 0;
+  for (int i = c0; i < c1; ++i) eq += sm.keys[i] == thr ? 1 : 0;
+  int tot;
+  const int eq_before = sm.eq_base + block_exclusive_scan(eq, sm.scan, &tot);
+  int sel = 0;
+  {
+    int e = eq_before;
+    for (int i = c0; i < c1; ++i) {
+      const uint32_t key = sm.keys[i];
+      if (key > thr) {
+        ++sel;
+      } else if (key == thr) {
+        sel += e < need_eq ? 1 : 0;
+        ++e;
+      }
+    }
+  }
+  int pos = sm.sel_base + block_exclusive_scan(sel, sm.scan, &tot);
+  int32_t* out = a.ids + static_cast<int64_t>(row) * a.ld_ids;
+  int e = eq_before;
+  for (int i = c0; i < c1; ++i) {
+    const uint32_t key = sm.keys[i];
+    bool take = key > thr;
+    if (key == thr) {
+      take = e < need_eq;
+      ++e;
+    }
+    if (take) out[pos++] = n0 + i;
+  }
+  // No CTA leaves while another may still read its shared memory, nor with
+  // its own bulk copies still in flight (after a timed-out wait).
+  if (!have && tid == 0) (void)mbar_wait_bounded(&sm.bar, 0, kWaitLimitNs);
+  cluster.sync();
+}
+
+// Whether a cluster of kCluster CTAs with this much shared memory can be
+// scheduled on the device (asked once per kernel, device and size: the
+// answer is cached, so later calls -- also under stream capture -- make no
+// query).
+template <typename Query>
+bool cluster_fits(const void* fn, int device, size_t smem, Query query) {
+  static std::mutex mu;
+  static std::unordered_map<std::string, bool> known;
+  std::string key(reinterpret_cast<const char*>(&fn), sizeof(fn));
+  key.append(reinterpret_cast<const char*>(&device), sizeof(device));
+  key.append(reinterpret_cast<const char*>(&smem), sizeof(smem));
+  std::lock_guard<std::mutex> lock(mu);
+  auto it = known.find(key);
+  if (it != known.end()) return it->second;
+  int clusters = 0;
+  clear_stale_error();
+  const bool ok = query(&clusters) == cudaSuccess && clusters > 0;
+  clear_stale_error();
+  known.emplace(key, ok);
+  return ok;
+}
+
 struct SelLayout {
   size_t enc, hist, cand, counts, total;
 };
@@ -492,6 +834,59 @@ extern "C" int qcc_selector_scores_topk(const void* x, int64_t ldx, int batch, i
   args.cand = reinterpret_cast<uint2*>(ws + lay.cand);
   args.counts = reinterpret_cast<int2*>(ws + lay.counts);
   const size_t esize = dtype == QCC_DTYPE_F32 ? 4 : 2;
+
+  // Cluster path: the row's neurons fit the cluster's shared memory.
+  if (n_out <= kCluster * kSliceCap && (latent * args.nchunk + kCluster - 1) / kCluster <= kMaxItemsPerCta) {
+    ClusterArgs ca;
+    ca.a = args;
+    ca.a.x = x;
+    ca.a.ldx = ldx;
+    ca.a.rows = batch;
+    ca.a.ids = ids;
+    ca.a.scores = scores;
+    ca.a.cpr = kCluster;
+    const size_t base = (sizeof(ClusterSmem) + 127) / 128 * 128;
+    const size_t fc_bytes = static_cast<size_t>(latent) * latent * esize;
+    const size_t slice_max = static_cast<size_t>((n_out + kCluster - 1) / kCluster) * latent * esize;
+    const size_t limit = static_cast<size_t>(info.max_smem_optin);
+    ca.fc_smem = kind == 0 && fc_bytes % 16 == 0 && aligned16(fc1_w) && aligned16(fc2_w) &&
+                 base + 2 * fc_bytes <= limit;
+    ca.fc_bytes = static_cast<uint32_t>(fc_bytes);
+    const size_t head_off = ca.fc_smem ? (2 * fc_bytes + 127) / 128 * 128 : 0;
+    ca.head_off = static_cast<uint32_t>(head_off);
+    ca.head_smem = (static_cast<size_t>(latent) * esize) % 16 == 0 && aligned16(out_w) &&
+                   base + head_off + slice_max <= limit;
+    const size_t smem = base + head_off + (ca.head_smem ? slice_max : 0);
+    void (*cfn)(const ClusterArgs) = nullptr;
+    if (dtype == QCC_DTYPE_BF16)
+      cfn = score_select_cluster_kernel<__nv_bfloat16>;
+    else if (dtype == QCC_DTYPE_F16)
+      cfn = score_select_cluster_kernel<__half>;
+    else
+      cfn = score_select_cluster_kernel<float>;
+    if (smem <= limit && ensure_max_dynamic_smem(reinterpret_cast<const void*>(cfn), device)) {
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(static_cast<unsigned>(kCluster * batch));
+      cfg.blockDim = dim3(kCThreads);
+      cfg.dynamicSmemBytes = smem;
+      cfg.stream = stream;
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = kCluster;
+      attr[0].val.clusterDim.y = 1;
+      attr[0].val.clusterDim.z = 1;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      if (cluster_fits(reinterpret_cast<const void*>(cfn), device, smem, [&](int* clusters) {
+            return cudaOccupancyMaxActiveClusters(clusters, cfn, &cfg);
+          })) {
+        clear_stale_error();
+        if (!cuda_ok(cudaLaunchKernelEx(&cfg, cfn, ca))) return QCC_ERR_CUDA;
+        return QCC_OK;
+      }
+      clear_stale_error();  // no cluster of this size fits: the grid path below
+    }
+  }
 
   for (int r0 = 0; r0 < batch; r0 += kMaxRows) {
     const int rows = std::min(kMaxRows, batch - r0);

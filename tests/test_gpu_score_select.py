@@ -119,3 +119,29 @@ def test_mirrors_of_the_reference_classes():
     assert np.abs(got - raw).max() <= SCORE_TOL * max(1.0, np.abs(raw).max())
     with pytest.raises(ValueError, match="batch"):
         cuda.scores(x[0])
+
+
+@pytest.mark.parametrize("n,latent,dtype", [
+    (40000, 32, torch.bfloat16),   # beyond one cluster's shared memory: the grid-wide kernel
+    (17408, 64, torch.float32),    # cluster kernel, head rows read from global memory
+    (17408, 36, torch.float16),    # latent not a multiple of 8: scalar weight rows
+])
+def test_both_kernel_paths(n, latent, dtype):
+    g = torch.Generator().manual_seed(n + latent)
+    h = 1000
+    p = {"enc_w": torch.randn(latent, h, generator=g) * 0.05, "enc_b": torch.randn(latent, generator=g) * 0.1,
+         "fc1_w": torch.randn(latent, latent, generator=g) * 0.2, "fc1_b": torch.randn(latent, generator=g) * 0.1,
+         "fc2_w": torch.randn(latent, latent, generator=g) * 0.2, "fc2_b": None,
+         "ln_w": 1 + 0.1 * torch.randn(latent, generator=g), "ln_b": None,
+         "out_w": torch.randn(n, latent, generator=g) * 0.2, "out_b": torch.randn(n, generator=g) * 0.1}
+    p = {a: (None if b is None else b.numpy()) for a, b in p.items()}
+    k = opred.retention_count(n, 0.3)
+    eng = _engine(p, 0, k, dtype)
+    x = torch.randn(2, h, generator=g).cuda()
+    for _ in range(2):  # the second call checks the workspace was left clean
+        scores, ids = eng.run(x)
+        eng.check()
+        ref = opred.predictor_scores(x.to(dtype).double().cpu().numpy(), _rounded(p, dtype), "residual")
+        got = scores.double().cpu().numpy()
+        assert np.abs(got - ref).max() <= SCORE_TOL * max(1.0, np.abs(ref).max())
+        _check_selection(ids.cpu().numpy(), scores.cpu().numpy(), ref, k)
