@@ -35,6 +35,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cstddef>
 #include <mutex>
 #include <string>
 #include <unordered_map>
@@ -147,6 +148,29 @@ __device__ __forceinline__ float dot_row_smem(const T* w, const float* z, int L)
     }
   } else {
     for (int j = 0; j < L; ++j) acc = fmaf(to_f32<T>(w[j]), z[j], acc);
+  }
+  return acc;
+}
+
+// dot_row_smem for rows read one per thread: each thread starts at a
+// different 16-byte piece of its row, so that the eight threads of a
+// 128-byte shared-memory wavefront hit eight different bank groups (rows of
+// 64 bytes would otherwise put sixteen threads of a warp on the same banks).
+template <typename T>
+__device__ __forceinline__ float dot_row_smem_rot(const T* w, const float* z, int L, int t) {
+  if ((L & 7) != 0) return dot_row_smem<T>(w, z, L);
+  const int row_bytes = L * static_cast<int>(sizeof(T));
+  const int pieces = L / 8;  // 8-element pieces of the row
+  const int rot = row_bytes < 128 ? t / (128 / row_bytes) : t;
+  float acc = 0.f;
+#pragma unroll 4
+  for (int c = 0; c < pieces; ++c) {
+    int j = c + rot;
+    j %= pieces;
+    float f[8];
+    widen(load_pack8<T>(w + 8 * j), f);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc = fmaf(f[e], z[8 * j + e], acc);
   }
   return acc;
 }
@@ -453,12 +477,20 @@ struct ClusterSmem {
   int2 cnt;                           // this CTA's keys above / equal to T (read by the cluster)
   float part[kMaxItemsPerCta];        // this CTA's encoder items
   float r[kMaxLatent], u[kMaxLatent], z[kMaxLatent];
+  float vec[5][kMaxLatent];           // enc_b, fc1_b, fc2_b, ln_w, ln_b (staged at launch)
+  int2 cnts[kCluster];                // every CTA's counts, gathered
   uint32_t keys[kSliceCap];
-  int hist[kTop];                     // this CTA's 12-bit histogram (read by the cluster)
-  int tot[kTop];                      // the row's 12-bit histogram
-  int h2[kLow];                       // this CTA's 10-bit histogram (read by the cluster)
-  int h3[kLow];                       // this CTA's last-10-bit histogram (read by the cluster)
-  int tot2[kLow];
+  // This CTA's histograms, read by the whole cluster: each digit has fine bins
+  // and coarse bins (64 / 32 fine bins each), so that finding a bin reads the
+  // cluster's coarse bins and then only the fine bins of one coarse bin.
+  int hist[kTop];                     // 12-bit digit
+  int c1[kTop / 64];
+  int h2[kLow];                       // next 10 bits, candidates of the 12-bit bin
+  int c2[kLow / 32];
+  int h3[kLow];                       // last 10 bits
+  int c3[kLow / 32];
+  int gath[kCluster][64];             // bins gathered from the cluster
+  int sum[64];
 };
 // Followed, 128-byte aligned, by the prefetched weights: fc1 | fc2 (when
 // prefetched) | head slice (when prefetched).
@@ -477,6 +509,77 @@ struct ClusterArgs {
   uint32_t fc_bytes;    // bytes of one of fc1 / fc2
   uint32_t head_off;    // offset of the head slice after the fc weights
 };
+
+// Warp 0: the bin (of NB in cnt, visited from the highest) that holds the
+// rem-th largest element, and rem minus the elements in higher bins.
+template <int NB>
+__device__ __forceinline__ void warp_find(const int* cnt, int rem, int* out_bin, int* out_rem) {
+  constexpr int PER = NB / 32;
+  const int lane = threadIdx.x & 31;
+  const int top = NB - 1 - PER * lane;
+  int c[PER];
+  int s = 0;
+#pragma unroll
+  for (int j = 0; j < PER; ++j) {
+    c[j] = cnt[top - j];
+    s += c[j];
+  }
+  int x = s;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  int above = x - s;
+#pragma unroll
+  for (int j = 0; j < PER; ++j) {
+    if (above < rem && above + c[j] >= rem) {
+      *out_bin = top - j;
+      *out_rem = rem - above;
+    }
+    above += c[j];
+  }
+}
+
+// All threads: the bin of the rem-th largest key of a digit whose per-CTA
+// histograms (fine[NC * W], coarse[NC]) live in the cluster's CTAs.  Two
+// gathers of one remote word per thread: the coarse bins, then the W fine
+// bins of the chosen coarse bin.  Returns the fine bin; *rem_out the rank
+// left inside it.
+template <int NC, int W>
+__device__ __forceinline__ int cluster_find(cooperative_groups::cluster_group& cluster, ClusterSmem& sm, int* fine,
+                                            int* coarse, int rem, int* rem_out) {
+  static_assert(NC <= 64 && W <= 64 && kCluster * 64 <= kCThreads, "gather shape");
+  const int tid = threadIdx.x;
+  const int q = tid >> 6, j = tid & 63;
+  if (j < NC) sm.gath[q][j] = cluster.map_shared_rank(coarse, q)[j];
+  __syncthreads();
+  if (tid < NC) {
+    int t = 0;
+#pragma unroll
+    for (int r = 0; r < kCluster; ++r) t += sm.gath[r][tid];
+    sm.sum[tid] = t;
+  }
+  __syncthreads();
+  if (tid < 32) warp_find<NC>(sm.sum, rem, &sm.bin, &sm.rem);
+  __syncthreads();
+  const int cb = sm.bin, crem = sm.rem;
+  if (j < W) sm.gath[q][j] = cluster.map_shared_rank(fine, q)[cb * W + j];
+  __syncthreads();
+  if (tid < W) {
+    int t = 0;
+#pragma unroll
+    for (int r = 0; r < kCluster; ++r) t += sm.gath[r][tid];
+    sm.sum[tid] = t;
+  }
+  __syncthreads();
+  if (tid < 32) warp_find<W>(sm.sum, crem, &sm.bin, &sm.rem);
+  __syncthreads();
+  const int fb = cb * W + sm.bin;
+  *rem_out = sm.rem;
+  __syncthreads();  // sm.bin / sm.rem are written again by the next call
+  return fb;
+}
 
 template <typename T>
 __global__ void __launch_bounds__(kCThreads, 1) score_select_cluster_kernel(const ClusterArgs ca) {
@@ -522,29 +625,55 @@ __global__ void __launch_bounds__(kCThreads, 1) score_select_cluster_kernel(cons
     }
   }
 
-  // 1. Encoder items i = rank, rank + kCluster, ... over this CTA's warps.
+  // Small vectors and this thread's head biases are loaded now, so that no
+  // global round trip sits inside the dependent chain after the encoder.
+  for (int l = tid; l < L; l += kCThreads) {
+    sm.vec[0][l] = ld_opt<T>(a.enc_b, l, 0.f);
+    sm.vec[1][l] = ld_opt<T>(a.fc1_b, l, 0.f);
+    sm.vec[2][l] = ld_opt<T>(a.fc2_b, l, 0.f);
+    sm.vec[3][l] = ld_opt<T>(a.ln_w, l, 1.f);
+    sm.vec[4][l] = ld_opt<T>(a.ln_b, l, 0.f);
+  }
+  constexpr int kPerThread = kSliceCap / kCThreads;
+  float bias[kPerThread];
+#pragma unroll
+  for (int q = 0; q < kPerThread; ++q) {
+    const int i = tid + q * kCThreads;
+    bias[q] = i < len ? ld_opt<T>(a.out_b, n0 + i, 0.f) : 0.f;
+  }
+
+  // 1. Encoder items i = rank, rank + kCluster, ... over this CTA's warps,
+  //    two items per warp at a time (all their loads in flight together).
   {
     const T* xr = reinterpret_cast<const T*>(a.x) + static_cast<int64_t>(row) * a.ldx;
-    for (int j = warp; rank + kCluster * j < items; j += kW) {
-      const int item = rank + kCluster * j;
-      const int l = item / a.nchunk;
-      const int h0 = (item - l * a.nchunk) * kEncChunk;
-      float acc = 0.f;
+    for (int j = warp; rank + kCluster * j < items; j += 2 * kW) {
+      const int j2 = j + kW;
+      const bool two = rank + kCluster * j2 < items;
+      const int item = rank + kCluster * j, item2 = rank + kCluster * (two ? j2 : j);
+      const int l = item / a.nchunk, l2 = item2 / a.nchunk;
+      const int h0 = (item - l * a.nchunk) * kEncChunk, h02 = (item2 - l2 * a.nchunk) * kEncChunk;
+      float acc = 0.f, acc2 = 0.f;
 #pragma unroll
       for (int e = 0; e < kEncChunk / 32; ++e) {
-        const int h = h0 + lane + 32 * e;
+        const int h = h0 + lane + 32 * e, hb = h02 + lane + 32 * e;
         if (h < H) acc = fmaf(to_f32<T>(xr[h]), ld_f<T>(a.enc_w, static_cast<int64_t>(l) * H + h), acc);
+        if (hb < H) acc2 = fmaf(to_f32<T>(xr[hb]), ld_f<T>(a.enc_w, static_cast<int64_t>(l2) * H + hb), acc2);
       }
       acc = warp_sum(acc);
-      if (lane == 0) sm.part[j] = acc;
+      acc2 = warp_sum(acc2);
+      if (lane == 0) {
+        sm.part[j] = acc;
+        if (two) sm.part[j2] = acc2;
+      }
     }
   }
   for (int b = tid; b < kTop; b += kCThreads) sm.hist[b] = 0;
+  if (tid < kTop / 64) sm.c1[tid] = 0;
   cluster.sync();
 
   // 2. Latent MLP (identical in every CTA of the row), this slice's scores.
   for (int l = tid; l < L; l += kCThreads) {
-    float pre = ld_opt<T>(a.enc_b, l, 0.f);
+    float pre = sm.vec[0][l];
     for (int c = 0; c < a.nchunk; ++c) {
       const int item = l * a.nchunk + c;
       pre += cluster.map_shared_rank(sm.part, item % kCluster)[item / kCluster];
@@ -562,14 +691,14 @@ __global__ void __launch_bounds__(kCThreads, 1) score_select_cluster_kernel(cons
       const float acc = ca.fc_smem ? (have ? dot_row_smem<T>(fc1s + static_cast<int64_t>(l) * L, sm.r, L) : 0.f)
                                    : dot_row<T>(reinterpret_cast<const T*>(a.fc1_w) + static_cast<int64_t>(l) * L,
                                                 sm.r, L, a.vec_fc);
-      sm.u[l] = silu_f(acc + ld_opt<T>(a.fc1_b, l, 0.f));
+      sm.u[l] = silu_f(acc + sm.vec[1][l]);
     }
     __syncthreads();
     for (int l = tid; l < L; l += kCThreads) {
       const float acc = ca.fc_smem ? (have ? dot_row_smem<T>(fc2s + static_cast<int64_t>(l) * L, sm.u, L) : 0.f)
                                    : dot_row<T>(reinterpret_cast<const T*>(a.fc2_w) + static_cast<int64_t>(l) * L,
                                                 sm.u, L, a.vec_fc);
-      sm.z[l] = acc + ld_opt<T>(a.fc2_b, l, 0.f) + sm.r[l];
+      sm.z[l] = acc + sm.vec[2][l] + sm.r[l];
     }
     __syncthreads();
     if (warp == 0) {
@@ -589,89 +718,90 @@ __global__ void __launch_bounds__(kCThreads, 1) score_select_cluster_kernel(cons
     }
     __syncthreads();
     for (int l = tid; l < L; l += kCThreads)
-      sm.z[l] = (sm.z[l] - sm.stat[0]) * sm.stat[1] * ld_opt<T>(a.ln_w, l, 1.f) + ld_opt<T>(a.ln_b, l, 0.f);
+      sm.z[l] = (sm.z[l] - sm.stat[0]) * sm.stat[1] * sm.vec[3][l] + sm.vec[4][l];
   }
   __syncthreads();
-  for (int i = tid; i < len; i += kCThreads) {
+#pragma unroll
+  for (int q = 0; q < kPerThread; ++q) {
+    const int i = tid + q * kCThreads;
+    if (i >= len) break;
     const int n = n0 + i;
     float acc;
     if (ca.head_smem)
-      acc = have ? dot_row_smem<T>(heads + static_cast<int64_t>(i) * L, sm.z, L) : 0.f;
+      acc = have ? dot_row_smem_rot<T>(heads + static_cast<int64_t>(i) * L, sm.z, L, tid) : 0.f;
     else
       acc = dot_row<T>(reinterpret_cast<const T*>(a.out_w) + static_cast<int64_t>(n) * L, sm.z, L, a.vec_out);
-    const float sc = acc + ld_opt<T>(a.out_b, n, 0.f);
+    const float sc = acc + bias[q];
     sm.keys[i] = score_key(sc);
     if (a.scores != nullptr) a.scores[static_cast<int64_t>(row) * a.ld_scores + n] = sc;
   }
   __syncthreads();
+  // The coarse bins are few and hot, so they are summed from the fine bins
+  // rather than counted with atomics of their own.
   for (int i = tid; i < len; i += kCThreads) atomicAdd(&sm.hist[sm.keys[i] >> 20], 1);
+  __syncthreads();
+  if (tid < kTop / 64) {
+    int t = 0;
+    for (int b = 0; b < 64; ++b) t += sm.hist[tid * 64 + b];
+    sm.c1[tid] = t;
+  }
   for (int b = tid; b < kLow; b += kCThreads) {
     sm.h2[b] = 0;
     sm.h3[b] = 0;
   }
+  if (tid < kLow / 32) {
+    sm.c2[tid] = 0;
+    sm.c3[tid] = 0;
+  }
   cluster.sync();
 
-  // 3. The row's 12-bit histogram, bin by bin over the cluster; bin of the k-th key.
-  for (int b = tid; b < kTop; b += kCThreads) {
-    int t = 0;
-#pragma unroll
-    for (int q = 0; q < kCluster; ++q) t += cluster.map_shared_rank(sm.hist, q)[b];
-    sm.tot[b] = t;
-  }
-  __syncthreads();
-  find_bin<kTop / kCThreads>(sm.tot, a.k, sm.scan, &sm.bin, &sm.rem);
-  __syncthreads();
-  const uint32_t bin = static_cast<uint32_t>(sm.bin);
-  const int rem = sm.rem;
+  // 3. The bin of the k-th key in the row's 12-bit histogram.
+  int rem;
+  const uint32_t bin = static_cast<uint32_t>(cluster_find<kTop / 64, 64>(cluster, sm, sm.hist, sm.c1, a.k, &rem));
   for (int i = tid; i < len; i += kCThreads)
-    if ((sm.keys[i] >> 20) == bin) atomicAdd(&sm.h2[(sm.keys[i] >> 10) & (kLow - 1)], 1);
+    if ((sm.keys[i] >> 20) == bin) {
+      atomicAdd(&sm.h2[(sm.keys[i] >> 10) & (kLow - 1)], 1);
+      atomicAdd(&sm.c2[(sm.keys[i] >> 15) & 31], 1);
+    }
   cluster.sync();
 
   // 4. Next 10 bits over the cluster's candidates.
-  for (int b = tid; b < kLow; b += kCThreads) {
-    int t = 0;
-#pragma unroll
-    for (int q = 0; q < kCluster; ++q) t += cluster.map_shared_rank(sm.h2, q)[b];
-    sm.tot2[b] = t;
-  }
-  __syncthreads();
-  find_bin<kLow / kCThreads>(sm.tot2, rem, sm.scan, &sm.bin, &sm.rem);
-  __syncthreads();
-  const uint32_t prefix = (bin << 10) | static_cast<uint32_t>(sm.bin);
-  const int rem_a = sm.rem;
-  __syncthreads();
+  int rem_a;
+  const uint32_t prefix =
+      (bin << 10) | static_cast<uint32_t>(cluster_find<kLow / 32, 32>(cluster, sm, sm.h2, sm.c2, rem, &rem_a));
   for (int i = tid; i < len; i += kCThreads)
-    if ((sm.keys[i] >> 10) == prefix) atomicAdd(&sm.h3[sm.keys[i] & (kLow - 1)], 1);
+    if ((sm.keys[i] >> 10) == prefix) {
+      atomicAdd(&sm.h3[sm.keys[i] & (kLow - 1)], 1);
+      atomicAdd(&sm.c3[(sm.keys[i] >> 5) & 31], 1);
+    }
   cluster.sync();
 
   // 5. Last 10 bits: the exact k-th key T and the ties still needed.
-  for (int b = tid; b < kLow; b += kCThreads) {
-    int t = 0;
-#pragma unroll
-    for (int q = 0; q < kCluster; ++q) t += cluster.map_shared_rank(sm.h3, q)[b];
-    sm.tot2[b] = t;
-  }
-  __syncthreads();
-  find_bin<kLow / kCThreads>(sm.tot2, rem_a, sm.scan, &sm.bin, &sm.rem);
-  __syncthreads();
-  const uint32_t thr = (prefix << 10) | static_cast<uint32_t>(sm.bin);
-  const int need_eq = sm.rem;
+  int need_eq;
+  const uint32_t thr =
+      (prefix << 10) | static_cast<uint32_t>(cluster_find<kLow / 32, 32>(cluster, sm, sm.h3, sm.c3, rem_a, &need_eq));
+  // Counts above / equal to T over this thread's contiguous chunk (index
+  // order), both prefix-summed by one scan of (above << 16 | equal).
+  const int per = (len + kCThreads - 1) / kCThreads;
+  const int c0 = min(len, tid * per), c1 = min(len, c0 + per);
   int gt = 0, eqc = 0;
-  for (int i = tid; i < len; i += kCThreads) {
+  for (int i = c0; i < c1; ++i) {
     gt += sm.keys[i] > thr ? 1 : 0;
     eqc += sm.keys[i] == thr ? 1 : 0;
   }
-  int tot_gt, tot_eq;
-  (void)block_exclusive_scan(gt, sm.scan, &tot_gt);
-  (void)block_exclusive_scan(eqc, sm.scan, &tot_eq);
-  if (tid == 0) sm.cnt = make_int2(tot_gt, tot_eq);
+  int packed_tot;
+  const int packed_before = block_exclusive_scan((gt << 16) | eqc, sm.scan, &packed_tot);
+  const int gt_before = packed_before >> 16, eq_before_cta = packed_before & 0xFFFF;
+  if (tid == 0) sm.cnt = make_int2(packed_tot >> 16, packed_tot & 0xFFFF);
   cluster.sync();
 
   // 6. Offsets from the earlier CTAs' counts; selected indices, ascending.
+  if (tid < kCluster) sm.cnts[tid] = *cluster.map_shared_rank(&sm.cnt, tid);
+  __syncthreads();
   if (tid == 0) {
     int sel = 0, eqb = 0;
     for (int q = 0; q < rank; ++q) {
-      const int2 c = *cluster.map_shared_rank(&sm.cnt, q);
+      const int2 c = sm.cnts[q];
       sel += c.x + min(c.y, max(0, need_eq - eqb));
       eqb += c.y;
     }
@@ -679,26 +809,10 @@ __global__ void __launch_bounds__(kCThreads, 1) score_select_cluster_kernel(cons
     sm.eq_base = eqb;
   }
   __syncthreads();
-  const int per = (len + kCThreads - 1) / kCThreads;
-  const int c0 = min(len, tid * per), c1 = min(len, c0 + per);
-  int eq = 0;
-  for (int i = c0; i < c1; ++i) eq += sm.keys[i] == thr ? 1 : 0;
-  int tot;
-  const int eq_before = sm.eq_base + block_exclusive_scan(eq, sm.scan, &tot);
-  int sel = 0;
-  {
-    int e = eq_before;
-    for (int i = c0; i < c1; ++i) {
-      const uint32_t key = sm.keys[i];
-      if (key > thr) {
-        ++sel;
-      } else if (key == thr) {
-        sel += e < need_eq ? 1 : 0;
-        ++e;
-      }
-    }
-  }
-  int pos = sm.sel_base + block_exclusive_scan(sel, sm.scan, &tot);
+  // Ties are taken lowest index first: of this CTA's ties before this
+  // thread's chunk, those still needed after the earlier CTAs' ties count.
+  const int eq_before = sm.eq_base + eq_before_cta;
+  int pos = sm.sel_base + gt_before + min(eq_before_cta, max(0, need_eq - sm.eq_base));
   int32_t* out = a.ids + static_cast<int64_t>(row) * a.ld_ids;
   int e = eq_before;
   for (int i = c0; i < c1; ++i) {
