@@ -682,17 +682,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t col0 = lane_base + j * kAccCols;
       if (ks > 0) {
         // Not this unit's first K steps: hand the accumulators to the CTA that finishes it.
-        // Column-major slot (column * 128 + row): the 32 rows of a warp store
-        // one 128-byte line per column.
-        float* slot = a.partials + static_cast<size_t>(blockIdx.x) * kSlotFloats;
+        // Column-quad-major slot (float4 of columns 4m..4m+3 at m * 128 + row):
+        // the 32 rows of a warp store 512 contiguous bytes per instruction.
+        float4* slot = reinterpret_cast<float4*>(a.partials + static_cast<size_t>(blockIdx.x) * kSlotFloats);
         for (int i = 0; i < nt; ++i) {
-          float* dst = slot + static_cast<size_t>(i) * 128 * 128 + row;
+          float4* dst = slot + static_cast<size_t>(i) * 32 * 128 + row;
 #pragma unroll 1
           for (int c = 0; c < 4; ++c) {
             float v[32];
             tmem_load32(col0 + i * 128u + c * 32u, v);
 #pragma unroll
-            for (int e = 0; e < 32; ++e) __stcg(dst + (c * 32 + e) * 128, v[e]);
+            for (int e = 0; e < 8; ++e)
+              __stcg(dst + (c * 8 + e) * 128, make_float4(v[4 * e], v[4 * e + 1], v[4 * e + 2], v[4 * e + 3]));
           }
         }
         __threadfence();
@@ -712,12 +713,15 @@ __global__ void __launch_bounds__(kThreads, 1)
             tmem_load32(col0 + i * 128u + 64u + c * 32u, v);
             if (wait_others) {
               for (int ci = 0; ci < ctl->r.n_contrib[0]; ++ci) {
-                const float* p = a.partials + static_cast<size_t>(ctl->r.contrib[0][ci]) * kSlotFloats +
-                                 static_cast<size_t>(i) * 128 * 128 + row;
+                const float4* p = reinterpret_cast<const float4*>(
+                                      a.partials + static_cast<size_t>(ctl->r.contrib[0][ci]) * kSlotFloats) +
+                                  static_cast<size_t>(i) * 32 * 128 + row;
 #pragma unroll
-                for (int e = 0; e < 32; ++e) {
-                  g[e] += __ldcg(p + (c * 32 + e) * 128);
-                  v[e] += __ldcg(p + (64 + c * 32 + e) * 128);
+                for (int e = 0; e < 8; ++e) {
+                  const float4 pg = __ldcg(p + (c * 8 + e) * 128);
+                  const float4 pu = __ldcg(p + (16 + c * 8 + e) * 128);
+                  g[4 * e] += pg.x, g[4 * e + 1] += pg.y, g[4 * e + 2] += pg.z, g[4 * e + 3] += pg.w;
+                  v[4 * e] += pu.x, v[4 * e + 1] += pu.y, v[4 * e + 2] += pu.z, v[4 * e + 3] += pu.w;
                 }
               }
             }
@@ -872,14 +876,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after_sync();
       const uint32_t col0 = lane_base + j * kAccCols;
       if (ks > 0) {
-        // Column-major slot, as in phase 1.
-        float* dst = a.partials + static_cast<size_t>(blockIdx.x) * kSlotFloats + row;
+        // Column-quad-major slot, as in phase 1.
+        float4* dst = reinterpret_cast<float4*>(a.partials + static_cast<size_t>(blockIdx.x) * kSlotFloats) + row;
 #pragma unroll 1
         for (int c = 0; c < 8; ++c) {
           float vv[32];
           tmem_load32(col0 + c * 32u, vv);
 #pragma unroll
-          for (int e = 0; e < 32; ++e) __stcg(dst + (c * 32 + e) * 128, vv[e]);
+          for (int e = 0; e < 8; ++e)
+            __stcg(dst + (c * 8 + e) * 128, make_float4(vv[4 * e], vv[4 * e + 1], vv[4 * e + 2], vv[4 * e + 3]));
         }
         __threadfence();
         epilogue_sync();
@@ -897,9 +902,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_load32(col0 + c * 32u, vv);
           if (wait_others) {
             for (int ci = 0; ci < ctl->r.n_contrib[1]; ++ci) {
-              const float* p = a.partials + static_cast<size_t>(ctl->r.contrib[1][ci]) * kSlotFloats + row;
+              const float4* p =
+                  reinterpret_cast<const float4*>(a.partials + static_cast<size_t>(ctl->r.contrib[1][ci]) * kSlotFloats) + row;
 #pragma unroll
-              for (int e = 0; e < 32; ++e) vv[e] += __ldcg(p + (c * 32 + e) * 128);
+              for (int e = 0; e < 8; ++e) {
+                const float4 pv = __ldcg(p + (c * 8 + e) * 128);
+                vv[4 * e] += pv.x, vv[4 * e + 1] += pv.y, vv[4 * e + 2] += pv.z, vv[4 * e + 3] += pv.w;
+              }
             }
           }
           const int h0 = r * kHRange + c * 32;
