@@ -72,6 +72,7 @@ constexpr uint32_t kBox128 = 128 * 128;   // [128 rows x 64 elements]: 16 KB
 constexpr uint32_t kStageBytes = 48 * 1024;
 constexpr int kSmemList = 2048;           // down steps staged in shared memory
 constexpr int kPlanUnits = 4096;          // gate/up units the plan kernel keeps in shared memory
+constexpr int kPlanListBlocks = 4096;     // blocks up to which the plan keeps the tile lists in shared memory
 constexpr uint32_t kControlBytes = 12 * 1024;
 constexpr uint32_t kSmemBytes = kStages * kStageBytes + kControlBytes + 1024;  // + alignment slack
 constexpr uint32_t kTmemCols = 512;
@@ -335,29 +336,50 @@ __global__ void __launch_bounds__(kPlanThreads)
   __shared__ int scratch[64];
   __shared__ int s_down[kMaxDownUnits + 1];
   __shared__ int s_tile_count[kMaxTiles];
+  __shared__ int s_off[kMaxTiles + 1];
   __shared__ int s_fail;
+  // The prefill launch that follows may be scheduled now; it waits for this
+  // grid to complete before it reads anything.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const int tid = threadIdx.x;
   const int n_words = (n_blocks + 3) / 4;
   const int cap = min(2 * n_blocks + 8, kPlanUnits);
   int* s_units = reinterpret_cast<int*>(words + n_words);
   int* s_prefix = s_units + cap;
+  const bool list_smem = n_blocks <= kPlanListBlocks;
+  int* s_list = s_prefix + cap + 1;  // [kMaxTiles][n_blocks] when list_smem
   for (int i = tid; i < n_words; i += blockDim.x) words[i] = 0u;
   if (tid == 0) s_fail = 0;
+  if (tid <= n_tiles) s_off[tid] = __ldg(tile_offsets + tid);
   __syncthreads();
-  bool bad = false;
-  for (int t = 0; t < n_tiles; ++t) {
-    const int begin = __ldg(tile_offsets + t);
-    const int end = __ldg(tile_offsets + t + 1);
-    if (begin < 0 || end < begin) {
-      bad = true;
-      continue;
-    }
-    for (int j = begin + tid; j < end; j += blockDim.x) {
+  bool bad = false, sorted_offsets = true;
+  for (int t = 0; t < n_tiles; ++t)
+    if (s_off[t] < 0 || s_off[t + 1] < s_off[t]) sorted_offsets = false;
+  if (sorted_offsets) {
+    // Every tile's block ids in one pass (all loads in flight at once).
+    for (int j = s_off[0] + tid; j < s_off[n_tiles]; j += blockDim.x) {
+      int t = 0;
+      while (t + 1 < n_tiles && j >= s_off[t + 1]) ++t;
       const int b = __ldg(tile_blocks + j);
       if (b >= 0 && b < n_blocks)
         atomicOr(&words[b >> 2], (1u << t) << (8 * (b & 3)));
       else
         bad = true;
+    }
+  } else {
+    for (int t = 0; t < n_tiles; ++t) {
+      const int begin = s_off[t], end = s_off[t + 1];
+      if (begin < 0 || end < begin) {
+        bad = true;
+        continue;
+      }
+      for (int j = begin + tid; j < end; j += blockDim.x) {
+        const int b = __ldg(tile_blocks + j);
+        if (b >= 0 && b < n_blocks)
+          atomicOr(&words[b >> 2], (1u << t) << (8 * (b & 3)));
+        else
+          bad = true;
+      }
     }
   }
   if (bad) atomicOr(header + kHdrStatus, QCC_DEV_ID_RANGE);
@@ -366,17 +388,36 @@ __global__ void __launch_bounds__(kPlanThreads)
   const int chunk = (n_blocks + blockDim.x - 1) / blockDim.x;
   const int lo = min(n_blocks, tid * chunk);
   const int hi = min(n_blocks, lo + chunk);
-  // Each tile's blocks in ascending order.
-  for (int t = 0; t < n_tiles; ++t) {
-    int cnt = 0;
-    for (int i = lo; i < hi; ++i) cnt += (mask[i] >> t) & 1;
-    int total;
-    int p = block_exclusive_scan(cnt, scratch, &total);
-    for (int i = lo; i < hi; ++i)
-      if ((mask[i] >> t) & 1) tile_list[t * n_blocks + p++] = i;
-    if (tid == 0) s_tile_count[t] = total;
+  // Each tile's blocks in ascending order: the four tiles' counts go through
+  // two scans, two tiles per 32-bit word (a count fits 16 bits: n_blocks <=
+  // kMaxBlocks = 2^15).
+  static_assert(kMaxTiles == 4 && kMaxBlocks <= 65535, "packed tile counts");
+  int c01 = 0, c23 = 0;
+  for (int i = lo; i < hi; ++i) {
+    const int m = mask[i];
+    c01 += (m & 1) | (((m >> 1) & 1) << 16);
+    c23 += ((m >> 2) & 1) | (((m >> 3) & 1) << 16);
   }
-  __syncthreads();  // tile lists (global) and counts visible to the block
+  int tot01, tot23;
+  const int p01 = block_exclusive_scan(c01, scratch, &tot01);
+  const int p23 = block_exclusive_scan(c23, scratch, &tot23);
+  int pos_t[kMaxTiles] = {p01 & 0xFFFF, p01 >> 16, p23 & 0xFFFF, p23 >> 16};
+  for (int i = lo; i < hi; ++i) {
+    const int m = mask[i];
+#pragma unroll
+    for (int t = 0; t < kMaxTiles; ++t)
+      if (t < n_tiles && ((m >> t) & 1)) {
+        tile_list[t * n_blocks + pos_t[t]] = i;
+        if (list_smem) s_list[t * n_blocks + pos_t[t]] = i;
+        ++pos_t[t];
+      }
+  }
+  if (tid == 0) {
+    const int tots[kMaxTiles] = {tot01 & 0xFFFF, tot01 >> 16, tot23 & 0xFFFF, tot23 >> 16};
+    for (int t = 0; t < kMaxTiles; ++t) s_tile_count[t] = t < n_tiles ? tots[t] : 0;
+  }
+  __syncthreads();  // tile lists and counts visible to the block
+  const int* lst = list_smem ? s_list : tile_list;
   // Gate/up units: each tile's blocks in pairs.  Order: pair i of every tile,
   // then pair i + 1, so units sharing hot blocks run side by side; the cost
   // prefix follows in closed form (a pair costs 3 per chunk, a single 2).
@@ -398,9 +439,9 @@ __global__ void __launch_bounds__(kPlanThreads)
         const int last = n_pairs[t2] - 1;  // index of t2's single, if it has one
         singles += (odd[t2] && (last < i || (last == i && t2 < t))) ? 1 : 0;
       }
-      const int b1 = tile_list[t * n_blocks + 2 * i];
+      const int b1 = lst[t * n_blocks + 2 * i];
       const bool two = 2 * i + 1 < s_tile_count[t];
-      const int b2 = two ? tile_list[t * n_blocks + 2 * i + 1] : kNoBlock;
+      const int b2 = two ? lst[t * n_blocks + 2 * i + 1] : kNoBlock;
       const int word = static_cast<int>((static_cast<uint32_t>(t) << 30) | (static_cast<uint32_t>(b2) << 15) |
                                         static_cast<uint32_t>(b1));
       const int run = (3 * pos - singles) * n_chunks;
@@ -499,6 +540,9 @@ template <bool kBf16>
 __global__ void __launch_bounds__(kThreads, 1)
     prefill_kernel(const __grid_constant__ CUtensorMap tm_records, const __grid_constant__ CUtensorMap tm_x,
                    const __grid_constant__ CUtensorMap tm_abuf, const PrefillArgs a) {
+  // Launched as a programmatic dependent of the plan kernel: the grid may be
+  // scheduled while the plan runs, and waits here for it to complete.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align_1024(smem_raw);
   Control* ctl = reinterpret_cast<Control*>(smem + kStages * kStageBytes);
@@ -1110,7 +1154,8 @@ extern "C" int qcc_indexed_ffn_prefill(const void* x, int64_t ldx, int n_tokens,
     return QCC_ERR_CUDA;
   const size_t plan_smem =
       round_up(static_cast<size_t>(l.n_blocks), 4) +
-      (2 * static_cast<size_t>(std::min(2 * l.n_blocks + 8, kPlanUnits)) + 1) * 4;
+      (2 * static_cast<size_t>(std::min(2 * l.n_blocks + 8, kPlanUnits)) + 1) * 4 +
+      (l.n_blocks <= kPlanListBlocks ? static_cast<size_t>(kMaxTiles) * l.n_blocks * 4 : 0);
   const uint8_t* xb = static_cast<const uint8_t*>(x);
   uint8_t* yb = static_cast<uint8_t*>(y);
 
@@ -1139,11 +1184,15 @@ extern "C" int qcc_indexed_ffn_prefill(const void* x, int64_t ldx, int n_tokens,
     cfg.blockDim = dim3(kThreads);
     cfg.dynamicSmemBytes = kSmemBytes;
     cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
+    // Cooperative (grid barrier between the phases) and a programmatic
+    // dependent of the plan kernel (its launch overlaps the plan).
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeCooperative;
     attr[0].val.cooperative = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = 2;
     void* kargs[] = {&tm_records, &tm_x, &tm_abuf, &args};
     if (!cuda_ok(cudaLaunchKernelExC(&cfg, kernel, kargs))) return QCC_ERR_CUDA;
   }
