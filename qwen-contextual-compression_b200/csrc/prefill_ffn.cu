@@ -73,6 +73,7 @@ constexpr uint32_t kStageBytes = 48 * 1024;
 constexpr int kSmemList = 2048;           // down steps staged in shared memory
 constexpr int kPlanUnits = 4096;          // gate/up units the plan kernel keeps in shared memory
 constexpr int kPlanListBlocks = 4096;     // blocks up to which the plan keeps the tile lists in shared memory
+constexpr int kMaxPlanGrid = 256;         // prefill CTAs the plan computes ranges for (one per SM)
 constexpr uint32_t kControlBytes = 12 * 1024;
 constexpr uint32_t kSmemBytes = kStages * kStageBytes + kControlBytes + 1024;  // + alignment slack
 constexpr uint32_t kTmemCols = 512;
@@ -338,6 +339,8 @@ __global__ void __launch_bounds__(kPlanThreads)
   __shared__ int s_tile_count[kMaxTiles];
   __shared__ int s_off[kMaxTiles + 1];
   __shared__ int s_fail;
+  __shared__ int s_epoch;
+  __shared__ int s_bu[2][kMaxPlanGrid + 1], s_bk[2][kMaxPlanGrid + 1];  // stream-K range boundaries
   // The prefill launch that follows may be scheduled now; it waits for this
   // grid to complete before it reads anything.
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
@@ -349,7 +352,10 @@ __global__ void __launch_bounds__(kPlanThreads)
   const bool list_smem = n_blocks <= kPlanListBlocks;
   int* s_list = s_prefix + cap + 1;  // [kMaxTiles][n_blocks] when list_smem
   for (int i = tid; i < n_words; i += blockDim.x) words[i] = 0u;
-  if (tid == 0) s_fail = 0;
+  if (tid == 0) {
+    s_fail = 0;
+    s_epoch = header[kHdrEpoch];  // read now, not in the serial section below
+  }
   if (tid <= n_tiles) s_off[tid] = __ldg(tile_offsets + tid);
   __syncthreads();
   bool bad = false, sorted_offsets = true;
@@ -464,15 +470,19 @@ __global__ void __launch_bounds__(kPlanThreads)
     header[kHdrCost] = total1;
     unit_prefix[total_units] = total1;
     if (total_units < cap) s_prefix[total_units] = total1;
-    header[kHdrEpoch] = header[kHdrEpoch] + 1;
+    header[kHdrEpoch] = s_epoch + 1;
     header[kHdrArrive] = 0;
-    // Down units: v = range * n_tiles + tile, steps = blocks of the tile.
-    int r = 0;
-    for (int v = 0; v < n_hranges * n_tiles; ++v) {
-      s_down[v] = r;
-      r += s_tile_count[v % n_tiles];
+  }
+  // Down units: v = range * n_tiles + tile, steps = blocks of the tile; their
+  // step prefix in closed form, one thread per unit.
+  for (int v = tid; v <= n_hranges * n_tiles; v += blockDim.x) {
+    const int part = v % n_tiles;
+    int tot = 0, pre = 0;
+    for (int t = 0; t < n_tiles; ++t) {
+      tot += s_tile_count[t];
+      if (t < part) pre += s_tile_count[t];
     }
-    s_down[n_hranges * n_tiles] = r;
+    s_down[v] = (v / n_tiles) * tot + pre;
   }
   __syncthreads();
   // Ranges of every CTA of the prefill grid.
@@ -485,13 +495,31 @@ __global__ void __launch_bounds__(kPlanThreads)
   int max_steps = 0;
   for (int t = 0; t < n_tiles; ++t) max_steps = max(max_steps, s_tile_count[t]);
   const int g2 = effective_ranges(total2, max_steps, grid);
+  // Every range boundary once, in parallel (phase 1 on threads 0..g1, phase 2
+  // on threads kPlanThreads/2..): the per-CTA pass below only reads them.
+  if (tid <= g1) {
+    int u, k;
+    locate_gate_up(u_arr, p_arr, total_units, total1, static_cast<int64_t>(tid) * total1 / g1, &u, &k);
+    s_bu[0][tid] = u;
+    s_bk[0][tid] = k;
+  }
+  if (tid >= kPlanThreads / 2 && tid - kPlanThreads / 2 <= g2) {
+    const int j = tid - kPlanThreads / 2;
+    int u, k;
+    locate_down(s_down, n_down, static_cast<int64_t>(j) * total2 / g2, &u, &k);
+    s_bu[1][j] = u;
+    s_bk[1][j] = k;
+  }
+  __syncthreads();
   for (int i = tid; i < grid; i += blockDim.x) {
     Ranges r;
     auto bound1 = [&](int j, int* u, int* k) {
-      locate_gate_up(u_arr, p_arr, total_units, total1, static_cast<int64_t>(j) * total1 / g1, u, k);
+      *u = s_bu[0][j];
+      *k = s_bk[0][j];
     };
     auto bound2 = [&](int j, int* u, int* k) {
-      locate_down(s_down, n_down, static_cast<int64_t>(j) * total2 / g2, u, k);
+      *u = s_bu[1][j];
+      *k = s_bk[1][j];
     };
     const bool ok = range_of(i, g1, bound1, &r, 0) & range_of(i, g2, bound2, &r, 1);
     if (!ok) s_fail = 1;
@@ -1109,7 +1137,7 @@ extern "C" int qcc_indexed_ffn_prefill(const void* x, int64_t ldx, int n_tokens,
   const DeviceInfo& info = device_info(device);
   const PrefillLayout l = prefill_layout(n_records, info.num_sms);
   if (workspace_bytes < l.total) return QCC_ERR_WORKSPACE;
-  if (info.max_smem_optin < static_cast<int>(kSmemBytes)) return QCC_ERR_UNSUPPORTED;
+  if (info.max_smem_optin < static_cast<int>(kSmemBytes) || l.grid > kMaxPlanGrid) return QCC_ERR_UNSUPPORTED;
   const int hp = hidden_pad(hidden, dtype);
   uint8_t* ws = static_cast<uint8_t*>(workspace);
 
