@@ -781,9 +781,29 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll 1
           for (int c = 0; c < 2; ++c) {
             float g[32], v[32];
+            // One contributor (the usual case): its partials are requested
+            // before the TMEM loads, so the two latencies overlap.
+            const bool one = wait_others && ctl->r.n_contrib[0] == 1;
+            float4 pg[8], pu[8];
+            if (one) {
+              const float4* p =
+                  reinterpret_cast<const float4*>(a.partials + static_cast<size_t>(ctl->r.contrib[0][0]) * kSlotFloats) +
+                  static_cast<size_t>(i) * 32 * 128 + row;
+#pragma unroll
+              for (int e = 0; e < 8; ++e) {
+                pg[e] = __ldcg(p + (c * 8 + e) * 128);
+                pu[e] = __ldcg(p + (16 + c * 8 + e) * 128);
+              }
+            }
             tmem_load32(col0 + i * 128u + c * 32u, g);
             tmem_load32(col0 + i * 128u + 64u + c * 32u, v);
-            if (wait_others) {
+            if (one) {
+#pragma unroll
+              for (int e = 0; e < 8; ++e) {
+                g[4 * e] += pg[e].x, g[4 * e + 1] += pg[e].y, g[4 * e + 2] += pg[e].z, g[4 * e + 3] += pg[e].w;
+                v[4 * e] += pu[e].x, v[4 * e + 1] += pu[e].y, v[4 * e + 2] += pu[e].z, v[4 * e + 3] += pu[e].w;
+              }
+            } else if (wait_others) {
               for (int ci = 0; ci < ctl->r.n_contrib[0]; ++ci) {
                 const float4* p = reinterpret_cast<const float4*>(
                                       a.partials + static_cast<size_t>(ctl->r.contrib[0][ci]) * kSlotFloats) +
