@@ -504,6 +504,7 @@ __device__ __forceinline__ void bulk_copy(void* dst, const void* src, uint32_t b
 
 struct ClusterArgs {
   SelArgs a;
+  int vec_enc;     // x rows and encoder rows load as 16-byte pieces (hidden % 8 == 0, aligned)
   int fc_smem;     // fc1 / fc2 are prefetched into shared memory
   int head_smem;   // the head slice is prefetched into shared memory
   uint32_t fc_bytes;    // bytes of one of fc1 / fc2
@@ -653,11 +654,36 @@ __global__ void __launch_bounds__(kCThreads, 1) score_select_cluster_kernel(cons
       const int l = item / a.nchunk, l2 = item2 / a.nchunk;
       const int h0 = (item - l * a.nchunk) * kEncChunk, h02 = (item2 - l2 * a.nchunk) * kEncChunk;
       float acc = 0.f, acc2 = 0.f;
+      if (ca.vec_enc) {
+        // Lane owns 16 contiguous elements of the chunk: two 16-byte pieces of
+        // x and of each encoder row.
+        const T* w1 = reinterpret_cast<const T*>(a.enc_w) + static_cast<int64_t>(l) * H;
+        const T* w2 = reinterpret_cast<const T*>(a.enc_w) + static_cast<int64_t>(l2) * H;
 #pragma unroll
-      for (int e = 0; e < kEncChunk / 32; ++e) {
-        const int h = h0 + lane + 32 * e, hb = h02 + lane + 32 * e;
-        if (h < H) acc = fmaf(to_f32<T>(xr[h]), ld_f<T>(a.enc_w, static_cast<int64_t>(l) * H + h), acc);
-        if (hb < H) acc2 = fmaf(to_f32<T>(xr[hb]), ld_f<T>(a.enc_w, static_cast<int64_t>(l2) * H + hb), acc2);
+        for (int e = 0; e < 2; ++e) {
+          const int h = h0 + lane * 16 + e * 8, hb = h02 + lane * 16 + e * 8;
+          if (h < H) {
+            float fx[8], fw[8];
+            widen(load_global_pack8<T>(xr + h), fx);
+            widen(load_global_pack8<T>(w1 + h), fw);
+#pragma unroll
+            for (int q = 0; q < 8; ++q) acc = fmaf(fx[q], fw[q], acc);
+          }
+          if (hb < H) {
+            float fx[8], fw[8];
+            widen(load_global_pack8<T>(xr + hb), fx);
+            widen(load_global_pack8<T>(w2 + hb), fw);
+#pragma unroll
+            for (int q = 0; q < 8; ++q) acc2 = fmaf(fx[q], fw[q], acc2);
+          }
+        }
+      } else {
+#pragma unroll
+        for (int e = 0; e < kEncChunk / 32; ++e) {
+          const int h = h0 + lane + 32 * e, hb = h02 + lane + 32 * e;
+          if (h < H) acc = fmaf(to_f32<T>(xr[h]), ld_f<T>(a.enc_w, static_cast<int64_t>(l) * H + h), acc);
+          if (hb < H) acc2 = fmaf(to_f32<T>(xr[hb]), ld_f<T>(a.enc_w, static_cast<int64_t>(l2) * H + hb), acc2);
+        }
       }
       acc = warp_sum(acc);
       acc2 = warp_sum(acc2);
@@ -959,6 +985,7 @@ extern "C" int qcc_selector_scores_topk(const void* x, int64_t ldx, int batch, i
     ca.a.ids = ids;
     ca.a.scores = scores;
     ca.a.cpr = kCluster;
+    ca.vec_enc = hidden % 8 == 0 && aligned16(x) && (static_cast<size_t>(ldx) * esize) % 16 == 0 && aligned16(enc_w);
     const size_t base = (sizeof(ClusterSmem) + 127) / 128 * 128;
     const size_t fc_bytes = static_cast<size_t>(latent) * latent * esize;
     const size_t slice_max = static_cast<size_t>((n_out + kCluster - 1) / kCluster) * latent * esize;
