@@ -83,6 +83,7 @@ constexpr int kMaxBlocks = 1 << 15;        // block ids fit the 15-bit fields of
 constexpr int kMaxDownUnits = 512;        // tiles x 256-wide hidden ranges (hidden <= 32768)
 constexpr size_t kSlotFloats = 128 * 256; // one CTA's partial accumulators
 constexpr int kMaxContrib = 16;           // CTAs that may hand partial sums to one unit's finishing CTA
+constexpr int kPairCost = 3, kSingleCost = 4;  // stream-K cost of one gate/up chunk of a block pair / single block
 constexpr int kSplitTarget = 8;           // ranges are at least 1/8 of the largest unit's cost
 
 // Workspace header (int32 words).
@@ -242,8 +243,10 @@ __device__ __forceinline__ int unit_blocks(int unit) { return ((unit >> 15) & 0x
 // Stream-K ranges.
 // ---------------------------------------------------------------------------
 
-// Phase 1: (unit, chunk) at cost position p.  A chunk of a unit costs its
-// blocks + 1 (16 KB of gate/up rows per block plus one 16 KB box of x).
+// Phase 1: (unit, chunk) at cost position p.  A chunk of a block pair costs
+// kPairCost, a chunk of a single block kSingleCost: measured per-step times
+// of 0.154 and 0.202 us (a single block's N = 128 MMA takes as long as a
+// pair's N = 256 one, and the per-step overhead is the same).
 __device__ void locate_gate_up(const int* units, const int* prefix, int n_units, int total, int64_t p, int* u,
                                int* k) {
   if (p >= total || n_units == 0) {
@@ -260,7 +263,7 @@ __device__ void locate_gate_up(const int* units, const int* prefix, int n_units,
       hi = mid - 1;
   }
   *u = lo;
-  *k = static_cast<int>((p - prefix[lo]) / (unit_blocks(units[lo]) + 1));
+  *k = static_cast<int>((p - prefix[lo]) / (unit_blocks(units[lo]) == 2 ? kPairCost : kSingleCost));
 }
 
 // Phase 2: (unit, step) at position p; units without steps share their
@@ -426,7 +429,7 @@ __global__ void __launch_bounds__(kPlanThreads)
   const int* lst = list_smem ? s_list : tile_list;
   // Gate/up units: each tile's blocks in pairs.  Order: pair i of every tile,
   // then pair i + 1, so units sharing hot blocks run side by side; the cost
-  // prefix follows in closed form (a pair costs 3 per chunk, a single 2).
+  // prefix follows in closed form (kPairCost per chunk for a pair, kSingleCost for a single).
   int n_pairs[kMaxTiles], odd[kMaxTiles];
   int total_units = 0;
 #pragma unroll
@@ -450,7 +453,7 @@ __global__ void __launch_bounds__(kPlanThreads)
       const int b2 = two ? lst[t * n_blocks + 2 * i + 1] : kNoBlock;
       const int word = static_cast<int>((static_cast<uint32_t>(t) << 30) | (static_cast<uint32_t>(b2) << 15) |
                                         static_cast<uint32_t>(b1));
-      const int run = (3 * pos - singles) * n_chunks;
+      const int run = (kPairCost * (pos - singles) + kSingleCost * singles) * n_chunks;
       units[pos] = word;
       unit_prefix[pos] = run;
       if (pos < cap) {
@@ -462,7 +465,7 @@ __global__ void __launch_bounds__(kPlanThreads)
   int total_singles = 0;
 #pragma unroll
   for (int t = 0; t < kMaxTiles; ++t) total_singles += odd[t];
-  const int total_cost = 3 * total_units - total_singles;
+  const int total_cost = kPairCost * (total_units - total_singles) + kSingleCost * total_singles;
   const int total1 = total_cost * n_chunks;
   if (tid == 0) {
     for (int t = 0; t < kMaxTiles; ++t) header[kHdrTileCount + t] = t < n_tiles ? s_tile_count[t] : 0;
@@ -489,7 +492,7 @@ __global__ void __launch_bounds__(kPlanThreads)
   const bool staged = total_units < cap;
   const int* u_arr = staged ? s_units : units;
   const int* p_arr = staged ? s_prefix : unit_prefix;
-  const int g1 = effective_ranges(total1, 3ll * n_chunks, grid);
+  const int g1 = effective_ranges(total1, static_cast<int64_t>(max(kPairCost, kSingleCost)) * n_chunks, grid);
   const int n_down = n_hranges * n_tiles;
   const int total2 = s_down[n_down];
   int max_steps = 0;
