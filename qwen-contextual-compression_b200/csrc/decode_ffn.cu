@@ -477,9 +477,10 @@ __global__ void __launch_bounds__(kMaxThreads, 1) indexed_ffn_decode_kernel(cons
   //    loads in flight at once), then one warp per column sums the grid rows
   //    in a fixed order (lane-strided, then a shuffle tree).  One rank writes
   //    the four outputs in the output dtype; with several ranks every CTA
-  //    first sends its column sums to all ranks (plain stores over NVLink into
-  //    their exchange buffers, then a release flag per rank), waits for the
-  //    other ranks' flags for the same slice, and adds the ranks in rank order.
+  //    first stores its column sums into every rank's exchange buffer (relaxed
+  //    system-scope stores over NVLink), waits until no word of the other
+  //    ranks' sums for the same slice is the empty mark, and adds the ranks in
+  //    rank order.
   if (*s_flag) {
     const int c0 = blockIdx.x * per;
     const int width = max(0, min(nvec, c0 + per) - c0);
