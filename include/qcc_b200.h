@@ -5,8 +5,9 @@
  * launches on that stream, never synchronises and never allocates memory.
  * Scratch memory is caller-provided ("workspace"); its size is given by the
  * matching *_workspace_bytes() query and it must be zero-filled once with
- * qcc_workspace_init() before first use (each call leaves it zeroed again).
- * A workspace must not be shared by calls that can overlap on the GPU.
+ * qcc_workspace_init() before first use (each call leaves its counters at
+ * zero again).  A workspace must not be shared by calls that can overlap on
+ * the GPU.
  *
  * Return value: QCC_OK (0) or one of the QCC_ERR_* host-side codes below.
  * Conditions that are only visible on the device (an index out of range, a
@@ -39,7 +40,7 @@ extern "C" {
 #define QCC_API
 #endif
 
-#define QCC_ABI_VERSION 1
+#define QCC_ABI_VERSION 2
 
 /* Element types (weights, x, y, activations). */
 #define QCC_DTYPE_BF16 0
@@ -48,6 +49,16 @@ extern "C" {
 /* Index types. */
 #define QCC_INDEX_I32 0
 #define QCC_INDEX_I64 1
+/* Flag OR-ed into the index type of the decode entry points: the ids (and
+ * n_ids_dev / token_mask, when given) are not written by any qcc_* kernel
+ * launched earlier on the same stream -- e.g. they came from a host copy or
+ * from another library's kernel.  The decode kernels let the next launch on
+ * the stream start before they finish; with this flag a decode launch reads
+ * its ids and starts its record copies at once, while the launches ahead of
+ * it are still finishing, and waits for them only before it reads x.  Do not
+ * set it for ids produced by qcc_select_topk, qcc_build_union or
+ * qcc_selector_scores_topk on the same stream. */
+#define QCC_IDS_READY 0x100
 
 /* Host-side status codes. */
 #define QCC_OK 0
@@ -117,19 +128,24 @@ QCC_API int qcc_workspace_init(void* workspace, size_t workspace_bytes, cudaStre
 
 /*
  * y[b, :] = sum_j  m[j,b] * silu(G[id_j] . x[b]) * (U[id_j] . x[b]) * D[:, id_j]
- * for the selected records id_j, j < n_ids, in one launch.
+ * for the selected records id_j, j < n_ids.
  *
  * Replaces runtime/cuda_indexed.py:61-64 (cuda_indexed_ffn ->
  * indexed_ffn_cuda, two launches: gate_up then down) and
  * runtime/ffn.py:34-39 (TorchDynamicSparseFFN.forward).  Math follows
  * runtime/ffn.py:26-31: activation = silu(gate) * up, y = activation @ down.
  * Accumulation is fp32 throughout; y is rounded once to y_dtype.
+ * Two launches on `stream`: the record stream (one CTA per SM, each storing
+ * a partial y row in the workspace) and a reduce of those rows in a fixed
+ * order, so y is bit-reproducible for a given device.  Both let the next
+ * launch on the stream be scheduled early (programmatic dependent launch).
  *
  *   x          : [batch, hidden] in `dtype`, row stride ldx elements
  *   packed     : qcc_pack_records layout, n_records records
- *   ids        : n_ids selected record indices (QCC_INDEX_I32 or _I64); any
- *                order, duplicates count twice (as index_select does);
- *                out-of-range ids contribute nothing and raise QCC_DEV_ID_RANGE
+ *   ids        : n_ids selected record indices (ids_dtype QCC_INDEX_I32 or
+ *                _I64, optionally | QCC_IDS_READY); any order, duplicates
+ *                count twice (as index_select does); out-of-range ids
+ *                contribute nothing and raise QCC_DEV_ID_RANGE
  *   n_ids_dev  : optional device int32 count; when non-null the kernel uses
  *                min(*n_ids_dev, n_ids) ids (output of qcc_build_union)
  *   token_mask : optional [n_ids] bytes; bit b set = token b uses record j.
@@ -157,25 +173,30 @@ QCC_API int qcc_indexed_ffn_decode(const void* x, int64_t ldx, int batch, int hi
 #define QCC_STATIC_SCRATCH_BYTES (4u << 20)
 
 /*
- * qcc_indexed_ffn_decode without a workspace argument: for callers that cannot
- * allocate device memory where they run the layer (inside another
- * framework's allocator or memory pool, plugin hosts that only hand over the
- * input and output buffers, loops that must not call cudaMalloc / cudaFree
- * because those can synchronise the device).  No counterpart in the
- * reference, whose extension allocates its outputs per call.
+ * qcc_indexed_ffn_decode without a workspace argument; it reports no device
+ * status (QCC_DEV_* bits are not readable), so out-of-range ids and bounded
+ * waits that ran out go unseen, although out-of-range ids still contribute
+ * nothing.  For callers that cannot allocate device memory where they run
+ * the layer: code inside another framework's allocator or memory pool,
+ * plugin hosts that only hand over the input and output buffers, loops that
+ * must not call cudaMalloc / cudaFree because those can synchronise the
+ * device.  No counterpart in the reference, whose extension allocates its
+ * outputs per call.
  *
- * Same arguments and results as qcc_indexed_ffn_decode minus the workspace
- * (and without the y_in input).
- * The scratch is a fixed QCC_STATIC_SCRATCH_BYTES array in the library image,
- * held by every GPU that loads the library until the process exits; requests
- * needing more (qcc_decode_workspace_bytes(batch, hidden, dtype) larger than
- * that: one token up to hidden 6552) return QCC_ERR_WORKSPACE.  The call
- * allocates nothing.  The first call on each device looks the scratch up with
+ * Otherwise the same arguments and results as qcc_indexed_ffn_decode minus
+ * the workspace (and without the y_in input).  The scratch is a fixed
+ * QCC_STATIC_SCRATCH_BYTES array in the library image, held by every GPU that
+ * loads the library until the process exits; requests needing more
+ * (qcc_decode_workspace_bytes(batch, hidden, dtype) larger than that: one
+ * token up to hidden 6552) return QCC_ERR_WORKSPACE.  The call allocates
+ * nothing.  The first call on each device looks the scratch up with
  * cudaGetSymbolAddress (which may load the module there), so make it before
- * any stream capture.  All calls on a device share the scratch and each one
- * clears its header first: calls that can overlap on the GPU race and must be
- * serialised by the caller.  Device-side status bits (QCC_DEV_*) are not
- * reported by this variant; out-of-range ids still contribute nothing.
+ * any stream capture; the address is kept for the life of the process, so a
+ * cudaDeviceReset (or any other teardown of the device's primary context)
+ * makes this entry point unusable on that device.  Nothing in the scratch
+ * needs clearing between calls (single-device decode reads no counter), but
+ * all calls on a device share it: calls that can overlap on the GPU race and
+ * must be serialised by the caller.
  */
 QCC_API int qcc_indexed_ffn_decode_static(const void* x, int64_t ldx, int batch, int hidden, const void* packed,
                                           int64_t n_records, int dtype, const void* ids, int ids_dtype, int n_ids,
@@ -264,8 +285,11 @@ QCC_API int qcc_gather_records(const void* host_store, int64_t record_bytes, con
 #define QCC_IPC_HANDLE_BYTES 64
 
 /* Bytes of one rank's exchange buffer (a 256-byte header holding the
- * buffer's launch counter, then three rotating slots of column sums for every
- * rank) for world ranks, batch tokens and this hidden size. */
+ * buffer's launch counter and its wait bound, then three rotating slots of
+ * column sums for every rank) for world ranks, batch tokens and this hidden
+ * size.  Size every rank's buffer for the largest batch it will serve: the
+ * slots are spaced by the buffer's size, so every rank's buffer must have the
+ * same size, and calls with smaller batches use the front of each slot. */
 QCC_API size_t qcc_exchange_bytes(int world, int batch, int hidden, int dtype);
 
 /* Setup-time helpers (these allocate / map, unlike every compute entry):
@@ -274,10 +298,19 @@ QCC_API size_t qcc_exchange_bytes(int world, int batch, int hidden, int dtype);
  * (QCC_IPC_HANDLE_BYTES bytes), and the mapping of another process's buffer
  * from its handle. */
 QCC_API int qcc_exchange_alloc(size_t bytes, void** ptr);
+/* Re-initialise an exchange buffer in place (counter and wait bound zero,
+ * every column-sum word the empty mark; synchronises the device): the
+ * recovery after a QCC_DEV_TIMEOUT, done by every rank, with no call of the
+ * cross-rank sum in flight on any rank, before any rank's next call. */
+QCC_API int qcc_exchange_init(void* ptr, size_t bytes);
 QCC_API int qcc_exchange_free(void* ptr);
 QCC_API int qcc_ipc_handle(void* ptr, void* handle);
 QCC_API int qcc_ipc_open(const void* handle, void** ptr);
 QCC_API int qcc_ipc_close(void* ptr);
+/* Bound, in ns, on each wait of the cross-rank sum for the sums of the other
+ * ranks in this rank's buffer (0 = the default 2 s).  Setup time: a
+ * synchronous copy into the buffer's header. */
+QCC_API int qcc_exchange_set_wait_limit(void* ptr, uint64_t limit_ns);
 
 /*
  * qcc_indexed_ffn_decode on this rank's record shard with the sum over the
@@ -294,11 +327,14 @@ QCC_API int qcc_ipc_close(void* ptr);
  * is this rank's own; the others are peer mappings from qcc_ipc_open),
  * each exchange_bytes large and initialised by qcc_exchange_alloc.  Every
  * rank makes the same sequence of calls on its buffer (the buffer counts its
- * launches; call e uses slot e % 3).  Each CTA stores its column sums into
- * every rank's buffer with relaxed system-scope 16-byte stores over NVLink; the words themselves signal arrival (a reader waits, bounded,
- * 2 s, until none is the empty mark, then marks them empty again), so there is
- * no fence or flag round trip.  After a QCC_DEV_TIMEOUT the buffers must be
- * reallocated.  Replaces the NCCL all-reduce plus fp32 cast that
+ * launches; call e uses slot e % 3).  Each CTA of the reduce launch stores
+ * its column sums into every rank's buffer with relaxed system-scope 16-byte
+ * stores over NVLink; the words themselves signal arrival (a reader waits,
+ * bounded by qcc_exchange_set_wait_limit, default 2 s, until none is the
+ * empty mark, then marks them empty again), so there is no fence or flag
+ * round trip.  A wait that runs out sets QCC_DEV_TIMEOUT in the workspace
+ * status and leaves those columns of y unwritten; every rank must then
+ * re-initialise its buffer (qcc_exchange_init) before the next call.  Replaces the NCCL all-reduce plus fp32 cast that
  * follow a sharded partial; the reference has no distributed path
  * (integration/freetoken_qcc/low_vram/adapter.py:106-107 refuses TP != 1).
  */

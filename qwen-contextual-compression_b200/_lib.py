@@ -17,6 +17,7 @@ _LIBRARY_PATH = _PACKAGE_DIR / "libqcc_b200.so"
 
 DTYPE_BF16, DTYPE_F16, DTYPE_F32 = 0, 1, 2
 INDEX_I32, INDEX_I64 = 0, 1
+IDS_READY = 0x100  # OR-ed into the index type: the ids are not written by an earlier qcc launch on the stream
 
 OK = 0
 ERR_INVALID_ARGUMENT, ERR_SHAPE, ERR_DTYPE, ERR_ALIGNMENT, ERR_UNSUPPORTED, ERR_WORKSPACE, ERR_CUDA = range(1, 8)
@@ -57,10 +58,12 @@ SIGNATURES = {
                                     _c_void_p]),
     "qcc_exchange_bytes": (_c_size_t, [_c_int, _c_int, _c_int, _c_int]),
     "qcc_exchange_alloc": (_c_int, [_c_size_t, ctypes.POINTER(_c_void_p)]),
+    "qcc_exchange_init": (_c_int, [_c_void_p, _c_size_t]),
     "qcc_exchange_free": (_c_int, [_c_void_p]),
     "qcc_ipc_handle": (_c_int, [_c_void_p, _c_void_p]),
     "qcc_ipc_open": (_c_int, [_c_void_p, ctypes.POINTER(_c_void_p)]),
     "qcc_ipc_close": (_c_int, [_c_void_p]),
+    "qcc_exchange_set_wait_limit": (_c_int, [_c_void_p, ctypes.c_uint64]),
     "qcc_indexed_ffn_decode_allreduce": (_c_int, [_c_void_p, _c_int64, _c_int, _c_int, _c_void_p, _c_int64, _c_int,
                                                   _c_void_p, _c_int, _c_int, _c_void_p, _c_void_p, _c_void_p,
                                                   _c_size_t, _c_void_p, _c_int64, _c_int, _c_void_p, _c_int64,

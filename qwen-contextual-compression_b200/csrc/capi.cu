@@ -206,20 +206,36 @@ __global__ void fill_u32_kernel(uint32_t* p, size_t n, uint32_t v) {
 }
 }  // namespace
 
-// The 256-byte header (launch counter) starts at zero, the column-sum words
-// after it as the empty mark (the bits of -0.0f).
+// The 256-byte header (launch counter, wait bound) starts at zero, the
+// column-sum words after it as the empty mark (the bits of -0.0f).
+extern "C" int qcc_exchange_init(void* ptr, size_t bytes) {
+  if (ptr == nullptr || bytes <= 256 || bytes % 16 != 0) return QCC_ERR_INVALID_ARGUMENT;
+  qcc::clear_stale_error();
+  fill_u32_kernel<<<64, 256>>>(static_cast<uint32_t*>(ptr) + 64, (bytes - 256) / 4, 0x80000000u);
+  if (!qcc::launch_ok() || !qcc::cuda_ok(cudaMemset(ptr, 0, 256)) || !qcc::cuda_ok(cudaDeviceSynchronize()))
+    return QCC_ERR_CUDA;
+  return QCC_OK;
+}
+
 extern "C" int qcc_exchange_alloc(size_t bytes, void** ptr) {
   if (ptr == nullptr || bytes <= 256 || bytes % 16 != 0) return QCC_ERR_INVALID_ARGUMENT;
   *ptr = nullptr;
   void* p = nullptr;
   if (!qcc::cuda_ok(cudaMalloc(&p, bytes))) return QCC_ERR_CUDA;
-  qcc::clear_stale_error();
-  fill_u32_kernel<<<64, 256>>>(static_cast<uint32_t*>(p) + 64, (bytes - 256) / 4, 0x80000000u);
-  if (!qcc::launch_ok() || !qcc::cuda_ok(cudaMemset(p, 0, 256)) || !qcc::cuda_ok(cudaDeviceSynchronize())) {
+  const int status = qcc_exchange_init(p, bytes);
+  if (status != QCC_OK) {
     cudaFree(p);
-    return QCC_ERR_CUDA;
+    return status;
   }
   *ptr = p;
+  return QCC_OK;
+}
+
+extern "C" int qcc_exchange_set_wait_limit(void* ptr, uint64_t limit_ns) {
+  if (ptr == nullptr) return QCC_ERR_INVALID_ARGUMENT;
+  // u64 at byte 8 of the header; the decode reduce launch reads it there.
+  if (!qcc::cuda_ok(cudaMemcpy(static_cast<uint8_t*>(ptr) + 8, &limit_ns, sizeof(limit_ns), cudaMemcpyHostToDevice)))
+    return QCC_ERR_CUDA;
   return QCC_OK;
 }
 

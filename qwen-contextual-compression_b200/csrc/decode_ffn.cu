@@ -1,22 +1,32 @@
 // Fused indexed gated FFN for decode / small batches (sm_100a).
 //
-// One persistent launch replaces the reference's two kernels
-// (runtime/cuda_indexed.py:23-26 gate_up_* then down_*): each CTA owns a
-// contiguous run of the selected-id list, streams the selected neurons'
-// packed records [gate_row | up_row | down_col] from HBM into a shared-memory
-// ring with one non-multicast bulk copy per record (mbarrier completion),
-// computes g = G_j.x, u = U_j.x with fp32 accumulation, a_j = silu(g) * u,
-// and accumulates a_j * D_j into a per-thread fp32 slice of y held in
-// registers.  At the end every CTA stores its partial y (fp32) to the
-// workspace, a bounded grid-wide barrier (cooperative launch: all CTAs are
-// resident, one per SM) waits for all partials, and each CTA sums one slice
-// of y over all partials in a fixed order and writes it in the output dtype.
-// No atomics touch y, so the result is bit-reproducible for a given grid.
+// Two launches replace the reference's two kernels
+// (runtime/cuda_indexed.py:23-26 gate_up_* then down_*), split differently:
+//
+// 1. indexed_ffn_decode_kernel: each CTA owns a contiguous run of the
+//    selected-id list, streams the selected neurons' packed records
+//    [gate_row | up_row | down_col] from HBM into a shared-memory ring with
+//    one non-multicast bulk copy per record (mbarrier completion), computes
+//    g = G_j.x, u = U_j.x with fp32 accumulation, a_j = silu(g) * u, and
+//    accumulates a_j * D_j into a per-thread fp32 slice of y held in
+//    registers.  At the end the CTA stores its partial y row (fp32) to the
+//    workspace and exits: no CTA waits for another.
+// 2. decode_reduce_kernel (a programmatic dependent of the first): each CTA
+//    sums one column slice of y over all partial rows in a fixed order and
+//    writes it in the output dtype -- or, with several ranks, stores its
+//    column sums into every rank's exchange buffer and adds the ranks' sums
+//    in rank order.  No atomics touch y, so the result is bit-reproducible
+//    for a given grid.
+//
+// Because decode CTAs exit as soon as their records are done, the SMs they
+// free take the next launch's CTAs while slower CTAs still stream.  With
+// QCC_IDS_READY the next decode starts its record copies right away, before
+// it waits for the launches ahead of it; only x is read after that wait.
 //
 // Thread t of a CTA owns the 8-element hidden slots v = t + k * blockDim.x
 // (k < VPT): it holds x[b, 8v:8v+8] and the partial y[b, 8v:8v+8] in
 // registers, reads the matching 16-byte pieces of every staged record, and
-// all partial dot products meet in one warp-shuffle + shared-atomic
+// all partial dot products meet in one warp-shuffle + shared-memory
 // reduction per group of R records (one __syncthreads per group).
 
 #include <cuda_runtime.h>
@@ -32,18 +42,24 @@ namespace qcc {
 
 namespace {
 
-constexpr int kWorkspaceHeader = 256;  // status word, arrive / depart counters, padding
-constexpr int kMaxGrid = 160;          // CTAs (one per SM) whose partial rows the workspace holds
+// Workspace header: status word (offset 0), the reduce launch's departure
+// counter (offset 8, used with several ranks), padding.
+constexpr int kWorkspaceHeader = 256;
+constexpr int kMaxGrid = 160;          // decode CTAs (one per SM) whose partial rows the workspace holds
+constexpr int kRowLoads = (kMaxGrid + 31) / 32;  // partial rows per lane in the reduce
 constexpr int kMaxStages = 8;
 constexpr int kMaxThreads = 320;  // 10 warps; hidden 5120 = two 8-element slots per thread
-constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s bound on any barrier wait
+constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s bound on any bulk-copy wait, default exchange bound
 constexpr int kMaxRanks = 8;
-// Cross-rank exchange buffer: a 256-byte header whose first word counts the
-// launches that used this buffer, then column sums [3 slots][world]
-// [B * hidden_pad / 4] float4, every word initialised to the empty mark (the
-// bits of -0.0f).  A writer stores its sums (with -0.0 turned into +0.0); a
-// reader waits until no word of a sum is the empty mark, then marks it empty
-// again.  The data is its own flag: no fences, no separate flag round trip.
+// Cross-rank exchange buffer: a 256-byte header -- the launches that used
+// this buffer (u32 at offset 0) and the exchange wait bound in ns (u64 at
+// offset 8, 0 = 2 s) -- then three slots, each holding one region of column
+// sums per rank, [3 slots][world][slot_words] float4.  slot_words follows
+// from the buffer's size, so the slots never move when the batch of a call
+// changes.  Every word starts as the empty mark (the bits of -0.0f).  A
+// writer stores its sums (with -0.0 turned into +0.0); a reader waits until
+// no word of a sum is the empty mark, then marks it empty again.  The data is
+// its own flag: no fences, no separate flag round trip.
 // Launch e of a buffer uses slot e % 3.  A rank starts launch e + 3 only
 // after finishing launch e + 2, which needed every rank's launch-(e + 2)
 // sums, and each rank wrote those after its own launch e had ended: so every
@@ -54,6 +70,7 @@ constexpr int kMaxRanks = 8;
 constexpr uint32_t kEmptyMark = 0x80000000u;
 constexpr int kXchgSlots = 3;
 constexpr int kXchgHeader = 256;
+constexpr int kXchgLimitOffset = 8;
 
 // Stores and polls of exchange words: relaxed at system scope, so the store
 // reaches the peer's memory without a fence and every poll reads it anew.
@@ -84,36 +101,49 @@ struct DecodeArgs {
   int hidden_pad;
   const void* ids;
   int ids64;
+  int ids_ready;  // ids / count / mask may be read before the preceding launches finish
   const uint8_t* token_mask;
   int n_ids;
   const int32_t* n_ids_dev;
   unsigned int* status;
-  unsigned int* arrive;   // CTAs that stored their partial y in this launch
-  unsigned int* depart;   // CTAs done reading partials; the last one resets both
-  float* partials;        // [gridDim.x][B * hidden_pad] fp32
-  void* y_out;
-  int64_t ldy;
-  int y_dtype;
-  const float* y_in;     // optional fp32 [B, ld_in] added to the result
-  int64_t ld_in;
+  float4* partials;  // [slices][gridDim.x][part_per] float4 (slice-major partial rows)
+  int part_per;      // float4 columns per reduce slice
   void* a_out;
   int64_t lda;
   int a_dtype;
   int stages;
-  int id_cap;        // capacity of the shared id cache (>= ids per CTA)
+  int id_cap;          // capacity of the shared id cache (>= ids per CTA)
   int64_t ring_bytes;  // stages * record_bytes (16-byte multiple)
   int x_vec;           // x rows are 16-byte aligned with hidden % 8 == 0: vector loads
-  // Cross-rank sum (world > 1): each CTA's column sums go to every rank's
-  // exchange buffer; y is the sum over ranks in rank order.
-  int world;
-  int rank;
   // Shard range (id_lo >= 0): the ids are global and ascending, and only
   // those in [id_lo, id_hi) -- one contiguous run of the list -- are used,
   // rebased by id_lo.  id_lo < 0: the ids are already local.
   int64_t id_lo;
   int64_t id_hi;
-  unsigned int* epoch;            // launch counter in this rank's exchange header (advanced by the last CTA)
-  uint8_t* xchg[kMaxRanks];       // column-sum slots of all ranks' exchange buffers, own included
+};
+
+struct ReduceArgs {
+  const float4* partials;  // [slices][rows][per]
+  int rows;                // partial rows (the decode grid)
+  int per;                 // float4 columns per slice (one slice per CTA)
+  int nvec;                // B * hidden_pad / 4
+  int seg;                 // hidden_pad
+  int hidden;
+  void* y_out;
+  int64_t ldy;
+  int y_dtype;
+  const float* y_in;  // optional fp32 [B, ld_in] added to the result
+  int64_t ld_in;
+  unsigned int* status;
+  unsigned int* depart;  // CTAs done with this launch (several ranks only; the last resets it)
+  // Cross-rank sum (world > 1): each CTA's column sums go to every rank's
+  // exchange buffer; y is the sum over ranks in rank order.
+  int world;
+  int rank;
+  int64_t slot_words;  // float4 words of one (slot, rank) region
+  unsigned int* epoch;  // launch counter in this rank's exchange header (advanced by the last CTA)
+  const unsigned long long* wait_limit;  // this rank's exchange wait bound (ns, 0 = default)
+  uint8_t* xchg[kMaxRanks];  // column-sum slots of all ranks' exchange buffers, own included
 };
 
 __device__ __forceinline__ int64_t load_id(const DecodeArgs& a, int j) {
@@ -170,11 +200,12 @@ __global__ void __launch_bounds__(kMaxThreads, 1) indexed_ffn_decode_kernel(cons
   int32_t* s_ids = s_flag + 4;
   uint8_t* s_bits = reinterpret_cast<uint8_t*>(s_ids + a.id_cap);
 
-  // Programmatic dependent launch: the next kernel on the stream may be
-  // scheduled now (it waits for this grid before touching memory), and this
-  // grid waits for the previous one before reading any input.
+  // Programmatic dependent launch: the reduce launch that follows may be
+  // scheduled now (it waits for this grid before reading the partial rows).
+  // This grid waits for the launches before it before reading x -- and, unless
+  // the caller marked the ids ready, before reading the ids too.
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-  asm volatile("griddepcontrol.wait;" ::: "memory");
+  if (!a.ids_ready) asm volatile("griddepcontrol.wait;" ::: "memory");
   // This CTA's share of the id list.
   int n = a.n_ids;
   if (a.n_ids_dev != nullptr) n = min(n, max(0, __ldg(a.n_ids_dev)));
@@ -205,6 +236,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1) indexed_ffn_decode_kernel(cons
     }
     first = static_cast<int>(lo);
     n = static_cast<int>(hi) - first;
+    __syncthreads();  // s_count is s_red, reused by the pipeline
   }
   const int begin = first + static_cast<int>((static_cast<int64_t>(n) * blockIdx.x) / gridDim.x);
   const int end = first + static_cast<int>((static_cast<int64_t>(n) * (blockIdx.x + 1)) / gridDim.x);
@@ -233,35 +265,42 @@ __global__ void __launch_bounds__(kMaxThreads, 1) indexed_ffn_decode_kernel(cons
     s_bits[i] = a.token_mask ? __ldg(a.token_mask + begin + i) : static_cast<uint8_t>(0xFFu);
   };
 
-  // Prologue.  Every thread first issues its small global loads -- its x
-  // slots and its share of the id cache -- so that they are in the memory
-  // system before any record copy (loads issued after the copies queue
-  // behind ~30 MB of record traffic).  Thread 0 then fetches the first S ids
-  // itself and starts their copies without waiting for the block barrier.
-  const int pre = min(S, cnt);
   float xr[B][VPT][8];
   float yr[B][VPT][8];
   const T* xg = reinterpret_cast<const T*>(a.x);
+  auto load_x = [&]() {
 #pragma unroll
-  for (int b = 0; b < B; ++b)
+    for (int b = 0; b < B; ++b)
 #pragma unroll
-    for (int k = 0; k < VPT; ++k) {
-      const int v = tid + k * nthreads;
-      if (a.x_vec && v < nslots) {
-        float f[8];
-        widen(load_global_pack8<T>(xg + b * a.ldx + 8 * v), f);
+      for (int k = 0; k < VPT; ++k) {
+        const int v = tid + k * nthreads;
+        if (a.x_vec && v < nslots) {
+          float f[8];
+          widen(load_global_pack8<T>(xg + b * a.ldx + 8 * v), f);
 #pragma unroll
-        for (int e = 0; e < 8; ++e) xr[b][k][e] = f[e];
-      } else {
+          for (int e = 0; e < 8; ++e) xr[b][k][e] = f[e];
+        } else {
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          const int h = 8 * v + e;
-          xr[b][k][e] = (v < nslots && h < a.hidden) ? to_f32<T>(xg[b * a.ldx + h]) : 0.f;
+          for (int e = 0; e < 8; ++e) {
+            const int h = 8 * v + e;
+            xr[b][k][e] = (v < nslots && h < a.hidden) ? to_f32<T>(xg[b * a.ldx + h]) : 0.f;
+          }
         }
-      }
 #pragma unroll
-      for (int e = 0; e < 8; ++e) yr[b][k][e] = 0.f;
-    }
+        for (int e = 0; e < 8; ++e) yr[b][k][e] = 0.f;
+      }
+  };
+
+  // Prologue.  Without QCC_IDS_READY every thread first issues its small
+  // global loads -- its x slots and its share of the id cache -- so that they
+  // are in the memory system before any record copy (loads issued after the
+  // copies queue behind ~30 MB of record traffic).  With it, x may only be
+  // read after the wait for the preceding launches, so the ids and the first
+  // record copies go first and x follows the wait.  Thread 0 fetches the first
+  // S ids itself and starts their copies without waiting for the block
+  // barrier.
+  const int pre = min(S, cnt);
+  if (!a.ids_ready) load_x();
   // Thread 0's first S ids are loaded into registers together with the
   // cache loads, so one memory latency covers both.
   int64_t first_ids[kMaxStages];
@@ -288,6 +327,10 @@ __global__ void __launch_bounds__(kMaxThreads, 1) indexed_ffn_decode_kernel(cons
       }
     }
     issued = pre;
+  }
+  if (a.ids_ready) {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    load_x();
   }
   __syncthreads();
 
@@ -421,25 +464,25 @@ __global__ void __launch_bounds__(kMaxThreads, 1) indexed_ffn_decode_kernel(cons
   }
 
   if (aborted && tid == 0) {
-    // Drain this CTA's bulk copies still in flight (bounded) before the ring
-    // memory is reused below.
+    // Drain this CTA's bulk copies still in flight (bounded) before the CTA
+    // exits and its shared memory goes to another CTA.
     atomicOr(a.status, QCC_DEV_TIMEOUT);
     for (int i = consumed; i < issued; ++i) (void)mbar_wait_bounded(&bars[i % S], (i / S) & 1, kWaitLimitNs);
   }
 
-  // 1. Every CTA (also one with no records) stores its partial y row.  The
-  //    row has nvec = B * seg / 4 float4 columns; column c belongs to the
-  //    final-sum slice of CTA c / per, and the partials are laid out
-  //    slice-major -- [slice][cta][per] float4 -- so that each CTA later reads
-  //    its slice of all grid rows as one contiguous block.
-  const int row_len = B * seg;
-  const int nvec = row_len / 4;
+  // Every CTA (also one with no records) stores its partial y row.  The row
+  // has nvec = B * seg / 4 float4 columns; column c belongs to the slice
+  // c / part_per of the reduce launch, and the partials are laid out
+  // slice-major -- [slice][cta][slice width] float4, the last slice possibly
+  // narrower -- so that each reduce CTA reads its slice of all rows as one
+  // contiguous block and the rows take exactly grid * nvec words.
+  const int per = a.part_per;
   const int grid = gridDim.x;
-  const int per = (nvec + grid - 1) / grid;
-  float4* part4 = reinterpret_cast<float4*>(a.partials);
+  const int nvec = B * seg / 4;
   auto part_index = [&](int c) {
     const int blk = c / per;
-    return (static_cast<int64_t>(blk) * grid + blockIdx.x) * per + (c - blk * per);
+    const int width = min(per, nvec - blk * per);
+    return static_cast<int64_t>(blk) * grid * per + static_cast<int64_t>(blockIdx.x) * width + (c - blk * per);
   };
 #pragma unroll
   for (int b = 0; b < B; ++b)
@@ -448,153 +491,130 @@ __global__ void __launch_bounds__(kMaxThreads, 1) indexed_ffn_decode_kernel(cons
       const int v = tid + k * nthreads;
       if (v < nslots) {
         const int c = (b * seg + 8 * v) / 4;
-        __stcg(part4 + part_index(c), make_float4(yr[b][k][0], yr[b][k][1], yr[b][k][2], yr[b][k][3]));
-        __stcg(part4 + part_index(c + 1), make_float4(yr[b][k][4], yr[b][k][5], yr[b][k][6], yr[b][k][7]));
+        __stcg(a.partials + part_index(c), make_float4(yr[b][k][0], yr[b][k][1], yr[b][k][2], yr[b][k][3]));
+        __stcg(a.partials + part_index(c + 1), make_float4(yr[b][k][4], yr[b][k][5], yr[b][k][6], yr[b][k][7]));
       }
     }
-  // 2. Bounded grid barrier: wait until every CTA's row is stored.
-  __syncthreads();
-  if (tid == 0) {
-    __threadfence();
-    atomicAdd(a.arrive, 1u);
-    const volatile unsigned int* arrive = a.arrive;
-    const uint64_t start = global_timer_ns();
-    bool all = true;
-    while (*arrive < gridDim.x) {
-      if (global_timer_ns() - start > kWaitLimitNs) {
-        atomicOr(a.status, QCC_DEV_TIMEOUT);
-        all = false;
-        break;
-      }
-      __nanosleep(64);
+}
+
+// Writes the four outputs of float4 column `col` (element e0 = 4 * col of the
+// [B][seg] row) in the output dtype, adding y_in when given.
+__device__ __forceinline__ void store_column(const ReduceArgs& a, int col, float4 acc) {
+  const int e0 = col * 4;
+  const int b = e0 / a.seg;
+  const int h0 = e0 - b * a.seg;
+  const float vals[4] = {acc.x, acc.y, acc.z, acc.w};
+#pragma unroll
+  for (int e = 0; e < 4; ++e)
+    if (h0 + e < a.hidden)
+      store_as(a.y_out, b * a.ldy + h0 + e, a.y_dtype,
+               vals[e] + (a.y_in != nullptr ? __ldg(a.y_in + b * a.ld_in + h0 + e) : 0.f));
+}
+
+// One CTA per column slice [blockIdx.x * per, + per).  Warp w sums columns
+// w, w + nwarps, ... of the slice over all partial rows: lane l adds rows l,
+// l + 32, ... (all loads in flight at once), then a shuffle tree -- a fixed
+// order, so y does not depend on timing.  With several ranks, lane 0 stores
+// the column sum into every rank's exchange buffer, then lane q < world polls
+// this rank's buffer for rank q's sum and the warp adds them in rank order.
+__global__ void __launch_bounds__(1024) decode_reduce_kernel(const ReduceArgs a) {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  const int tid = threadIdx.x;
+  const int lane = tid & 31;
+  const int warp = tid >> 5;
+  const int nwarps = blockDim.x >> 5;
+  const int c0 = blockIdx.x * a.per;
+  const int width = max(0, min(a.nvec, c0 + a.per) - c0);
+  const float4* blk = a.partials + static_cast<int64_t>(blockIdx.x) * a.rows * a.per;  // [rows][width]
+  const bool multi = a.world > 1;
+  const unsigned int ep = multi ? *reinterpret_cast<const volatile unsigned int*>(a.epoch) : 0u;
+  const int slot = static_cast<int>(ep % kXchgSlots);
+  for (int col = warp; col < width; col += nwarps) {
+    float4 v[kRowLoads];
+#pragma unroll
+    for (int u = 0; u < kRowLoads; ++u) {
+      const int row = lane + 32 * u;
+      v[u] = row < a.rows ? __ldcg(blk + static_cast<int64_t>(row) * width + col) : make_float4(0.f, 0.f, 0.f, 0.f);
     }
-    __threadfence();
-    *s_flag = all ? 1 : 0;
-  }
-  __syncthreads();
-  // 3. This CTA's slice of y: columns [blockIdx.x * per, ... + width).  Load
-  //    the contiguous [grid][per] block into shared memory (coalesced, all
-  //    loads in flight at once), then one warp per column sums the grid rows
-  //    in a fixed order (lane-strided, then a shuffle tree).  One rank writes
-  //    the four outputs in the output dtype; with several ranks every CTA
-  //    first stores its column sums into every rank's exchange buffer (relaxed
-  //    system-scope stores over NVLink), waits until no word of the other
-  //    ranks' sums for the same slice is the empty mark, and adds the ranks in
-  //    rank order.
-  if (*s_flag) {
-    const int c0 = blockIdx.x * per;
-    const int width = max(0, min(nvec, c0 + per) - c0);
-    if (width > 0) {
-      float4* s_blk = reinterpret_cast<float4*>(smem);  // the ring is idle now
-      const float4* blk = part4 + static_cast<int64_t>(blockIdx.x) * grid * per;
-      // All loads of a round in flight before any is stored (one latency).
-      const int total = grid * per;
-      for (int base = 0; base < total; base += 8 * nthreads) {
-        float4 v[8];
+    float4 acc = v[0];
 #pragma unroll
-        for (int u = 0; u < 8; ++u) {
-          const int i = base + u * nthreads + tid;
-          if (i < total) v[u] = __ldcg(blk + i);
-        }
+    for (int u = 1; u < kRowLoads; ++u) {
+      acc.x += v[u].x;
+      acc.y += v[u].y;
+      acc.z += v[u].z;
+      acc.w += v[u].w;
+    }
 #pragma unroll
-        for (int u = 0; u < 8; ++u) {
-          const int i = base + u * nthreads + tid;
-          if (i < total) s_blk[i] = v[u];
-        }
-      }
-      __syncthreads();
-      const bool multi = a.world > 1;
-      const unsigned int ep = multi ? *reinterpret_cast<volatile unsigned int*>(a.epoch) : 0u;
-      const int slot = static_cast<int>(ep % kXchgSlots);
-      for (int col = warp; col < width; col += nwarps) {
-        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int row = lane; row < grid; row += 32) {
-          const float4 p = s_blk[row * per + col];
-          acc.x += p.x;
-          acc.y += p.y;
-          acc.z += p.z;
-          acc.w += p.w;
-        }
-#pragma unroll
-        for (int off = 16; off >= 1; off >>= 1) {
-          acc.x += __shfl_xor_sync(0xffffffffu, acc.x, off);
-          acc.y += __shfl_xor_sync(0xffffffffu, acc.y, off);
-          acc.z += __shfl_xor_sync(0xffffffffu, acc.z, off);
-          acc.w += __shfl_xor_sync(0xffffffffu, acc.w, off);
-        }
-        if (lane == 0) {
-          if (multi) {
-            // -0.0 is the empty mark; the sum it stands for is +0.0.
-            const uint4 w = make_uint4(__float_as_uint(acc.x) == kEmptyMark ? 0u : __float_as_uint(acc.x),
-                                       __float_as_uint(acc.y) == kEmptyMark ? 0u : __float_as_uint(acc.y),
-                                       __float_as_uint(acc.z) == kEmptyMark ? 0u : __float_as_uint(acc.z),
-                                       __float_as_uint(acc.w) == kEmptyMark ? 0u : __float_as_uint(acc.w));
-            const int64_t at = (static_cast<int64_t>(slot) * a.world + a.rank) * nvec + c0 + col;
-            for (int q = 0; q < a.world; ++q) st_relaxed_sys(reinterpret_cast<uint4*>(a.xchg[q]) + at, w);
-          } else {
-            const int e0 = (c0 + col) * 4;
-            const int b = e0 / seg;
-            const int h0 = e0 - b * seg;
-            const float vals[4] = {acc.x, acc.y, acc.z, acc.w};
-#pragma unroll
-            for (int e = 0; e < 4; ++e)
-              if (h0 + e < a.hidden)
-                store_as(a.y_out, b * a.ldy + h0 + e, a.y_dtype,
-                         vals[e] + (a.y_in != nullptr ? __ldg(a.y_in + b * a.ld_in + h0 + e) : 0.f));
-          }
-        }
-      }
-      if (multi) {
-        // Sum over ranks in rank order, waiting (bounded) for each rank's words.
-        uint4* mine = reinterpret_cast<uint4*>(a.xchg[a.rank]);
-        for (int col = warp; col < width; col += nwarps) {
-          if (lane != 0) continue;
-          float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-          bool ok = true;
-          for (int q = 0; q < a.world; ++q) {
-            uint4* src = mine + (static_cast<int64_t>(slot) * a.world + q) * nvec + c0 + col;
-            uint4 w = ld_relaxed_sys(src);
-            if (has_empty_mark(w)) {
-              const uint64_t start = global_timer_ns();
-              while (true) {
-                w = ld_relaxed_sys(src);
-                if (!has_empty_mark(w)) break;
-                if (global_timer_ns() - start > kWaitLimitNs) {
-                  atomicOr(a.status, QCC_DEV_TIMEOUT);
-                  ok = false;
-                  break;
-                }
-              }
-            }
-            if (!ok) break;
-            acc.x += __uint_as_float(w.x);
-            acc.y += __uint_as_float(w.y);
-            acc.z += __uint_as_float(w.z);
-            acc.w += __uint_as_float(w.w);
-            *src = make_uint4(kEmptyMark, kEmptyMark, kEmptyMark, kEmptyMark);  // ready for launch e + 3
-          }
-          if (!ok) continue;
-          const int e0 = (c0 + col) * 4;
-          const int b = e0 / seg;
-          const int h0 = e0 - b * seg;
-          const float vals[4] = {acc.x, acc.y, acc.z, acc.w};
-#pragma unroll
-          for (int e = 0; e < 4; ++e)
-            if (h0 + e < a.hidden)
-              store_as(a.y_out, b * a.ldy + h0 + e, a.y_dtype,
-                       vals[e] + (a.y_in != nullptr ? __ldg(a.y_in + b * a.ld_in + h0 + e) : 0.f));
-        }
+    for (int off = 16; off >= 1; off >>= 1) {
+      acc.x += __shfl_xor_sync(0xffffffffu, acc.x, off);
+      acc.y += __shfl_xor_sync(0xffffffffu, acc.y, off);
+      acc.z += __shfl_xor_sync(0xffffffffu, acc.z, off);
+      acc.w += __shfl_xor_sync(0xffffffffu, acc.w, off);
+    }
+    if (lane == 0) {
+      if (!multi) {
+        store_column(a, c0 + col, acc);
+      } else {
+        // -0.0 is the empty mark; the sum it stands for is +0.0.
+        const uint4 w = make_uint4(__float_as_uint(acc.x) == kEmptyMark ? 0u : __float_as_uint(acc.x),
+                                   __float_as_uint(acc.y) == kEmptyMark ? 0u : __float_as_uint(acc.y),
+                                   __float_as_uint(acc.z) == kEmptyMark ? 0u : __float_as_uint(acc.z),
+                                   __float_as_uint(acc.w) == kEmptyMark ? 0u : __float_as_uint(acc.w));
+        const int64_t at = (static_cast<int64_t>(slot) * a.world + a.rank) * a.slot_words + c0 + col;
+        for (int q = 0; q < a.world; ++q) st_relaxed_sys(reinterpret_cast<uint4*>(a.xchg[q]) + at, w);
       }
     }
   }
-  // 4. The last CTA to finish reading resets the counters for the next launch.
+  if (!multi) return;
+
+  // Sum over ranks in rank order, lane q waiting (bounded) for rank q's words.
+  const unsigned long long cfg = *reinterpret_cast<const volatile unsigned long long*>(a.wait_limit);
+  const uint64_t limit = cfg != 0ull ? cfg : kWaitLimitNs;
+  uint4* mine = reinterpret_cast<uint4*>(a.xchg[a.rank]);
+  bool failed = false;  // after one wait ran out, later waits of this warp do not wait again
+  for (int col = warp; col < width; col += nwarps) {
+    uint4 w = make_uint4(0u, 0u, 0u, 0u);
+    bool ok = true;
+    uint4* src = nullptr;
+    if (lane < a.world) {
+      src = mine + (static_cast<int64_t>(slot) * a.world + lane) * a.slot_words + c0 + col;
+      w = ld_relaxed_sys(src);
+      if (has_empty_mark(w)) {
+        const uint64_t start = global_timer_ns();
+        while (true) {
+          w = ld_relaxed_sys(src);
+          if (!has_empty_mark(w)) break;
+          if (failed || global_timer_ns() - start > limit) {
+            ok = false;
+            break;
+          }
+        }
+      }
+    }
+    if (!__all_sync(0xffffffffu, ok)) {
+      failed = true;
+      if (lane == 0) atomicOr(a.status, QCC_DEV_TIMEOUT);
+      continue;
+    }
+    if (lane < a.world) *src = make_uint4(kEmptyMark, kEmptyMark, kEmptyMark, kEmptyMark);  // ready for e + 3
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int q = 0; q < a.world; ++q) {
+      acc.x += __uint_as_float(__shfl_sync(0xffffffffu, w.x, q));
+      acc.y += __uint_as_float(__shfl_sync(0xffffffffu, w.y, q));
+      acc.z += __uint_as_float(__shfl_sync(0xffffffffu, w.z, q));
+      acc.w += __uint_as_float(__shfl_sync(0xffffffffu, w.w, q));
+    }
+    if (lane == 0) store_column(a, c0 + col, acc);
+  }
+  // The last CTA to finish advances the buffer's launch counter (every CTA
+  // has read it in this launch) and resets the departure counter.
   __syncthreads();
   if (tid == 0) {
     __threadfence();
     if (atomicAdd(a.depart, 1u) == gridDim.x - 1) {
-      *a.arrive = 0u;
       *a.depart = 0u;
-      if (a.epoch != nullptr) *a.epoch += 1u;  // every CTA has read it in this launch
+      *a.epoch += 1u;
     }
   }
 }
@@ -656,8 +676,7 @@ size_t tail_bytes(int id_cap) {
          static_cast<size_t>(id_cap) * sizeof(int32_t) + (static_cast<size_t>(id_cap) + 15) / 16 * 16;
 }
 
-bool plan_launch(int batch, int hidden_pad, int64_t record_bytes, int max_smem, int id_cap,
-                 LaunchShape* out) {
+bool plan_launch(int hidden_pad, int64_t record_bytes, int max_smem, int id_cap, LaunchShape* out) {
   const int nslots = hidden_pad / 8;
   const int vpt = vpt_for(hidden_pad);
   if (vpt == 0) return false;
@@ -671,9 +690,7 @@ bool plan_launch(int batch, int hidden_pad, int64_t record_bytes, int max_smem, 
   out->threads = threads;
   out->vpt = vpt;
   out->stages = stages;
-  // The ring also holds one final-sum block: at most (nvec + kMaxGrid) float4.
-  const size_t block_bytes = (static_cast<size_t>(batch) * hidden_pad / 4 + kMaxGrid) * 16;
-  out->ring = std::max((static_cast<size_t>(stages) * record_bytes + 15) / 16 * 16, block_bytes);
+  out->ring = (static_cast<size_t>(stages) * record_bytes + 15) / 16 * 16;
   out->smem = out->ring + tail;
   return out->smem <= static_cast<size_t>(max_smem);
 }
@@ -713,6 +730,24 @@ int blocks_per_sm(KernelFn fn, int device, int threads, size_t smem) {
   return nb;
 }
 
+// Both launches are programmatic dependents of what precedes them on the
+// stream: the reduce launch is scheduled while the decode CTAs run (it waits
+// for them at entry), and the next decode is scheduled while this reduce runs.
+template <typename Fn, typename Args>
+bool launch_dependent(Fn fn, const Args& args, unsigned grid, unsigned threads, size_t smem, cudaStream_t stream) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(threads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cuda_ok(cudaLaunchKernelEx(&cfg, fn, args));
+}
+
 }  // namespace
 
 int decode_max_batch(int hidden, int dtype) {
@@ -727,20 +762,17 @@ size_t decode_workspace_bytes(int batch, int hidden, int dtype) {
 }
 
 int indexed_ffn_decode(const void* x, int64_t ldx, int batch, int hidden, const void* packed, int64_t n_records,
-                       int dtype, const void* ids, int ids_dtype, int n_ids, const int32_t* n_ids_dev,
+                       int dtype, const void* ids, int ids_kind, int n_ids, const int32_t* n_ids_dev,
                        const uint8_t* token_mask, void* workspace, size_t workspace_bytes, void* y_out, int64_t ldy,
                        int y_dtype, const float* y_in, int64_t ld_in, void* activation_out, int64_t lda,
-                       cudaStream_t stream, void* const* xchg, int world, int rank, int64_t id_lo,
-                       int64_t id_hi) {
+                       cudaStream_t stream, void* const* xchg, size_t xchg_bytes, int world, int rank,
+                       int64_t id_lo, int64_t id_hi) {
   if (!valid_dtype(dtype) || !valid_dtype(y_dtype)) return QCC_ERR_DTYPE;
   if (world < 1 || world > kMaxRanks || rank < 0 || rank >= world) return QCC_ERR_SHAPE;
   if (id_lo >= 0 && id_hi < id_lo) return QCC_ERR_SHAPE;
-  if (world > 1) {
-    if (xchg == nullptr) return QCC_ERR_INVALID_ARGUMENT;
-    for (int q = 0; q < world; ++q)
-      if (xchg[q] == nullptr || !aligned16(xchg[q])) return QCC_ERR_INVALID_ARGUMENT;
-  }
   if (y_dtype != dtype && y_dtype != QCC_DTYPE_F32) return QCC_ERR_DTYPE;
+  if ((ids_kind & ~(0xFF | QCC_IDS_READY)) != 0) return QCC_ERR_DTYPE;
+  const int ids_dtype = ids_kind & 0xFF;
   if (ids_dtype != QCC_INDEX_I32 && ids_dtype != QCC_INDEX_I64) return QCC_ERR_DTYPE;
   if (batch < 1 || hidden < 1 || n_records < 0 || n_ids < 0) return QCC_ERR_SHAPE;
   if (batch > decode_max_batch(hidden, dtype)) return QCC_ERR_UNSUPPORTED;
@@ -754,6 +786,18 @@ int indexed_ffn_decode(const void* x, int64_t ldx, int batch, int hidden, const 
   if (!aligned16(packed) || !aligned16(workspace)) return QCC_ERR_ALIGNMENT;
 
   const int hp = hidden_pad(hidden, dtype);
+  const int nvec = batch * hp / 4;
+  int64_t slot_words = 0;
+  if (world > 1) {
+    if (xchg == nullptr) return QCC_ERR_INVALID_ARGUMENT;
+    for (int q = 0; q < world; ++q)
+      if (xchg[q] == nullptr || !aligned16(xchg[q])) return QCC_ERR_INVALID_ARGUMENT;
+    // Slots are spaced by the buffer's capacity (the same on every rank), not
+    // by this call's batch, so calls with different batches never overlap.
+    if (xchg_bytes <= static_cast<size_t>(kXchgHeader)) return QCC_ERR_WORKSPACE;
+    slot_words = static_cast<int64_t>((xchg_bytes - kXchgHeader) / (static_cast<size_t>(kXchgSlots) * world * 16));
+    if (slot_words < nvec) return QCC_ERR_WORKSPACE;
+  }
   const int64_t rec = record_bytes(hidden, dtype);
   int device = 0;
   if (!cuda_ok(cudaGetDevice(&device))) return QCC_ERR_CUDA;
@@ -765,7 +809,7 @@ int indexed_ffn_decode(const void* x, int64_t ldx, int batch, int hidden, const 
   const int id_cap = std::max(1, (n_ids + std::min(info.num_sms, std::max(1, n_ids)) - 1) /
                                      std::min(info.num_sms, std::max(1, n_ids)));
   LaunchShape shape;
-  if (!plan_launch(batch, hp, rec, info.max_smem_optin, id_cap, &shape)) return QCC_ERR_UNSUPPORTED;
+  if (!plan_launch(hp, rec, info.max_smem_optin, id_cap, &shape)) return QCC_ERR_UNSUPPORTED;
 
   KernelFn fn = nullptr;
   if (dtype == QCC_DTYPE_BF16)
@@ -778,13 +822,18 @@ int indexed_ffn_decode(const void* x, int64_t ldx, int batch, int hidden, const 
 
   const int nb = blocks_per_sm(fn, device, shape.threads, shape.smem);
   if (nb <= 0) return QCC_ERR_CUDA;
-  // One CTA per SM (the workspace holds kMaxGrid partial rows); every CTA
-  // must be resident at once for the grid barrier, which the cooperative
-  // launch guarantees.
+  // At most one CTA per SM (the workspace holds kMaxGrid partial rows); no
+  // CTA waits for another, so residency of the whole grid is not required.
   int64_t grid = std::min<int64_t>(info.num_sms, kMaxGrid);
-  // Across ranks the grid (and with it every CTA's column slice) must be the
-  // same on every rank, whatever its share of the ids.
-  if (n_ids_dev == nullptr && world == 1) grid = std::min<int64_t>(grid, std::max(1, n_ids));
+  if (n_ids_dev == nullptr && id_lo < 0) grid = std::min<int64_t>(grid, std::max(1, n_ids));
+  // Reduce launch: one CTA per column slice, about one slice per SM.
+  const int slices_wanted = std::max(1, std::min(info.num_sms, nvec));
+  const int per = (nvec + slices_wanted - 1) / slices_wanted;
+  const int slices = (nvec + per - 1) / per;
+  const int reduce_threads = 32 * std::min(per, 32);
+
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  float4* partials = reinterpret_cast<float4*>(ws + kWorkspaceHeader);
 
   DecodeArgs args;
   args.x = x;
@@ -796,19 +845,13 @@ int indexed_ffn_decode(const void* x, int64_t ldx, int batch, int hidden, const 
   args.hidden_pad = hp;
   args.ids = ids;
   args.ids64 = ids_dtype == QCC_INDEX_I64;
+  args.ids_ready = (ids_kind & QCC_IDS_READY) != 0;
   args.token_mask = token_mask;
   args.n_ids = n_ids;
   args.n_ids_dev = n_ids_dev;
-  uint8_t* ws = static_cast<uint8_t*>(workspace);
   args.status = reinterpret_cast<unsigned int*>(ws);
-  args.arrive = reinterpret_cast<unsigned int*>(ws + 4);
-  args.depart = reinterpret_cast<unsigned int*>(ws + 8);
-  args.partials = reinterpret_cast<float*>(ws + kWorkspaceHeader);
-  args.y_out = y_out;
-  args.ldy = ldy;
-  args.y_dtype = y_dtype;
-  args.y_in = y_in;
-  args.ld_in = ld_in;
+  args.partials = partials;
+  args.part_per = per;
   args.a_out = activation_out;
   args.lda = lda;
   args.a_dtype = dtype;
@@ -816,31 +859,40 @@ int indexed_ffn_decode(const void* x, int64_t ldx, int batch, int hidden, const 
   args.id_cap = id_cap;
   args.ring_bytes = static_cast<int64_t>(shape.ring);
   args.x_vec = (hidden % 8 == 0) && aligned16(x) && ((ldx * dtype_bytes(dtype)) % 16 == 0);
-  args.world = world;
-  args.rank = rank;
   args.id_lo = id_lo >= 0 ? id_lo : -1;
   args.id_hi = id_lo >= 0 ? id_hi : -1;
-  args.epoch = world > 1 ? static_cast<unsigned int*>(xchg[rank]) : nullptr;
-  for (int q = 0; q < kMaxRanks; ++q)
-    args.xchg[q] = q < world && world > 1 ? static_cast<uint8_t*>(xchg[q]) + kXchgHeader : nullptr;
 
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(static_cast<unsigned>(grid));
-  cfg.blockDim = dim3(static_cast<unsigned>(shape.threads));
-  cfg.dynamicSmemBytes = shape.smem;
-  cfg.stream = stream;
-  // Cooperative (all CTAs resident for the grid barrier) and programmatic
-  // dependent launch: back-to-back layers overlap one launch's set-up with
-  // the previous kernel's tail (measured 34.35 -> 33.94 us per layer).
-  cudaLaunchAttribute attr[2];
-  attr[0].id = cudaLaunchAttributeCooperative;
-  attr[0].val.cooperative = 1;
-  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[1].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 2;
+  ReduceArgs red;
+  red.partials = partials;
+  red.rows = static_cast<int>(grid);
+  red.per = per;
+  red.nvec = nvec;
+  red.seg = hp;
+  red.hidden = hidden;
+  red.y_out = y_out;
+  red.ldy = ldy;
+  red.y_dtype = y_dtype;
+  red.y_in = y_in;
+  red.ld_in = ld_in;
+  red.status = reinterpret_cast<unsigned int*>(ws);
+  red.depart = reinterpret_cast<unsigned int*>(ws + 8);
+  red.world = world;
+  red.rank = rank;
+  red.slot_words = slot_words;
+  red.epoch = world > 1 ? static_cast<unsigned int*>(xchg[rank]) : nullptr;
+  red.wait_limit = world > 1 ? reinterpret_cast<const unsigned long long*>(
+                                   static_cast<const uint8_t*>(xchg[rank]) + kXchgLimitOffset)
+                             : nullptr;
+  for (int q = 0; q < kMaxRanks; ++q)
+    red.xchg[q] = q < world && world > 1 ? static_cast<uint8_t*>(xchg[q]) + kXchgHeader : nullptr;
+
   clear_stale_error();
-  if (!cuda_ok(cudaLaunchKernelEx(&cfg, fn, args))) return QCC_ERR_CUDA;
+  if (!launch_dependent(fn, args, static_cast<unsigned>(grid), static_cast<unsigned>(shape.threads), shape.smem,
+                        stream))
+    return QCC_ERR_CUDA;
+  if (!launch_dependent(decode_reduce_kernel, red, static_cast<unsigned>(slices),
+                        static_cast<unsigned>(reduce_threads), 0, stream))
+    return QCC_ERR_CUDA;
   return QCC_OK;
 }
 
@@ -888,5 +940,5 @@ extern "C" int qcc_indexed_ffn_decode_allreduce(const void* x, int64_t ldx, int 
   if (world > 1 && exchange_bytes < qcc::exchange_bytes(world, batch, hidden, dtype)) return QCC_ERR_WORKSPACE;
   return qcc::indexed_ffn_decode(x, ldx, batch, hidden, packed, n_records, dtype, ids, ids_dtype, n_ids, n_ids_dev,
                                  token_mask, workspace, workspace_bytes, y_out, ldy, y_dtype, y_in, ld_in, nullptr, 0,
-                                 stream, exchange, world, rank, id_begin, id_end);
+                                 stream, exchange, exchange_bytes, world, rank, id_begin, id_end);
 }

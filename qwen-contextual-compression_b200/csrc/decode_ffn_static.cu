@@ -17,9 +17,15 @@
 // All calls on one device share the array.  The first call on each device
 // looks up the array's device address with cudaGetSymbolAddress (this may
 // load the module on that device), so make that first call before any stream
-// capture.  Every call first clears the array's header on its stream; calls
-// that can overlap on the GPU (different streams without ordering, or several
-// host threads) race on the array and must be serialised by the caller.
+// capture.  The address is kept for the life of the process: after a
+// cudaDeviceReset (or any other teardown of the device's primary context) it
+// no longer names the reloaded array, and this entry point must not be used
+// on that device again.  Nothing in the array needs clearing between calls:
+// the single-device decode reads no counter from its scratch, only writes the
+// status word (which this entry point cannot report) and the partial rows it
+// reads back in the same call.  Calls that can overlap on the GPU (different
+// streams without ordering, or several host threads) race on the array and
+// must be serialised by the caller.
 
 #include <cuda_runtime.h>
 
@@ -31,7 +37,6 @@ namespace qcc {
 namespace {
 
 constexpr size_t kStaticScratchBytes = QCC_STATIC_SCRATCH_BYTES;
-constexpr size_t kScratchHeaderBytes = 256;  // status word and grid-barrier counters
 constexpr int kMaxDevices = 64;
 
 // Zero-initialised when the module is loaded; only device code and the
@@ -71,9 +76,6 @@ extern "C" int qcc_indexed_ffn_decode_static(const void* x, int64_t ldx, int bat
   if (!qcc::cuda_ok(cudaGetDevice(&device))) return QCC_ERR_CUDA;
   void* scratch = qcc::scratch_for_device(device);
   if (scratch == nullptr) return QCC_ERR_CUDA;
-  // Status word and barrier counters must start at zero; the partial rows are
-  // written before they are read and need no clearing.
-  if (!qcc::cuda_ok(cudaMemsetAsync(scratch, 0, qcc::kScratchHeaderBytes, stream))) return QCC_ERR_CUDA;
   return qcc::indexed_ffn_decode(x, ldx, batch, hidden, packed, n_records, dtype, ids, ids_dtype, n_ids, n_ids_dev,
                                  token_mask, scratch, qcc::kStaticScratchBytes, y_out, ldy, y_dtype, nullptr, 0,
                                  activation_out, lda, stream);

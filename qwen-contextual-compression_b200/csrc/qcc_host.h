@@ -49,11 +49,11 @@ int decode_max_batch(int hidden, int dtype);
 size_t decode_workspace_bytes(int batch, int hidden, int dtype);
 
 int indexed_ffn_decode(const void* x, int64_t ldx, int batch, int hidden, const void* packed, int64_t n_records,
-                       int dtype, const void* ids, int ids_dtype, int n_ids, const int32_t* n_ids_dev,
+                       int dtype, const void* ids, int ids_kind, int n_ids, const int32_t* n_ids_dev,
                        const uint8_t* token_mask, void* workspace, size_t workspace_bytes, void* y_out, int64_t ldy,
                        int y_dtype, const float* y_in, int64_t ld_in, void* activation_out, int64_t lda,
-                       cudaStream_t stream, void* const* xchg = nullptr, int world = 1, int rank = 0,
-                       int64_t id_lo = -1, int64_t id_hi = -1);
+                       cudaStream_t stream, void* const* xchg = nullptr, size_t xchg_bytes = 0, int world = 1,
+                       int rank = 0, int64_t id_lo = -1, int64_t id_hi = -1);
 
 // Bytes of one rank's cross-rank exchange buffer for this world / batch / hidden.
 size_t exchange_bytes(int world, int batch, int hidden, int dtype);

@@ -1,16 +1,16 @@
 """The fused indexed gated-FFN engine (one packed layer on one GPU).
 
-``IndexedSparseFFN(weights)(x, ids)`` computes, in one kernel launch per
-chunk of <= 4 tokens,
+``IndexedSparseFFN(weights)(x, ids)`` computes, in one call of the C ABI
+(a record-streaming launch and a reduce launch) per chunk of <= 4 tokens,
 
     y[b] = sum_j mask[j, b] * silu(G[ids_j] . x[b]) * (U[ids_j] . x[b]) * D[:, ids_j]
 
 which is reference runtime/ffn.py:34-39 (``TorchDynamicSparseFFN.forward``)
 and runtime/cuda_indexed.py:61-64 (``cuda_indexed_ffn``) without gathered
-copies.  The kernel's scratch (a status word, grid-barrier counters and one
-fp32 partial-y row per CTA) is a device buffer shared by every engine that
+copies.  The kernel's scratch (a status word, a counter and one fp32
+partial-y row per CTA) is a device buffer shared by every engine that
 launches on the same CUDA stream -- launches on one stream never overlap --
-zeroed once; the kernel leaves its counters at zero after every call.
+zeroed once; the kernels leave the counter at zero after every call.
 """
 from __future__ import annotations
 
@@ -106,7 +106,8 @@ class IndexedSparseFFN:
             if bits & _lib.DEV_ID_RANGE:
                 raise ValueError("selected ID out of range")
             if bits & _lib.DEV_TIMEOUT:
-                raise RuntimeError("qcc_indexed_ffn_decode: a bounded wait on a bulk copy ran out")
+                raise RuntimeError("qcc_indexed_ffn_decode: a bounded wait ran out (a record copy, or the "
+                                   "other ranks' sums of a cross-rank exchange)")
 
     def __call__(self, x: torch.Tensor, ids: torch.Tensor, **kwargs) -> torch.Tensor:
         return self.forward(x, ids, **kwargs)
@@ -115,7 +116,7 @@ class IndexedSparseFFN:
                 n_ids_dev: torch.Tensor | None = None, out: torch.Tensor | None = None,
                 out_dtype: torch.dtype | None = None, activation: torch.Tensor | None = None,
                 accumulate: torch.Tensor | None = None, exchange=None,
-                id_range: tuple[int, int] | None = None) -> torch.Tensor:
+                id_range: tuple[int, int] | None = None, ids_ready: bool = False) -> torch.Tensor:
         """y [B, H] for x [B, H] (or [H] -> [H]) and the 1-D selected-id list ``ids``.
 
         token_mask: optional uint8 [len(ids)], bit b = token b uses record j.
@@ -128,6 +129,12 @@ class IndexedSparseFFN:
         id_range:   optional (begin, end): ``ids`` is the global ascending id
                     list and only its ids in [begin, end), rebased by begin,
                     select records of this engine (the kernel finds the run).
+        ids_ready:  the ids (and token_mask / n_ids_dev) were not written by an
+                    earlier qcc_b200 launch on this stream (e.g. they came from
+                    a host copy): the kernel then starts its record copies
+                    before the launches ahead of it finish (QCC_IDS_READY).
+                    Leave it False for ids from ``select_topk``,
+                    ``build_union`` or the fused selector on the same stream.
         """
         squeeze = x.dim() == 1
         if squeeze:
@@ -144,6 +151,7 @@ class IndexedSparseFFN:
         if ws is None:
             ws = self._workspace_for(stream)
         lib = plan.lib
+        ids_code = plan.ids_code | (_lib.IDS_READY if ids_ready else 0)
         x_ptr, out_ptr = x.data_ptr(), out.data_ptr()
         x_row, out_row = x.stride(0) * plan.esize_x, out.stride(0) * plan.esize_y
         mask_ptr = None if token_mask is None else token_mask.data_ptr()
@@ -173,7 +181,7 @@ class IndexedSparseFFN:
                 world, rank = (exchange.world, exchange.rank) if exchange is not None else (1, 0)
                 status = lib.qcc_indexed_ffn_decode_allreduce(
                     x_ptr + start * x_row, x.stride(0), chunk, plan.hidden, plan.packed_ptr, plan.n_records,
-                    plan.code, ids.data_ptr(), plan.ids_code, n_ids, count_ptr, mask_ptr, ws.ptr, ws.nbytes,
+                    plan.code, ids.data_ptr(), ids_code, n_ids, count_ptr, mask_ptr, ws.ptr, ws.nbytes,
                     out_ptr + start * out_row, out.stride(0), plan.y_code, acc_ptr, acc_ld, id_begin, id_end,
                     exchange.pointers if exchange is not None else None,
                     exchange.nbytes if exchange is not None else 0, world, rank, stream)
@@ -182,7 +190,7 @@ class IndexedSparseFFN:
                 continue
             status = lib.qcc_indexed_ffn_decode(
                 x_ptr + start * x_row, x.stride(0), chunk, plan.hidden, plan.packed_ptr, plan.n_records, plan.code,
-                ids.data_ptr(), plan.ids_code, n_ids, count_ptr, mask_ptr, ws.ptr, ws.nbytes,
+                ids.data_ptr(), ids_code, n_ids, count_ptr, mask_ptr, ws.ptr, ws.nbytes,
                 out_ptr + start * out_row, out.stride(0), plan.y_code, acc_ptr, acc_ld, a_ptr, n_ids if a_ptr else 0,
                 stream)
             if status:

@@ -36,14 +36,18 @@ class PeerExchange:
 
     Each rank allocates one buffer (``qcc_exchange_bytes``), shares its CUDA
     IPC handle through the process group, and maps the other ranks' buffers.
-    Collective: every rank of the group constructs it.
+    Collective: every rank of the group constructs it.  ``wait_limit_ns``
+    bounds each wait for the other ranks' sums (None: the library's 2 s).
     """
 
-    def __init__(self, group, device: torch.device, batch: int, hidden: int, dtype: torch.dtype):
+    def __init__(self, group, device: torch.device, batch: int, hidden: int, dtype: torch.dtype,
+                 wait_limit_ns: int | None = None):
         import ctypes
         import torch.distributed as dist
 
         lib = _lib.library()
+        self.group = group
+        self.wait_limit_ns = wait_limit_ns
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
         self.nbytes = int(lib.qcc_exchange_bytes(self.world, batch, hidden, _lib.dtype_code(dtype)))
@@ -53,6 +57,9 @@ class PeerExchange:
             local = ctypes.c_void_p()
             _lib.check(lib.qcc_exchange_alloc(self.nbytes, ctypes.byref(local)), "qcc_exchange_alloc")
             self._local = local.value
+            if wait_limit_ns is not None:
+                _lib.check(lib.qcc_exchange_set_wait_limit(self._local, int(wait_limit_ns)),
+                           "qcc_exchange_set_wait_limit")
             handle = (ctypes.c_uint8 * 64)()
             _lib.check(lib.qcc_ipc_handle(self._local, handle), "qcc_ipc_handle")
             mine = torch.tensor(list(handle), dtype=torch.uint8, device=device)
@@ -72,6 +79,25 @@ class PeerExchange:
                 ptrs.append(p.value)
         self.pointers = (ctypes.c_void_p * self.world)(*ptrs)
         self.device = device
+
+    def reset(self) -> None:
+        """Re-initialise every rank's buffer after a timed-out exchange (collective).
+
+        Every rank calls it between steps, with none of its exchange calls in
+        flight; the barriers keep any rank from writing into a buffer that its
+        owner has not re-initialised yet.
+        """
+        import torch.distributed as dist
+
+        lib = _lib.library()
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+        with torch.cuda.device(self.device):
+            _lib.check(lib.qcc_exchange_init(self._local, self.nbytes), "qcc_exchange_init")
+            if self.wait_limit_ns is not None:
+                _lib.check(lib.qcc_exchange_set_wait_limit(self._local, int(self.wait_limit_ns)),
+                           "qcc_exchange_set_wait_limit")
+        dist.barrier(group=self.group)
 
     def close(self) -> None:
         lib = _lib.library()
@@ -96,7 +122,7 @@ class ShardedIndexedFFN:
         self.group = group
         self.begin = weights.record_offset
         self.end = weights.record_offset + weights.n_records
-        self.allreduce = allreduce if group is not None else "nccl"
+        self.allreduce = allreduce if (group is not None or exchange is not None) else "nccl"
         self._own_exchange = False
         self.exchange = exchange
         if self.allreduce == "fused" and self.exchange is None:
@@ -115,14 +141,16 @@ class ShardedIndexedFFN:
         return self.engine(x2, local, token_mask=mask if per_token else None, n_ids_dev=count,
                            out_dtype=torch.float32)
 
-    def __call__(self, x: torch.Tensor, ids: torch.Tensor) -> torch.Tensor:
-        return self.forward(x, ids)
+    def __call__(self, x: torch.Tensor, ids: torch.Tensor, ids_ready: bool = False) -> torch.Tensor:
+        return self.forward(x, ids, ids_ready=ids_ready)
 
-    def forward(self, x: torch.Tensor, ids: torch.Tensor) -> torch.Tensor:
+    def forward(self, x: torch.Tensor, ids: torch.Tensor, ids_ready: bool = False) -> torch.Tensor:
+        """y of the whole layer on every rank; ``ids_ready`` as in ``IndexedSparseFFN.forward``
+        (used with one shared 1-D id list and the fused sum)."""
         if self.allreduce == "fused" and ids.ndim == 1:
             # One id list for every token: the kernel finds this shard's run.
             x2 = x if x.ndim == 2 else x.unsqueeze(0)
-            y = self.engine(x2, ids, exchange=self.exchange, id_range=(self.begin, self.end))
+            y = self.engine(x2, ids, exchange=self.exchange, id_range=(self.begin, self.end), ids_ready=ids_ready)
             return y if x.ndim == 2 else y.squeeze(0)
         if self.allreduce == "fused":
             rows = ids if ids.ndim == 2 else ids.unsqueeze(0)
@@ -141,6 +169,23 @@ class ShardedIndexedFFN:
         _lib.check(lib.qcc_cast_f32(y32.data_ptr(), out.data_ptr(), y32.numel(), _lib.dtype_code(out.dtype),
                                     _lib.stream_handle(y32.device)), "qcc_cast_f32")
         return out if x.ndim == 2 else out.squeeze(0)
+
+    def check(self) -> None:
+        """Raise if a call since the last check flagged a device-side error (host sync).
+
+        ``RuntimeError`` when a bounded wait ran out -- with the fused sum, the
+        other ranks' column sums did not arrive in time, y of that call is
+        incomplete, and every rank must call :meth:`recover` before the next
+        step; ``ValueError`` for a selected id outside the layer.
+        """
+        self.engine.check()
+
+    def recover(self) -> None:
+        """Clear the device status and re-initialise the exchange buffers (collective)."""
+        for ws in list(self.engine._streams_ws.values()):
+            ws.read_status(clear=True)
+        if self.exchange is not None:
+            self.exchange.reset()
 
     def close(self) -> None:
         if self._own_exchange and self.exchange is not None:

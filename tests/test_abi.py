@@ -37,7 +37,7 @@ def test_binding_covers_every_declared_symbol():
 
 def test_pure_host_queries_without_gpu():
     lib = _lib.library()
-    assert lib.qcc_version() == 1
+    assert lib.qcc_version() == 2
     assert lib.qcc_hidden_pad(5120, _lib.DTYPE_BF16) == 5120
     assert lib.qcc_hidden_pad(5, _lib.DTYPE_F32) == 8
     assert lib.qcc_record_bytes(5120, _lib.DTYPE_BF16) == 30720
@@ -69,6 +69,24 @@ def test_argument_validation_happens_before_any_cuda_call():
     args[13] = big
     args[4] = ctypes.c_void_p(18)  # packed not 16-byte aligned
     assert lib.qcc_indexed_ffn_decode(*args) == _lib.ERR_ALIGNMENT
+    args[4] = dummy
+    args[8] = _lib.INDEX_I32 | 0x200  # an unknown flag bit in the index type
+    assert lib.qcc_indexed_ffn_decode(*args) == _lib.ERR_DTYPE
+    args[8] = _lib.INDEX_I32 | _lib.IDS_READY
+    args[2] = 0
+    assert lib.qcc_indexed_ffn_decode(*args) == _lib.ERR_SHAPE  # the flag is accepted, batch 0 is not
+    # Cross-rank sum: the exchange buffers must hold three slots of this batch for every rank.
+    need = int(lib.qcc_exchange_bytes(2, 1, 8, _lib.DTYPE_BF16))
+    assert need == 256 + 3 * 2 * 2 * 16
+    xchg = (ctypes.c_void_p * 2)(16, 32)
+    ar = [dummy, 8, 1, 8, dummy, 4, _lib.DTYPE_BF16, dummy, _lib.INDEX_I32, 2, None, None, dummy, big, dummy, 8,
+          _lib.DTYPE_BF16, None, 0, 0, 4, xchg, need - 16, 2, 0, None]
+    assert lib.qcc_indexed_ffn_decode_allreduce(*ar) == _lib.ERR_WORKSPACE
+    ar[2] = 2  # a batch beyond what the buffer was sized for
+    ar[22] = need
+    assert lib.qcc_indexed_ffn_decode_allreduce(*ar) == _lib.ERR_WORKSPACE
+    assert lib.qcc_exchange_init(None, need) == _lib.ERR_INVALID_ARGUMENT
+    assert lib.qcc_exchange_set_wait_limit(None, 1000) == _lib.ERR_INVALID_ARGUMENT
     assert lib.qcc_select_topk(dummy, 4, 1, 4, 5, dummy, 5, None) == _lib.ERR_SHAPE  # k > n
     assert lib.qcc_build_union(dummy, 4, 9, 4, 0, 10, dummy, dummy, dummy, None) == _lib.ERR_SHAPE  # batch > 8
     assert lib.qcc_pack_records(dummy, dummy, 4, dummy, 1, 1, 4, 8, _lib.DTYPE_BF16, dummy, None) == _lib.ERR_SHAPE

@@ -73,6 +73,12 @@ def test_static_scratch_matches_workspace_entry_point_twice(hidden, intermediate
     stream = torch.cuda.current_stream(device).cuda_stream
     reference = _decode_with_workspace(lib, weights, xd, idd, stream)
     expected = offn.sparse_ffn_f64(x, ids, gate, up, down)
+    # A first call with an id outside the layer leaves a non-zero status word in
+    # the shared scratch (out-of-range ids are skipped, not a fault); the calls
+    # after it must not be disturbed by what it left behind.
+    bad = idd.clone()
+    bad[0] = intermediate + 5
+    _decode_static(lib, weights, xd, bad, stream)
     for _ in range(2):  # the second call reuses the scratch the first one left behind
         y = _decode_static(lib, weights, xd, idd, stream)
         torch.cuda.synchronize(device)
