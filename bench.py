@@ -175,6 +175,54 @@ def step_bytes(k: int) -> int:
     return workloads.decode_bytes(k, HIDDEN, 2)
 
 
+def workload_config(k: int, retention: float) -> dict:
+    """The workload both arms measure (identical dicts; how each arm runs it is reported beside)."""
+    return {"workload": "decode layer H=5120 N=17408 K/N=0.25 batch 1", "hidden": HIDDEN,
+            "intermediate": INTERMEDIATE, "k": k, "batch": 1, "retention": retention, "layers": LAYERS,
+            "l2": "inputs larger than L2: each step reads a 133.7 MB record set of the next of 4 "
+                  "independently drawn layers (ids of a different token)"}
+
+
+def cross_rank_parity(engine, x, ids, group, device, rank: int, world: int, begin: int, end: int) -> dict:
+    """One token through the fused exchange and through the NCCL path on every rank.
+
+    y of the fused path must be bit-identical on every rank and both paths
+    within the bf16 tolerance (rel-L2 1e-2) of a float64 torch evaluation of
+    the whole layer (rank 0 draws the full layer of the same seed).  Every
+    rank takes the same collective steps.
+    """
+    import torch.distributed as dist
+    from qcc_b200.runtime.sharded import ShardedIndexedFFN
+
+    y_fused = engine(x, ids)
+    nccl = ShardedIndexedFFN(engine.weights, group=group, allreduce="nccl")
+    y_nccl = nccl(x, ids)
+    gathered = [torch.empty_like(y_fused) for _ in range(world)]
+    dist.all_gather(gathered, y_fused, group=group)
+    torch.cuda.synchronize(device)
+    engine.check()
+    identical = all(torch.equal(g, gathered[0]) for g in gathered)
+    out = {"token": 0, "ranks_identical": identical, "tolerance_rel_l2": 1e-2}
+    if rank == 0:
+        full = workloads.decode_layer(device=device, seed=0).packed
+        sel = full.index_select(0, ids.long())
+        g, u, d = (sel[:, i * HIDDEN:(i + 1) * HIDDEN].double() for i in range(3))
+        xd = x.double()
+        gv, uv = xd @ g.t(), xd @ u.t()
+        ref = (gv * torch.sigmoid(gv) * uv) @ d
+        del full, sel, g, u, d
+
+        def rel(y):
+            return float(torch.linalg.vector_norm(y.double() - ref) / torch.linalg.vector_norm(ref))
+
+        out["fused_vs_f64_rel_l2"] = rel(y_fused)
+        out["nccl_vs_f64_rel_l2"] = rel(y_nccl)
+        out["ok"] = identical and out["fused_vs_f64_rel_l2"] <= 1e-2 and out["nccl_vs_f64_rel_l2"] <= 1e-2
+    del nccl
+    torch.cuda.empty_cache()
+    return out
+
+
 def cpu_reference_sample(layer_cpu, retention: float, seconds: float) -> dict:
     """Time the CPU restatement of the reference path (runtime/ffn.py:20-39) on this host."""
     from oracle import ffn as offn  # CPU baseline leg only
@@ -335,6 +383,70 @@ def score_select_cpu_sample(seconds: float) -> dict:
             "sample": f"{len(times)} calls, median, fp32 torch ops ({host_description()})"}
 
 
+def measure_dense_and_oracle(device, stream, side, sparse_us: float) -> dict:
+    """The dense layer the sparse path replaces, and the oracle-mode path, at full layer size (bf16).
+
+    * dense: reference runtime/ffn.py:11-17 (DenseFFN) as torch ops --
+      three cuBLAS GEMVs over the whole layer (267 MB) -- at batch 1;
+      ``speedup_of_sparse_decode`` = dense time / the headline step time.
+    * oracle_mode: ``OracleModeFFN`` (gate|up pass over every record, |a| *
+      ||D|| top-K per token, down pass over the selected records) at 1 and 4
+      tokens, K/N 0.25; bytes = gate|up of every record + the down parts of
+      the tokens' union + x + y.  Beside it the reference's formulation of the
+      same step as torch ops on this GPU (end_to_end/oracle_sparse_mlp.py:
+      dense gate/up, |a| * norms, torch.topk, scatter into zeros, dense down).
+    Steps alternate two independently drawn layers in one CUDA graph.
+    """
+    from qcc_b200.runtime.oracle_mode import OracleModeFFN, down_column_norms
+    from qcc_b200.runtime.packing import PackedFFNWeights
+    import torch.nn.functional as F
+
+    layers = [workloads.decode_layer(device=device, seed=500 + s) for s in range(2)]
+    views = [(l.gate(), l.up(), l.down()) for l in layers]
+    steps = 20
+    xs = torch.randn(steps, 4, HIDDEN, generator=torch.Generator().manual_seed(31)).to(device, torch.bfloat16)
+    out = {}
+
+    def dense_step(i, rows):
+        g, u, d = views[i % 2]
+        x = xs[i, :rows]
+        return F.linear(F.silu(F.linear(x, g)) * F.linear(x, u), d)
+
+    dense_us = graph_time_us(lambda i: dense_step(i, 1), steps, stream, side)
+    dense_bytes = 3 * HIDDEN * INTERMEDIATE * 2
+    out["dense"] = {"us_per_layer": round(dense_us, 2), "gbs": round(dense_bytes / (dense_us * 1e-6) / 1e9, 1),
+                    "impl": "torch F.linear x3 (cuBLAS), batch 1",
+                    "speedup_of_sparse_decode": round(dense_us / sparse_us, 2)}
+    engines = [OracleModeFFN(PackedFFNWeights(l.packed, HIDDEN, INTERMEDIATE), 0.25) for l in layers]
+    k = engines[0].k
+    for rows in (1, 4):
+        us = graph_time_us(lambda i: engines[i % 2](xs[i, :rows]), steps, stream, side)
+        _, ids = engines[0](xs[0, :rows])
+        union = int(torch.unique(ids).numel())
+        nbytes = INTERMEDIATE * 2 * HIDDEN * 2 + union * HIDDEN * 2 + 2 * rows * HIDDEN * 2
+        norms = [down_column_norms(e.weights) for e in engines]
+
+        def torch_step(i, rows=rows):
+            g, u, d = views[i % 2]
+            x = xs[i, :rows]
+            a = F.silu(F.linear(x, g)) * F.linear(x, u)
+            scores = a.abs().float() * norms[i % 2]
+            idx = torch.topk(scores, k, dim=-1, sorted=False).indices
+            sparse = torch.zeros_like(a).scatter_(-1, idx, a.gather(-1, idx))
+            return F.linear(sparse, d)
+
+        torch_us = graph_time_us(torch_step, steps, stream, side)
+        out[f"oracle_mode_tokens{rows}"] = {
+            "us": round(us, 2), "algorithmic_bytes": nbytes, "gbs": round(nbytes / (us * 1e-6) / 1e9, 1),
+            "union_records": union, "k": k, "launches": 4 * ((rows + 3) // 4) + 1,
+            "reference_formulation_torch_us": round(torch_us, 2)}
+        for e in engines:
+            e.check()
+    del engines, layers, views
+    torch.cuda.empty_cache()
+    return out
+
+
 def measure_prefill(device, stream, side, cpu_seconds: float) -> dict:
     """Block-sparse prefill: 512 tokens in four 128-token tiles, hidden 5120, N 17408, bf16.
 
@@ -425,6 +537,13 @@ def measure_offload(device, tokens: int) -> dict:
     torch.cuda.empty_cache()
     x = workloads.decode_x().to(device)
     stream = torch.cuda.current_stream(device)
+    # One call per layer with no ids first: kernels loaded, workspaces and
+    # events made, the cache left empty -- so that token 0 times the cold
+    # cache, not first-call set-up.
+    no_ids = torch.empty(0, dtype=torch.int32, device=device)
+    for layer in layers:
+        layer(x, no_ids)
+    torch.cuda.synchronize(device)
     per_token_ms, misses = [], []
     for t in range(tokens):
         start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -501,8 +620,8 @@ def run_reference(args) -> None:
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1e3 * total / len(times), 4),
         "us_per_layer": round(1e6 * total / len(times), 2), "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,0.02^2) weights, N(0,1) x)",
-        "config": {"workload": "decode layer H=5120 N=17408 K/N=0.25 batch 1", "hidden": HIDDEN,
-                   "intermediate": INTERMEDIATE, "k": k, "batch": 1, "parallelism": "host cores"},
+        "config": workload_config(k, args.retention),
+        "execution": f"reference CPU path (restated), {threads} host threads, steps one after another",
         "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": threads, "kind": "port", "sample": sample},
         "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)
@@ -540,13 +659,13 @@ def run_ours(args) -> None:
     if world == 1:
         engines = [IndexedSparseFFN(PackedFFNWeights(l.packed, HIDDEN, end - begin, begin, INTERMEDIATE))
                    for l in layers]
-        launches_per_step = 1
+        launches_per_step = 2  # record-streaming launch + reduce launch
     else:
         # One exchange buffer per rank serves every layer: the calls of one stream never overlap.
         exchange = PeerExchange(group, device, 1, HIDDEN, torch.bfloat16)
         engines = [ShardedIndexedFFN(PackedFFNWeights(l.packed, HIDDEN, end - begin, begin, INTERMEDIATE),
                                      group=group, allreduce="fused", exchange=exchange) for l in layers]
-        launches_per_step = 1  # fused FFN: shard range, records, cross-rank sum in its epilogue
+        launches_per_step = 2  # records of the shard's range, then the reduce with the cross-rank sum
     engine = engines[0]
     layer = layers[0]
 
@@ -558,6 +677,9 @@ def run_ours(args) -> None:
     def barrier():
         if world > 1:
             torch.distributed.barrier()
+
+    # N > 1: driver-visible correctness of the sharded path before any timing.
+    parity = cross_rank_parity(engines[0], x, ids_all[0], group, device, rank, world, begin, end) if world > 1 else None
 
     # Warm-up (builds the stream workspace / NCCL communicators) on the stream
     # the graph is captured on, so the capture finds everything ready.
@@ -628,8 +750,13 @@ def run_ours(args) -> None:
     del graph
     barrier()
 
-    # Duration of one step's launches (N=1: the record-streaming launch and its reduce).
-    kernel_ms = ms_per_step if world == 1 else None
+    # Duration of one step's launches (the record-streaming launch and its
+    # reduce; at N > 1 the reduce also does the cross-rank sum).
+    kernel_ms = ms_per_step
+    # Bytes this rank streams per step: its shard's records among the step's ids.
+    timed_ids = ids_all[args.warmup:args.warmup + args.steps]
+    local_k = float(((timed_ids >= begin) & (timed_ids < end)).sum().item()) / args.steps
+    rank_bytes = local_k * 3 * HIDDEN * 2 + HIDDEN * 2 * 2 + k * 4
 
     # End-to-end through the public API with host buffers: per step one
     # host->device copy of that step's x and ids (packed in one pinned
@@ -700,6 +827,9 @@ def run_ours(args) -> None:
     offload = None
     if not args.no_offload and world == 1:
         offload = measure_offload(device, args.offload_tokens)
+    dense_oracle = None
+    if not args.no_selector and world == 1:
+        dense_oracle = measure_dense_and_oracle(device, stream, side, ms_per_step * 1e3)
     prefill = None
     if not args.no_prefill and world == 1:
         prefill = measure_prefill(device, stream, side, 0.0 if args.no_cpu_baseline else 10.0)
@@ -727,25 +857,29 @@ def run_ours(args) -> None:
     peak_src = "measured" if peak else "fallback"
     peak = float(peak or FALLBACK_HBM_GBS)
     traffic = committed_traffic()
-    roofline = None
-    if kernel_ms is not None:
+    if world == 1:
         achieved = bytes_ / (kernel_ms * 1e-3) / 1e9
         roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                     "frac": round(achieved / peak, 4), "peak_source": peak_src,
                     "traffic": traffic.get("dram_bytes_per_launch") if traffic else None,
-                    "algorithmic_bytes": bytes_, "kernel": "indexed_ffn_decode_kernel"}
+                    "algorithmic_bytes": bytes_, "kernel": "indexed_ffn_decode_kernel (+ decode_reduce_kernel)"}
+    else:
+        achieved = rank_bytes / (kernel_ms * 1e-3) / 1e9
+        roofline = {"bound": "hbm", "scope": "per rank: rank 0's shard bytes over the max-over-ranks step time",
+                    "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
+                    "peak_source": peak_src, "traffic": None, "algorithmic_bytes": int(rank_bytes),
+                    "local_records_per_step": round(local_k, 1),
+                    "kernel": "indexed_ffn_decode_kernel (+ decode_reduce_kernel with the cross-rank sum)"}
     clock_summary = clocks.summary()
     line = {
         "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms_per_step, 6), "us_per_layer": round(ms_per_step * 1e3, 3),
         "tokens_per_s": round(1e3 / ms_per_step, 1), "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,0.02^2) weights, N(0,1) x)",
-        "config": {"workload": "decode layer H=5120 N=17408 K/N=0.25 batch 1", "hidden": HIDDEN,
-                   "intermediate": INTERMEDIATE, "k": k, "batch": 1, "retention": args.retention,
-                   "parallelism": f"intermediate-dim shard x{world}" if world > 1 else "single GPU",
-                   "layers": LAYERS,
-                   "l2": "inputs larger than L2: each step reads a 133.7 MB record set of the next of 4 "
-                         "independently drawn layers (ids of a different token); steps back to back in one CUDA graph"},
+        "config": workload_config(k, args.retention),
+        "execution": (f"intermediate-dim shard x{world}, cross-rank sum fused into the reduce launch" if world > 1
+                      else "single GPU") + "; steps back to back in one CUDA graph; ids are inputs resident before "
+                                           "the steps (QCC_IDS_READY), see ids_after_wait for the same steps without",
         "gpu_launches": launches_per_step * args.steps,
         "e2e": {"value": round(bytes_ / e2e_step_s / 1e9, 3), "unit": "GB/s",
                 "us_per_layer": round(e2e_step_s * 1e6, 2),
@@ -757,12 +891,16 @@ def run_ours(args) -> None:
                            "note": "same steps without QCC_IDS_READY: each step reads its ids only after the "
                                    "step before has finished (ids produced on the stream, e.g. by the selector)"},
     }
+    if parity is not None:
+        line["parity"] = parity
     if sweep is not None:
         line["sweep"] = sweep
     if selector is not None:
         line["selector_ffn"] = selector
     if offload is not None:
         line["offload"] = offload
+    if dense_oracle is not None:
+        line.update(dense_oracle)
     if prefill is not None:
         line["prefill"] = prefill
     if cpu is not None:

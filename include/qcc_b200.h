@@ -168,6 +168,41 @@ QCC_API int qcc_indexed_ffn_decode(const void* x, int64_t ldx, int batch, int hi
                                    size_t workspace_bytes, void* y_out, int64_t ldy, int y_dtype, const float* y_in,
                                    int64_t ld_in, void* activation_out, int64_t lda, cudaStream_t stream);
 
+/*
+ * Gate / up pass of the oracle-mode FFN: for every record n < n_records (all
+ * of them, in order) and token b < batch,
+ *   act_out[b * ld_act + n]       = silu(G[n] . x[b]) * (U[n] . x[b])   (fp32)
+ *   scores_out[b * ld_scores + n] = |act| * col_weights[n] (|act| when
+ *                                   col_weights is NULL; scores_out may be NULL)
+ * streaming only the gate and up parts of each record (2/3 of it).  The
+ * reference computes this activation with the model's dense gate and up
+ * projections and scores it in end_to_end/oracle_sparse_mlp.py:64-75
+ * (|a| * ||down column||) or oracle/importance.py:10-13 (|a|).  batch <=
+ * qcc_decode_max_batch; the workspace is the decode workspace (its status
+ * word reports QCC_DEV_TIMEOUT).  One launch; fp32 arithmetic.
+ */
+QCC_API int qcc_ffn_activations(const void* x, int64_t ldx, int batch, int hidden, const void* packed,
+                                int64_t n_records, int dtype, const float* col_weights, float* act_out, int64_t ld_act,
+                                float* scores_out, int64_t ld_scores, void* workspace, size_t workspace_bytes,
+                                cudaStream_t stream);
+
+/*
+ * Down pass of the oracle-mode FFN: y[b] = sum_j m[j,b] * act[b * ld_act + id_j] * D[:, id_j]
+ * (+ y_in) for the selected records id_j, streaming only the down part of
+ * each selected record (1/3 of it).  act is the activation of every record
+ * (act_dtype: bf16, fp16 or fp32), as qcc_ffn_activations writes it, indexed
+ * by record id; ids, n_ids_dev and token_mask as in qcc_indexed_ffn_decode
+ * (the output of qcc_build_union for per-token selections).  Replaces the
+ * scatter into zeros and the dense down projection of
+ * end_to_end/oracle_sparse_mlp.py:75 and oracle/sparse_ffn.py:8-13.  Same two
+ * launches, workspace and determinism as qcc_indexed_ffn_decode.
+ */
+QCC_API int qcc_indexed_ffn_down(const void* act, int64_t ld_act, int act_dtype, int batch, int hidden,
+                                 const void* packed, int64_t n_records, int dtype, const void* ids, int ids_dtype,
+                                 int n_ids, const int32_t* n_ids_dev, const uint8_t* token_mask, void* workspace,
+                                 size_t workspace_bytes, void* y_out, int64_t ldy, int y_dtype, const float* y_in,
+                                 int64_t ld_in, cudaStream_t stream);
+
 /* Bytes of the scratch built into the library for
  * qcc_indexed_ffn_decode_static (4 MiB). */
 #define QCC_STATIC_SCRATCH_BYTES (4u << 20)
@@ -220,6 +255,22 @@ QCC_API int qcc_indexed_ffn_decode_static(const void* x, int64_t ldx, int batch,
  */
 QCC_API int qcc_select_topk(const float* scores, int64_t ld_scores, int batch, int n, int k, int32_t* ids_out, int64_t ld_ids,
                     cudaStream_t stream);
+
+/*
+ * Per row b of an activation act [rows, n] (bf16, fp16 or fp32, row stride
+ * ld_act): the k largest scores, score = |a| * col_weights[i] (fp32, one
+ * rounding) or |a| when col_weights is NULL, selected with the rule of
+ * qcc_select_topk, written as k ascending int32 indices to ids_out[b * ld_ids
+ * ..]; when masked_out is not NULL it receives the row with every unselected
+ * entry set to 0 (same dtype, row stride ld_masked).  One launch, one CTA per
+ * row, the row read once.  Replaces the scoring, torch.topk and the
+ * zeros().scatter_(gather) of end_to_end/oracle_sparse_mlp.py:75 (weights =
+ * down-column norms) and oracle/importance.py:10 + :21-23 (no weights).
+ * n * 4 bytes must fit in shared memory (n <= 52224).
+ */
+QCC_API int qcc_activation_topk(const void* act, int64_t ld_act, int dtype, int rows, int n, const float* col_weights,
+                                int k, int32_t* ids_out, int64_t ld_ids, void* masked_out, int64_t ld_masked,
+                                cudaStream_t stream);
 
 /*
  * Union of the per-token sorted id lists ids [batch, k] restricted to
@@ -345,6 +396,13 @@ QCC_API int qcc_indexed_ffn_decode_allreduce(const void* x, int64_t ldx, int bat
                                              const float* y_in, int64_t ld_in, int64_t id_begin, int64_t id_end,
                                              void* const* exchange, size_t exchange_bytes, int world, int rank,
                                              cudaStream_t stream);
+
+/* fp32 L2 norms of the cols columns of a row-major [rows, cols] matrix (row
+ * stride ld elements, bf16 / fp16 / fp32), one pass with fp64 accumulation:
+ * the down-column norms ||D[:, j]||_2 that weight the oracle's importance
+ * (end_to_end/oracle_sparse_mlp.py:10-32 computes them in fp32 column chunks). */
+QCC_API int qcc_column_norms(const void* w, int64_t ld, int64_t rows, int64_t cols, int dtype, float* out,
+                             cudaStream_t stream);
 
 /* Elementwise cast of n fp32 values to dtype (used after a cross-rank sum). */
 QCC_API int qcc_cast_f32(const float* src, void* dst, int64_t n, int dtype, cudaStream_t stream);

@@ -48,9 +48,17 @@ SIGNATURES = {
                                                _c_void_p, _c_int, _c_int, _c_void_p, _c_void_p, _c_void_p, _c_int64,
                                                _c_int, _c_void_p, _c_int64, _c_void_p]),
     "qcc_select_topk": (_c_int, [_c_void_p, _c_int64, _c_int, _c_int, _c_int, _c_void_p, _c_int64, _c_void_p]),
+    "qcc_activation_topk": (_c_int, [_c_void_p, _c_int64, _c_int, _c_int, _c_int, _c_void_p, _c_int, _c_void_p,
+                                     _c_int64, _c_void_p, _c_int64, _c_void_p]),
+    "qcc_ffn_activations": (_c_int, [_c_void_p, _c_int64, _c_int, _c_int, _c_void_p, _c_int64, _c_int, _c_void_p,
+                                     _c_void_p, _c_int64, _c_void_p, _c_int64, _c_void_p, _c_size_t, _c_void_p]),
+    "qcc_indexed_ffn_down": (_c_int, [_c_void_p, _c_int64, _c_int, _c_int, _c_int, _c_void_p, _c_int64, _c_int,
+                                      _c_void_p, _c_int, _c_int, _c_void_p, _c_void_p, _c_void_p, _c_size_t,
+                                      _c_void_p, _c_int64, _c_int, _c_void_p, _c_int64, _c_void_p]),
     "qcc_build_union": (_c_int, [_c_void_p, _c_int64, _c_int, _c_int, ctypes.c_int32, ctypes.c_int32, _c_void_p,
                                  _c_void_p, _c_void_p, _c_void_p]),
     "qcc_cast_f32": (_c_int, [_c_void_p, _c_void_p, _c_int64, _c_int, _c_void_p]),
+    "qcc_column_norms": (_c_int, [_c_void_p, _c_int64, _c_int64, _c_int64, _c_int, _c_void_p, _c_void_p]),
     "qcc_cache_resolve": (_c_int, [_c_void_p, _c_int, _c_void_p, _c_void_p, _c_int, _c_int, _c_void_p, _c_void_p,
                                    _c_void_p, _c_int, _c_void_p, _c_int, _c_void_p, _c_void_p, _c_void_p, _c_void_p,
                                    _c_void_p]),

@@ -48,6 +48,32 @@ __global__ void pack_records_kernel(const T* __restrict__ gate, const T* __restr
   }
 }
 
+// ||W[:, c]||_2 for the columns of a row-major [rows, cols] matrix: thread c
+// walks its column down the rows (consecutive threads read consecutive
+// columns, so every row read is coalesced), accumulating squares in fp64, and
+// rounds the square root once to fp32.  The 8 rows of an unrolled step are
+// loaded before any is added, so eight loads per thread are in flight.
+template <typename T>
+__global__ void column_norms_kernel(const T* __restrict__ w, int64_t ld, int64_t rows, int64_t cols,
+                                    float* __restrict__ out) {
+  const int64_t c = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+  if (c >= cols) return;
+  double acc = 0.0;
+  int64_t r = 0;
+  for (; r + 8 <= rows; r += 8) {
+    float v[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) v[u] = to_f32<T>(w[(r + u) * ld + c]);
+#pragma unroll
+    for (int u = 0; u < 8; ++u) acc += static_cast<double>(v[u]) * static_cast<double>(v[u]);
+  }
+  for (; r < rows; ++r) {
+    const double v = to_f32<T>(w[r * ld + c]);
+    acc += v * v;
+  }
+  out[c] = static_cast<float>(sqrt(acc));
+}
+
 __global__ void cast_f32_kernel(const float* __restrict__ src, void* dst, int64_t n, int dtype) {
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x)
@@ -177,6 +203,28 @@ extern "C" int qcc_pack_records(const void* gate, const void* up, int64_t ld_gu,
   else
     QCC_PACK(float);
 #undef QCC_PACK
+  if (!qcc::launch_ok()) return QCC_ERR_CUDA;
+  return QCC_OK;
+}
+
+extern "C" int qcc_column_norms(const void* w, int64_t ld, int64_t rows, int64_t cols, int dtype, float* out,
+                                cudaStream_t stream) {
+  if (!qcc::valid_dtype(dtype)) return QCC_ERR_DTYPE;
+  if (rows < 0 || cols < 0 || ld < cols) return QCC_ERR_SHAPE;
+  if (cols == 0) return QCC_OK;
+  if (w == nullptr || out == nullptr) return QCC_ERR_INVALID_ARGUMENT;
+  const int threads = 128;
+  const int64_t blocks = (cols + threads - 1) / threads;
+  qcc::clear_stale_error();
+  if (dtype == QCC_DTYPE_BF16)
+    qcc::column_norms_kernel<<<static_cast<unsigned>(blocks), threads, 0, stream>>>(
+        static_cast<const __nv_bfloat16*>(w), ld, rows, cols, out);
+  else if (dtype == QCC_DTYPE_F16)
+    qcc::column_norms_kernel<<<static_cast<unsigned>(blocks), threads, 0, stream>>>(static_cast<const __half*>(w), ld,
+                                                                                   rows, cols, out);
+  else
+    qcc::column_norms_kernel<<<static_cast<unsigned>(blocks), threads, 0, stream>>>(static_cast<const float*>(w), ld,
+                                                                                   rows, cols, out);
   if (!qcc::launch_ok()) return QCC_ERR_CUDA;
   return QCC_OK;
 }

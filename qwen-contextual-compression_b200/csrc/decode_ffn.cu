@@ -47,7 +47,8 @@ namespace {
 constexpr int kWorkspaceHeader = 256;
 constexpr int kMaxGrid = 160;          // decode CTAs (one per SM) whose partial rows the workspace holds
 constexpr int kRowLoads = (kMaxGrid + 31) / 32;  // partial rows per lane in the reduce
-constexpr int kMaxStages = 8;
+constexpr int kMaxStages = 16;      // ring slots (mbarriers) for the gate|up-only and down-only passes
+constexpr int kMaxStagesFull = 8;   // ring slots when whole records stream (registers of the first ids)
 constexpr int kMaxThreads = 320;  // 10 warps; hidden 5120 = two 8-element slots per thread
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s bound on any bulk-copy wait, default exchange bound
 constexpr int kMaxRanks = 8;
@@ -91,6 +92,11 @@ __device__ __forceinline__ bool has_empty_mark(uint4 w) {
   return w.x == kEmptyMark || w.y == kEmptyMark || w.z == kEmptyMark || w.w == kEmptyMark;
 }
 
+// What one launch of the record-streaming kernel computes.
+constexpr int kModeFull = 0;    // y over the records: gate / up dot products, activation, down
+constexpr int kModeGateUp = 1;  // activations (and scores) only: gate | up parts of the records, no y
+constexpr int kModeDown = 2;    // y from given activations: down parts of the records only
+
 struct DecodeArgs {
   const void* x;
   int64_t ldx;
@@ -120,6 +126,22 @@ struct DecodeArgs {
   // rebased by id_lo.  id_lo < 0: the ids are already local.
   int64_t id_lo;
   int64_t id_hi;
+  // Part of each record that is streamed (bytes from the record start, size).
+  int64_t copy_offset;
+  int copy_bytes;
+  // kModeGateUp outputs, indexed by the record's (local) id: activation
+  // [B, ld_act_out] fp32 and, when score_out is set, |activation| * col_w[id]
+  // (col_w null: |activation|).
+  float* act_out;
+  int64_t ld_act_out;
+  float* score_out;
+  int64_t ld_score;
+  const float* col_w;
+  // kModeDown input: activation [B, ld_act_in] in act_in_dtype, read at the
+  // record's (local) id.
+  const void* act_in;
+  int64_t ld_act_in;
+  int act_in_dtype;
 };
 
 struct ReduceArgs {
@@ -146,9 +168,17 @@ struct ReduceArgs {
   uint8_t* xchg[kMaxRanks];  // column-sum slots of all ranks' exchange buffers, own included
 };
 
+// Id j of the list; with no list (ids null) the records themselves, in order.
 __device__ __forceinline__ int64_t load_id(const DecodeArgs& a, int j) {
+  if (a.ids == nullptr) return j;
   return a.ids64 ? __ldg(reinterpret_cast<const long long*>(a.ids) + j)
                  : static_cast<int64_t>(__ldg(reinterpret_cast<const int32_t*>(a.ids) + j));
+}
+
+__device__ __forceinline__ float load_as_f32(const void* base, int64_t idx, int dtype) {
+  if (dtype == QCC_DTYPE_BF16) return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(base)[idx]);
+  if (dtype == QCC_DTYPE_F16) return __half2float(reinterpret_cast<const __half*>(base)[idx]);
+  return __ldg(reinterpret_cast<const float*>(base) + idx);
 }
 
 __host__ __device__ constexpr int next_pow2(int v) { return v <= 1 ? 1 : 2 * next_pow2((v + 1) / 2); }
@@ -179,7 +209,7 @@ __device__ __forceinline__ float warp_reduce_multi(float (&v)[V], int lane) {
 // Shared-memory layout after the record ring (host mirrors it in tail_bytes):
 //   mbarriers [kMaxStages] | warp partials [2][VP][32] f32 | flag [4] i32 |
 //   ids [id_cap] i32 | token bits [id_cap] u8
-template <typename T, int B, int VPT, int R>
+template <typename T, int B, int VPT, int R, int MODE>
 __global__ void __launch_bounds__(kMaxThreads, 1) indexed_ffn_decode_kernel(const DecodeArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
   constexpr int kVals = 2 * R * B;          // partial sums per group: (gate, up) x records x tokens
@@ -243,16 +273,18 @@ __global__ void __launch_bounds__(kMaxThreads, 1) indexed_ffn_decode_kernel(cons
   const int cnt = end - begin;
 
   const uint64_t policy = policy_evict_first();
-  const uint32_t rec_bytes = static_cast<uint32_t>(a.record_bytes);
   int issued = 0;  // meaningful in thread 0 only
+  // Source of the streamed part of record id (read from the kernel parameters
+  // at each use, so that no pointer stays live in a register).
+  auto part_src = [&](int32_t id) { return a.packed + a.copy_offset + static_cast<int64_t>(id) * a.record_bytes; };
 
   auto issue = [&](int i, int stage) {  // thread 0: start the bulk copy of local record i
     const int32_t id = s_ids[i];
     uint64_t* bar = &bars[stage];
     if (id >= 0) {
-      mbar_arrive_expect_tx(bar, rec_bytes);
-      bulk_load(smem + static_cast<size_t>(stage) * a.record_bytes,
-                a.packed + static_cast<int64_t>(id) * a.record_bytes, rec_bytes, bar, policy);
+      const uint32_t bytes = static_cast<uint32_t>(a.copy_bytes);
+      mbar_arrive_expect_tx(bar, bytes);
+      bulk_load(smem + static_cast<size_t>(stage) * bytes, part_src(id), bytes, bar, policy);
     } else {
       mbar_arrive(bar);  // completes the phase with no data; consumers skip the record
     }
@@ -303,24 +335,28 @@ __global__ void __launch_bounds__(kMaxThreads, 1) indexed_ffn_decode_kernel(cons
   if (!a.ids_ready) load_x();
   // Thread 0's first S ids are loaded into registers together with the
   // cache loads, so one memory latency covers both.
-  int64_t first_ids[kMaxStages];
+  constexpr int kFirst = MODE == kModeFull ? kMaxStagesFull : kMaxStages;
+  int32_t first_ids[kFirst];
   if (tid == 0) {
 #pragma unroll
-    for (int i = 0; i < kMaxStages; ++i) first_ids[i] = i < pre ? load_id(a, begin + i) - rebase : -1;
+    for (int i = 0; i < kFirst; ++i) {
+      const int64_t id = i < pre ? load_id(a, begin + i) - rebase : -1;
+      first_ids[i] = (id >= 0 && id < a.n_records) ? static_cast<int32_t>(id) : -1;
+    }
   }
   for (int i = tid; i < cnt; i += nthreads) cache_id(i);
   if (tid == 0) {
     for (int s = 0; s < S; ++s) mbar_init(&bars[s], 1);
     fence_barrier_init();
 #pragma unroll
-    for (int i = 0; i < kMaxStages; ++i) {
+    for (int i = 0; i < kFirst; ++i) {
       if (i < pre) {
-        const int64_t id = first_ids[i];
+        const int32_t id = first_ids[i];
         uint64_t* bar = &bars[i];
-        if (id >= 0 && id < a.n_records) {
-          mbar_arrive_expect_tx(bar, rec_bytes);
-          bulk_load(smem + static_cast<size_t>(i) * a.record_bytes, a.packed + id * a.record_bytes, rec_bytes,
-                    bar, policy);
+        if (id >= 0) {
+          const uint32_t bytes = static_cast<uint32_t>(a.copy_bytes);
+          mbar_arrive_expect_tx(bar, bytes);
+          bulk_load(smem + static_cast<size_t>(i) * bytes, part_src(id), bytes, bar, policy);
         } else {
           mbar_arrive(bar);
         }
@@ -341,6 +377,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1) indexed_ffn_decode_kernel(cons
   //   with group g-1's down slices already in registers.  After the barrier
   //   the ring slots of group g are refilled at once.
   Pack8<T> dn_prev[R][VPT];
+  float act_prev[R][B];  // kModeDown: the activations of the previous group (0 where unused)
   int rn_prev = 0;
   int buf = 0;
   int stage0 = 0;    // ring slot of the group's first record
@@ -350,8 +387,23 @@ __global__ void __launch_bounds__(kMaxThreads, 1) indexed_ffn_decode_kernel(cons
   for (int g0 = 0;; g0 += R) {
     const int rn = min(R, cnt - g0);
     Pack8<T> dn_cur[R][VPT];
+    float act_cur[R][B];
     bool ok = true;
     if (rn > 0) {
+      if constexpr (MODE == kModeDown) {
+        // The given activations of this group's records, used next iteration.
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+          const int i = g0 + r;
+          const int32_t id = r < rn ? s_ids[i] : -1;
+          const unsigned bits = r < rn ? s_bits[i] : 0u;
+#pragma unroll
+          for (int b = 0; b < B; ++b)
+            act_cur[r][b] = (id >= 0 && ((bits >> b) & 1u)) ? load_as_f32(a.act_in, b * a.ld_act_in + id,
+                                                                           a.act_in_dtype)
+                                                            : 0.f;
+        }
+      }
       float part[VP];
 #pragma unroll
       for (int q = 0; q < VP; ++q) part[q] = 0.f;
@@ -365,14 +417,16 @@ __global__ void __launch_bounds__(kMaxThreads, 1) indexed_ffn_decode_kernel(cons
             phase ^= 1u;
           }
           ok = ok && mbar_wait_bounded(&bars[stage], phase, kWaitLimitNs);
-          const T* rec = reinterpret_cast<const T*>(smem + static_cast<size_t>(stage) * a.record_bytes);
+          const T* rec = reinterpret_cast<const T*>(smem + static_cast<size_t>(stage) * a.copy_bytes);
 #pragma unroll
           for (int k = 0; k < VPT; ++k) {
             const int v = tid + k * nthreads;
             if (v < nslots) {
+              if constexpr (MODE == kModeFull) dn_cur[r][k] = load_pack8(rec + 2 * seg + 8 * v);
+              if constexpr (MODE == kModeDown) dn_cur[r][k] = load_pack8(rec + 8 * v);
+              if constexpr (MODE == kModeDown) continue;
               const Pack8<T> gr = load_pack8(rec + 8 * v);
               const Pack8<T> ur = load_pack8(rec + seg + 8 * v);
-              dn_cur[r][k] = load_pack8(rec + 2 * seg + 8 * v);
               float gf[8], uf[8];
               widen(gr, gf);
               widen(ur, uf);
@@ -393,28 +447,46 @@ __global__ void __launch_bounds__(kMaxThreads, 1) indexed_ffn_decode_kernel(cons
           }
         }
       }
-      const float wsum = warp_reduce_multi<VP>(part, lane);
-      if ((lane % kLanesPer) == 0) s_red[(buf * VP + lane / kLanesPer) * 32 + warp] = wsum;
+      if constexpr (MODE != kModeDown) {
+        const float wsum = warp_reduce_multi<VP>(part, lane);
+        if ((lane % kLanesPer) == 0) s_red[(buf * VP + lane / kLanesPer) * 32 + warp] = wsum;
+      }
     }
     if (rn_prev > 0) {
       // Block totals of group g-1: value q = lane / kLanesPer summed over warps.
-      const float* redp = s_red + (buf ^ 1) * VP * 32 + (lane / kLanesPer) * 32;
       float t = 0.f;
-      for (int w = lane % kLanesPer; w < nwarps; w += kLanesPer) t += redp[w];
+      if constexpr (MODE != kModeDown) {
+        const float* redp = s_red + (buf ^ 1) * VP * 32 + (lane / kLanesPer) * 32;
+        for (int w = lane % kLanesPer; w < nwarps; w += kLanesPer) t += redp[w];
 #pragma unroll
-      for (int off = kLanesPer / 2; off >= 1; off >>= 1) t += __shfl_xor_sync(0xffffffffu, t, off);
+        for (int off = kLanesPer / 2; off >= 1; off >>= 1) t += __shfl_xor_sync(0xffffffffu, t, off);
+      }
 #pragma unroll
       for (int r = 0; r < R; ++r) {
         if (r < rn_prev) {
           const int i = g0 - R + r;
-          const bool valid = s_ids[i] >= 0;
+          const int32_t id = s_ids[i];
+          const bool valid = id >= 0;
           const unsigned bits = s_bits[i];
 #pragma unroll
           for (int b = 0; b < B; ++b) {
-            const float g = __shfl_sync(0xffffffffu, t, ((r * B + b) * 2 + 0) * kLanesPer);
-            const float u = __shfl_sync(0xffffffffu, t, ((r * B + b) * 2 + 1) * kLanesPer);
             const bool use = valid && ((bits >> b) & 1u);
-            const float act = use ? __fdividef(g, 1.f + __expf(-g)) * u : 0.f;
+            float act;
+            if constexpr (MODE == kModeDown) {
+              act = act_prev[r][b];
+            } else {
+              const float g = __shfl_sync(0xffffffffu, t, ((r * B + b) * 2 + 0) * kLanesPer);
+              const float u = __shfl_sync(0xffffffffu, t, ((r * B + b) * 2 + 1) * kLanesPer);
+              act = use ? __fdividef(g, 1.f + __expf(-g)) * u : 0.f;
+            }
+            if constexpr (MODE == kModeGateUp) {
+              if (use && tid == 0) {
+                a.act_out[b * a.ld_act_out + id] = act;
+                if (a.score_out != nullptr)
+                  a.score_out[b * a.ld_score + id] = a.col_w != nullptr ? fabsf(act) * __ldg(a.col_w + id) : fabsf(act);
+              }
+              continue;
+            }
             if (a.a_out != nullptr && tid == 0) store_as(a.a_out, b * a.lda + begin + i, a.a_dtype, act);
             if (use) {
 #pragma unroll
@@ -451,9 +523,14 @@ __global__ void __launch_bounds__(kMaxThreads, 1) indexed_ffn_decode_kernel(cons
       }
     }
 #pragma unroll
-    for (int r = 0; r < R; ++r)
+    for (int r = 0; r < R; ++r) {
 #pragma unroll
       for (int k = 0; k < VPT; ++k) dn_prev[r][k] = dn_cur[r][k];
+      if constexpr (MODE == kModeDown) {
+#pragma unroll
+        for (int b = 0; b < B; ++b) act_prev[r][b] = act_cur[r][b];
+      }
+    }
     rn_prev = rn;
     buf ^= 1;
     stage0 += R;
@@ -469,6 +546,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1) indexed_ffn_decode_kernel(cons
     atomicOr(a.status, QCC_DEV_TIMEOUT);
     for (int i = consumed; i < issued; ++i) (void)mbar_wait_bounded(&bars[i % S], (i / S) & 1, kWaitLimitNs);
   }
+  if constexpr (MODE == kModeGateUp) return;  // activations only: no partial y
 
   // Every CTA (also one with no records) stores its partial y row.  The row
   // has nvec = B * seg / 4 float4 columns; column c belongs to the slice
@@ -632,26 +710,33 @@ constexpr int group_records() {
   return (sizeof(T) == 2 && B <= 2) ? 2 : 1;
 }
 
-template <typename T, int B, int VPT>
+template <typename T, int B, int VPT, int MODE>
 KernelFn kernel_for() {
-  return indexed_ffn_decode_kernel<T, B, VPT, group_records<T, B>()>;
+  return indexed_ffn_decode_kernel<T, B, VPT, group_records<T, B>(), MODE>;
 }
 
 // Slots of 8 hidden elements per thread: 1, 2 or 4 (hidden <= 2560, 5120,
 // 10240).  Batch per launch: up to 4 tokens with <= 2 slots, 1 with 4.
-template <typename T>
+template <typename T, int MODE>
 KernelFn pick_kernel(int batch, int vpt) {
   if (vpt == 1 || vpt == 2) {
     switch (batch) {
-      case 1: return vpt == 1 ? kernel_for<T, 1, 1>() : kernel_for<T, 1, 2>();
-      case 2: return vpt == 1 ? kernel_for<T, 2, 1>() : kernel_for<T, 2, 2>();
-      case 3: return vpt == 1 ? kernel_for<T, 3, 1>() : kernel_for<T, 3, 2>();
-      case 4: return vpt == 1 ? kernel_for<T, 4, 1>() : kernel_for<T, 4, 2>();
+      case 1: return vpt == 1 ? kernel_for<T, 1, 1, MODE>() : kernel_for<T, 1, 2, MODE>();
+      case 2: return vpt == 1 ? kernel_for<T, 2, 1, MODE>() : kernel_for<T, 2, 2, MODE>();
+      case 3: return vpt == 1 ? kernel_for<T, 3, 1, MODE>() : kernel_for<T, 3, 2, MODE>();
+      case 4: return vpt == 1 ? kernel_for<T, 4, 1, MODE>() : kernel_for<T, 4, 2, MODE>();
       default: return nullptr;
     }
   }
-  if (vpt == 4 && batch == 1) return kernel_for<T, 1, 4>();
+  if (vpt == 4 && batch == 1) return kernel_for<T, 1, 4, MODE>();
   return nullptr;
+}
+
+template <typename T>
+KernelFn pick_kernel_mode(int mode, int batch, int vpt) {
+  if (mode == kModeGateUp) return pick_kernel<T, kModeGateUp>(batch, vpt);
+  if (mode == kModeDown) return pick_kernel<T, kModeDown>(batch, vpt);
+  return pick_kernel<T, kModeFull>(batch, vpt);
 }
 
 int vpt_for(int hidden_pad_) {
@@ -676,7 +761,7 @@ size_t tail_bytes(int id_cap) {
          static_cast<size_t>(id_cap) * sizeof(int32_t) + (static_cast<size_t>(id_cap) + 15) / 16 * 16;
 }
 
-bool plan_launch(int hidden_pad, int64_t record_bytes, int max_smem, int id_cap, LaunchShape* out) {
+bool plan_launch(int hidden_pad, int64_t record_bytes, int max_smem, int id_cap, int max_stages, LaunchShape* out) {
   const int nslots = hidden_pad / 8;
   const int vpt = vpt_for(hidden_pad);
   if (vpt == 0) return false;
@@ -685,7 +770,7 @@ bool plan_launch(int hidden_pad, int64_t record_bytes, int max_smem, int id_cap,
   const size_t tail = tail_bytes(id_cap);
   if (record_bytes <= 0 || static_cast<size_t>(max_smem) < tail) return false;
   int stages = static_cast<int>((static_cast<size_t>(max_smem) - tail) / static_cast<size_t>(record_bytes));
-  stages = std::min(stages, kMaxStages);
+  stages = std::min(stages, max_stages);
   if (stages < 2) return false;
   out->threads = threads;
   out->vpt = vpt;
@@ -761,44 +846,101 @@ size_t decode_workspace_bytes(int batch, int hidden, int dtype) {
   return kWorkspaceHeader + (rows + 255) / 256 * 256;
 }
 
-int indexed_ffn_decode(const void* x, int64_t ldx, int batch, int hidden, const void* packed, int64_t n_records,
-                       int dtype, const void* ids, int ids_kind, int n_ids, const int32_t* n_ids_dev,
-                       const uint8_t* token_mask, void* workspace, size_t workspace_bytes, void* y_out, int64_t ldy,
-                       int y_dtype, const float* y_in, int64_t ld_in, void* activation_out, int64_t lda,
-                       cudaStream_t stream, void* const* xchg, size_t xchg_bytes, int world, int rank,
-                       int64_t id_lo, int64_t id_hi) {
-  if (!valid_dtype(dtype) || !valid_dtype(y_dtype)) return QCC_ERR_DTYPE;
-  if (world < 1 || world > kMaxRanks || rank < 0 || rank >= world) return QCC_ERR_SHAPE;
-  if (id_lo >= 0 && id_hi < id_lo) return QCC_ERR_SHAPE;
-  if (y_dtype != dtype && y_dtype != QCC_DTYPE_F32) return QCC_ERR_DTYPE;
-  if ((ids_kind & ~(0xFF | QCC_IDS_READY)) != 0) return QCC_ERR_DTYPE;
-  const int ids_dtype = ids_kind & 0xFF;
+namespace {
+
+// Everything one call of the decode family needs; the entry points below
+// fill the fields their mode uses.
+struct DecodeRequest {
+  int mode = kModeFull;
+  const void* x = nullptr;
+  int64_t ldx = 0;
+  int batch = 0;
+  int hidden = 0;
+  const void* packed = nullptr;
+  int64_t n_records = 0;
+  int dtype = QCC_DTYPE_BF16;
+  const void* ids = nullptr;
+  int ids_kind = QCC_INDEX_I32;
+  int n_ids = 0;
+  const int32_t* n_ids_dev = nullptr;
+  const uint8_t* token_mask = nullptr;
+  void* workspace = nullptr;
+  size_t workspace_bytes = 0;
+  void* y_out = nullptr;
+  int64_t ldy = 0;
+  int y_dtype = QCC_DTYPE_BF16;
+  const float* y_in = nullptr;
+  int64_t ld_in = 0;
+  void* activation_out = nullptr;
+  int64_t lda = 0;
+  cudaStream_t stream = nullptr;
+  void* const* xchg = nullptr;
+  size_t xchg_bytes = 0;
+  int world = 1;
+  int rank = 0;
+  int64_t id_lo = -1;
+  int64_t id_hi = -1;
+  // kModeGateUp
+  float* act_out = nullptr;
+  int64_t ld_act_out = 0;
+  float* score_out = nullptr;
+  int64_t ld_score = 0;
+  const float* col_w = nullptr;
+  // kModeDown
+  const void* act_in = nullptr;
+  int64_t ld_act_in = 0;
+  int act_in_dtype = QCC_DTYPE_F32;
+};
+
+int launch_decode(const DecodeRequest& q) {
+  const int mode = q.mode;
+  if (!valid_dtype(q.dtype) || (mode != kModeGateUp && !valid_dtype(q.y_dtype))) return QCC_ERR_DTYPE;
+  if (q.world < 1 || q.world > kMaxRanks || q.rank < 0 || q.rank >= q.world) return QCC_ERR_SHAPE;
+  if (q.id_lo >= 0 && q.id_hi < q.id_lo) return QCC_ERR_SHAPE;
+  if (mode != kModeGateUp && q.y_dtype != q.dtype && q.y_dtype != QCC_DTYPE_F32) return QCC_ERR_DTYPE;
+  if ((q.ids_kind & ~(0xFF | QCC_IDS_READY)) != 0) return QCC_ERR_DTYPE;
+  const int ids_dtype = q.ids_kind & 0xFF;
   if (ids_dtype != QCC_INDEX_I32 && ids_dtype != QCC_INDEX_I64) return QCC_ERR_DTYPE;
-  if (batch < 1 || hidden < 1 || n_records < 0 || n_ids < 0) return QCC_ERR_SHAPE;
-  if (batch > decode_max_batch(hidden, dtype)) return QCC_ERR_UNSUPPORTED;
-  if (ldx < hidden || ldy < hidden || (activation_out != nullptr && lda < n_ids)) return QCC_ERR_SHAPE;
-  if (y_in != nullptr && ld_in < hidden) return QCC_ERR_SHAPE;
-  if (x == nullptr || y_out == nullptr || workspace == nullptr) return QCC_ERR_INVALID_ARGUMENT;
+  if (mode == kModeDown && !valid_dtype(q.act_in_dtype)) return QCC_ERR_DTYPE;
+  if (q.batch < 1 || q.hidden < 1 || q.n_records < 0 || q.n_ids < 0) return QCC_ERR_SHAPE;
+  if (q.batch > decode_max_batch(q.hidden, q.dtype)) return QCC_ERR_UNSUPPORTED;
+  if (mode != kModeDown && q.ldx < q.hidden) return QCC_ERR_SHAPE;
+  if (mode != kModeGateUp && q.ldy < q.hidden) return QCC_ERR_SHAPE;
+  if (q.activation_out != nullptr && q.lda < q.n_ids) return QCC_ERR_SHAPE;
+  if (q.y_in != nullptr && q.ld_in < q.hidden) return QCC_ERR_SHAPE;
+  if (mode == kModeGateUp && (q.ld_act_out < q.n_records || (q.score_out != nullptr && q.ld_score < q.n_records)))
+    return QCC_ERR_SHAPE;
+  if (mode == kModeDown && q.ld_act_in < q.n_records) return QCC_ERR_SHAPE;
+  if (q.workspace == nullptr) return QCC_ERR_INVALID_ARGUMENT;
+  if (mode != kModeDown && q.x == nullptr) return QCC_ERR_INVALID_ARGUMENT;
+  if (mode != kModeGateUp && q.y_out == nullptr) return QCC_ERR_INVALID_ARGUMENT;
+  if (mode == kModeGateUp && q.act_out == nullptr) return QCC_ERR_INVALID_ARGUMENT;
+  if (mode == kModeDown && q.act_in == nullptr) return QCC_ERR_INVALID_ARGUMENT;
   // An empty shard (n_records 0, e.g. an empty slice whose pointer is NULL)
   // reads no record: every id is outside it.
-  if (n_ids > 0 && (ids == nullptr || (packed == nullptr && n_records > 0))) return QCC_ERR_INVALID_ARGUMENT;
-  if (workspace_bytes < decode_workspace_bytes(batch, hidden, dtype)) return QCC_ERR_WORKSPACE;
-  if (!aligned16(packed) || !aligned16(workspace)) return QCC_ERR_ALIGNMENT;
+  if (q.n_ids > 0 && ((q.ids == nullptr && mode != kModeGateUp) || (q.packed == nullptr && q.n_records > 0)))
+    return QCC_ERR_INVALID_ARGUMENT;
+  if (q.workspace_bytes < decode_workspace_bytes(q.batch, q.hidden, q.dtype)) return QCC_ERR_WORKSPACE;
+  if (!aligned16(q.packed) || !aligned16(q.workspace)) return QCC_ERR_ALIGNMENT;
 
-  const int hp = hidden_pad(hidden, dtype);
-  const int nvec = batch * hp / 4;
+  const int hp = hidden_pad(q.hidden, q.dtype);
+  const int nvec = q.batch * hp / 4;
   int64_t slot_words = 0;
-  if (world > 1) {
-    if (xchg == nullptr) return QCC_ERR_INVALID_ARGUMENT;
-    for (int q = 0; q < world; ++q)
-      if (xchg[q] == nullptr || !aligned16(xchg[q])) return QCC_ERR_INVALID_ARGUMENT;
+  if (q.world > 1) {
+    if (q.xchg == nullptr) return QCC_ERR_INVALID_ARGUMENT;
+    for (int r = 0; r < q.world; ++r)
+      if (q.xchg[r] == nullptr || !aligned16(q.xchg[r])) return QCC_ERR_INVALID_ARGUMENT;
     // Slots are spaced by the buffer's capacity (the same on every rank), not
     // by this call's batch, so calls with different batches never overlap.
-    if (xchg_bytes <= static_cast<size_t>(kXchgHeader)) return QCC_ERR_WORKSPACE;
-    slot_words = static_cast<int64_t>((xchg_bytes - kXchgHeader) / (static_cast<size_t>(kXchgSlots) * world * 16));
+    if (q.xchg_bytes <= static_cast<size_t>(kXchgHeader)) return QCC_ERR_WORKSPACE;
+    slot_words =
+        static_cast<int64_t>((q.xchg_bytes - kXchgHeader) / (static_cast<size_t>(kXchgSlots) * q.world * 16));
     if (slot_words < nvec) return QCC_ERR_WORKSPACE;
   }
-  const int64_t rec = record_bytes(hidden, dtype);
+  const int64_t rec = record_bytes(q.hidden, q.dtype);
+  const int64_t part = rec / 3;  // one of the gate / up / down parts (Hp elements)
+  const int64_t copy_offset = mode == kModeDown ? 2 * part : 0;
+  const int64_t copy_bytes = mode == kModeFull ? rec : (mode == kModeGateUp ? 2 * part : part);
   int device = 0;
   if (!cuda_ok(cudaGetDevice(&device))) return QCC_ERR_CUDA;
   const DeviceInfo& info = device_info(device);
@@ -806,18 +948,21 @@ int indexed_ffn_decode(const void* x, int64_t ldx, int batch, int hidden, const 
 
   // Ids per CTA never exceed ceil(n_ids / min(#SMs, n_ids)): the grid is at
   // least that large whenever it is smaller than n_ids.
+  const int n_ids = q.n_ids;
   const int id_cap = std::max(1, (n_ids + std::min(info.num_sms, std::max(1, n_ids)) - 1) /
                                      std::min(info.num_sms, std::max(1, n_ids)));
   LaunchShape shape;
-  if (!plan_launch(hp, rec, info.max_smem_optin, id_cap, &shape)) return QCC_ERR_UNSUPPORTED;
+  if (!plan_launch(hp, copy_bytes, info.max_smem_optin, id_cap, mode == kModeFull ? kMaxStagesFull : kMaxStages,
+                   &shape))
+    return QCC_ERR_UNSUPPORTED;
 
   KernelFn fn = nullptr;
-  if (dtype == QCC_DTYPE_BF16)
-    fn = pick_kernel<__nv_bfloat16>(batch, shape.vpt);
-  else if (dtype == QCC_DTYPE_F16)
-    fn = pick_kernel<__half>(batch, shape.vpt);
+  if (q.dtype == QCC_DTYPE_BF16)
+    fn = pick_kernel_mode<__nv_bfloat16>(mode, q.batch, shape.vpt);
+  else if (q.dtype == QCC_DTYPE_F16)
+    fn = pick_kernel_mode<__half>(mode, q.batch, shape.vpt);
   else
-    fn = pick_kernel<float>(batch, shape.vpt);
+    fn = pick_kernel_mode<float>(mode, q.batch, shape.vpt);
   if (fn == nullptr) return QCC_ERR_UNSUPPORTED;
 
   const int nb = blocks_per_sm(fn, device, shape.threads, shape.smem);
@@ -825,42 +970,58 @@ int indexed_ffn_decode(const void* x, int64_t ldx, int batch, int hidden, const 
   // At most one CTA per SM (the workspace holds kMaxGrid partial rows); no
   // CTA waits for another, so residency of the whole grid is not required.
   int64_t grid = std::min<int64_t>(info.num_sms, kMaxGrid);
-  if (n_ids_dev == nullptr && id_lo < 0) grid = std::min<int64_t>(grid, std::max(1, n_ids));
+  if (q.n_ids_dev == nullptr && q.id_lo < 0) grid = std::min<int64_t>(grid, std::max(1, n_ids));
   // Reduce launch: one CTA per column slice, about one slice per SM.
   const int slices_wanted = std::max(1, std::min(info.num_sms, nvec));
   const int per = (nvec + slices_wanted - 1) / slices_wanted;
   const int slices = (nvec + per - 1) / per;
   const int reduce_threads = 32 * std::min(per, 32);
 
-  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  uint8_t* ws = static_cast<uint8_t*>(q.workspace);
   float4* partials = reinterpret_cast<float4*>(ws + kWorkspaceHeader);
 
   DecodeArgs args;
-  args.x = x;
-  args.ldx = ldx;
-  args.packed = static_cast<const uint8_t*>(packed);
+  args.x = q.x;
+  args.ldx = q.ldx;
+  args.packed = static_cast<const uint8_t*>(q.packed);
   args.record_bytes = rec;
-  args.n_records = n_records;
-  args.hidden = hidden;
+  args.n_records = q.n_records;
+  args.hidden = q.hidden;
   args.hidden_pad = hp;
-  args.ids = ids;
+  args.ids = q.ids;
   args.ids64 = ids_dtype == QCC_INDEX_I64;
-  args.ids_ready = (ids_kind & QCC_IDS_READY) != 0;
-  args.token_mask = token_mask;
+  args.ids_ready = (q.ids_kind & QCC_IDS_READY) != 0;
+  args.token_mask = q.token_mask;
   args.n_ids = n_ids;
-  args.n_ids_dev = n_ids_dev;
+  args.n_ids_dev = q.n_ids_dev;
   args.status = reinterpret_cast<unsigned int*>(ws);
   args.partials = partials;
   args.part_per = per;
-  args.a_out = activation_out;
-  args.lda = lda;
-  args.a_dtype = dtype;
+  args.a_out = q.activation_out;
+  args.lda = q.lda;
+  args.a_dtype = q.dtype;
   args.stages = shape.stages;
   args.id_cap = id_cap;
   args.ring_bytes = static_cast<int64_t>(shape.ring);
-  args.x_vec = (hidden % 8 == 0) && aligned16(x) && ((ldx * dtype_bytes(dtype)) % 16 == 0);
-  args.id_lo = id_lo >= 0 ? id_lo : -1;
-  args.id_hi = id_lo >= 0 ? id_hi : -1;
+  args.x_vec = q.x != nullptr && (q.hidden % 8 == 0) && aligned16(q.x) && ((q.ldx * dtype_bytes(q.dtype)) % 16 == 0);
+  args.id_lo = q.id_lo >= 0 ? q.id_lo : -1;
+  args.id_hi = q.id_lo >= 0 ? q.id_hi : -1;
+  args.copy_offset = copy_offset;
+  args.copy_bytes = static_cast<int>(copy_bytes);
+  args.act_out = q.act_out;
+  args.ld_act_out = q.ld_act_out;
+  args.score_out = q.score_out;
+  args.ld_score = q.ld_score;
+  args.col_w = q.col_w;
+  args.act_in = q.act_in;
+  args.ld_act_in = q.ld_act_in;
+  args.act_in_dtype = q.act_in_dtype;
+
+  clear_stale_error();
+  if (!launch_dependent(fn, args, static_cast<unsigned>(grid), static_cast<unsigned>(shape.threads), shape.smem,
+                        q.stream))
+    return QCC_ERR_CUDA;
+  if (mode == kModeGateUp) return QCC_OK;  // no partial rows to reduce
 
   ReduceArgs red;
   red.partials = partials;
@@ -868,32 +1029,67 @@ int indexed_ffn_decode(const void* x, int64_t ldx, int batch, int hidden, const 
   red.per = per;
   red.nvec = nvec;
   red.seg = hp;
-  red.hidden = hidden;
-  red.y_out = y_out;
-  red.ldy = ldy;
-  red.y_dtype = y_dtype;
-  red.y_in = y_in;
-  red.ld_in = ld_in;
+  red.hidden = q.hidden;
+  red.y_out = q.y_out;
+  red.ldy = q.ldy;
+  red.y_dtype = q.y_dtype;
+  red.y_in = q.y_in;
+  red.ld_in = q.ld_in;
   red.status = reinterpret_cast<unsigned int*>(ws);
   red.depart = reinterpret_cast<unsigned int*>(ws + 8);
-  red.world = world;
-  red.rank = rank;
+  red.world = q.world;
+  red.rank = q.rank;
   red.slot_words = slot_words;
-  red.epoch = world > 1 ? static_cast<unsigned int*>(xchg[rank]) : nullptr;
-  red.wait_limit = world > 1 ? reinterpret_cast<const unsigned long long*>(
-                                   static_cast<const uint8_t*>(xchg[rank]) + kXchgLimitOffset)
-                             : nullptr;
-  for (int q = 0; q < kMaxRanks; ++q)
-    red.xchg[q] = q < world && world > 1 ? static_cast<uint8_t*>(xchg[q]) + kXchgHeader : nullptr;
-
-  clear_stale_error();
-  if (!launch_dependent(fn, args, static_cast<unsigned>(grid), static_cast<unsigned>(shape.threads), shape.smem,
-                        stream))
-    return QCC_ERR_CUDA;
+  red.epoch = q.world > 1 ? static_cast<unsigned int*>(q.xchg[q.rank]) : nullptr;
+  red.wait_limit = q.world > 1 ? reinterpret_cast<const unsigned long long*>(
+                                     static_cast<const uint8_t*>(q.xchg[q.rank]) + kXchgLimitOffset)
+                               : nullptr;
+  for (int r = 0; r < kMaxRanks; ++r)
+    red.xchg[r] = r < q.world && q.world > 1 ? static_cast<uint8_t*>(q.xchg[r]) + kXchgHeader : nullptr;
   if (!launch_dependent(decode_reduce_kernel, red, static_cast<unsigned>(slices),
-                        static_cast<unsigned>(reduce_threads), 0, stream))
+                        static_cast<unsigned>(reduce_threads), 0, q.stream))
     return QCC_ERR_CUDA;
   return QCC_OK;
+}
+
+}  // namespace
+
+int indexed_ffn_decode(const void* x, int64_t ldx, int batch, int hidden, const void* packed, int64_t n_records,
+                       int dtype, const void* ids, int ids_kind, int n_ids, const int32_t* n_ids_dev,
+                       const uint8_t* token_mask, void* workspace, size_t workspace_bytes, void* y_out, int64_t ldy,
+                       int y_dtype, const float* y_in, int64_t ld_in, void* activation_out, int64_t lda,
+                       cudaStream_t stream, void* const* xchg, size_t xchg_bytes, int world, int rank,
+                       int64_t id_lo, int64_t id_hi) {
+  DecodeRequest q;
+  q.x = x;
+  q.ldx = ldx;
+  q.batch = batch;
+  q.hidden = hidden;
+  q.packed = packed;
+  q.n_records = n_records;
+  q.dtype = dtype;
+  q.ids = ids;
+  q.ids_kind = ids_kind;
+  q.n_ids = n_ids;
+  q.n_ids_dev = n_ids_dev;
+  q.token_mask = token_mask;
+  q.workspace = workspace;
+  q.workspace_bytes = workspace_bytes;
+  q.y_out = y_out;
+  q.ldy = ldy;
+  q.y_dtype = y_dtype;
+  q.y_in = y_in;
+  q.ld_in = ld_in;
+  q.activation_out = activation_out;
+  q.lda = lda;
+  q.stream = stream;
+  q.xchg = xchg;
+  q.xchg_bytes = xchg_bytes;
+  q.world = world;
+  q.rank = rank;
+  q.id_lo = id_lo;
+  q.id_hi = id_hi;
+  return launch_decode(q);
 }
 
 size_t exchange_bytes(int world, int batch, int hidden, int dtype) {
@@ -941,4 +1137,73 @@ extern "C" int qcc_indexed_ffn_decode_allreduce(const void* x, int64_t ldx, int 
   return qcc::indexed_ffn_decode(x, ldx, batch, hidden, packed, n_records, dtype, ids, ids_dtype, n_ids, n_ids_dev,
                                  token_mask, workspace, workspace_bytes, y_out, ldy, y_dtype, y_in, ld_in, nullptr, 0,
                                  stream, exchange, exchange_bytes, world, rank, id_begin, id_end);
+}
+
+namespace qcc {
+namespace {
+
+int activation_pass(const void* x, int64_t ldx, int batch, int hidden, const void* packed, int64_t n_records,
+                    int dtype, const float* col_weights, float* act_out, int64_t ld_act, float* scores_out,
+                    int64_t ld_scores, void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+  DecodeRequest q;
+  q.mode = kModeGateUp;
+  q.x = x;
+  q.ldx = ldx;
+  q.batch = batch;
+  q.hidden = hidden;
+  q.packed = packed;
+  q.n_records = n_records;
+  q.dtype = dtype;
+  q.n_ids = n_records > 0x7fffffff ? -1 : static_cast<int>(n_records);  // every record, in order
+  q.workspace = workspace;
+  q.workspace_bytes = workspace_bytes;
+  q.stream = stream;
+  q.act_out = act_out;
+  q.ld_act_out = ld_act;
+  q.score_out = scores_out;
+  q.ld_score = ld_scores;
+  q.col_w = col_weights;
+  return launch_decode(q);
+}
+
+}  // namespace
+}  // namespace qcc
+
+extern "C" int qcc_ffn_activations(const void* x, int64_t ldx, int batch, int hidden, const void* packed,
+                                   int64_t n_records, int dtype, const float* col_weights, float* act_out,
+                                   int64_t ld_act, float* scores_out, int64_t ld_scores, void* workspace,
+                                   size_t workspace_bytes, cudaStream_t stream) {
+  return qcc::activation_pass(x, ldx, batch, hidden, packed, n_records, dtype, col_weights, act_out, ld_act,
+                              scores_out, ld_scores, workspace, workspace_bytes, stream);
+}
+
+extern "C" int qcc_indexed_ffn_down(const void* act, int64_t ld_act, int act_dtype, int batch, int hidden,
+                                    const void* packed, int64_t n_records, int dtype, const void* ids, int ids_dtype,
+                                    int n_ids, const int32_t* n_ids_dev, const uint8_t* token_mask, void* workspace,
+                                    size_t workspace_bytes, void* y_out, int64_t ldy, int y_dtype, const float* y_in,
+                                    int64_t ld_in, cudaStream_t stream) {
+  qcc::DecodeRequest q;
+  q.mode = qcc::kModeDown;
+  q.batch = batch;
+  q.hidden = hidden;
+  q.packed = packed;
+  q.n_records = n_records;
+  q.dtype = dtype;
+  q.ids = ids;
+  q.ids_kind = ids_dtype;
+  q.n_ids = n_ids;
+  q.n_ids_dev = n_ids_dev;
+  q.token_mask = token_mask;
+  q.workspace = workspace;
+  q.workspace_bytes = workspace_bytes;
+  q.y_out = y_out;
+  q.ldy = ldy;
+  q.y_dtype = y_dtype;
+  q.y_in = y_in;
+  q.ld_in = ld_in;
+  q.stream = stream;
+  q.act_in = act;
+  q.ld_act_in = ld_act;
+  q.act_in_dtype = act_dtype;
+  return qcc::launch_decode(q);
 }

@@ -14,6 +14,14 @@
 // runtime/selector.py:24 and end_to_end/oracle_sparse_mlp.py:75, with the
 // tie order fixed.
 //
+// qcc_activation_topk: the same selection with the scores made on the fly
+// from an activation row a (bf16 / fp16 / fp32) and optional per-column fp32
+// weights w: score = |a| (importance "activation", oracle/importance.py:10)
+// or |a| * w (the down-column-norm weighting of
+// end_to_end/oracle_sparse_mlp.py:75, one fp32 rounding as there), plus an
+// optional masked copy of the row (a where selected, 0 elsewhere) -- the
+// zeros().scatter_(gather) of the same line -- written in the output pass.
+//
 // qcc_build_union: one CTA.  Sets per-neuron token bits for all rows in a
 // shared byte map over [id_begin, id_end) and compacts the non-zero entries
 // with one block-wide scan.
@@ -36,9 +44,36 @@ constexpr int kDigitBins = 1 << 10;                        // key bits 19..10, t
 constexpr int kCandidateCap = kDigit1Bins - kDigitBins;   // candidate keys that fit beside a 10-bit histogram
 constexpr int kLoadRound = 8;                              // loads in flight per thread
 
+// How a row element becomes its score.
+constexpr int kScoreRaw = 0;       // the fp32 value itself
+constexpr int kScoreAbs = 1;       // |a|
+constexpr int kScoreAbsScaled = 2;  // |a| * w[i]
+
+template <int SCORE>
+__device__ __forceinline__ float make_score(float v, const float* w, int i) {
+  if constexpr (SCORE == kScoreRaw) return v;
+  else if constexpr (SCORE == kScoreAbs) return fabsf(v);
+  else return fabsf(v) * __ldg(w + i);
+}
+
+template <typename T>
+__device__ __forceinline__ void widen_any(uint4 raw, float (&f)[16 / sizeof(T)]) {
+  if constexpr (sizeof(T) == 4) {
+    f[0] = __uint_as_float(raw.x);
+    f[1] = __uint_as_float(raw.y);
+    f[2] = __uint_as_float(raw.z);
+    f[3] = __uint_as_float(raw.w);
+  } else {
+    Pack8<T> p;
+    p.w[0] = raw;
+    widen(p, f);
+  }
+}
+
+template <typename T, int SCORE>
 __global__ void __launch_bounds__(kSelectThreads, 1)
-    select_topk_kernel(const float* __restrict__ scores, int64_t ld_scores, int n, int k, int32_t* __restrict__ ids,
-                       int64_t ld_ids) {
+    select_topk_kernel(const T* __restrict__ scores, int64_t ld_scores, const float* __restrict__ col_w, int n, int k,
+                       int32_t* __restrict__ ids, int64_t ld_ids, T* __restrict__ masked, int64_t ld_masked) {
   extern __shared__ __align__(16) uint32_t keys[];
   // Top-digit histogram; after that digit is chosen the same space holds the
   // candidate keys ([0, kCandidateCap)) and the 10-bit histograms after them.
@@ -50,8 +85,9 @@ __global__ void __launch_bounds__(kSelectThreads, 1)
   const int tid = threadIdx.x;
   const int lane = tid & 31;
   const int warp = tid >> 5;
-  const float* src = scores + blockIdx.x * ld_scores;
+  const T* src = scores + blockIdx.x * ld_scores;
   int32_t* out = ids + blockIdx.x * ld_ids;
+  constexpr int V = 16 / sizeof(T);  // elements per 16-byte load
 
   for (int i = tid; i < kDigit1Bins; i += kSelectThreads) hist[i] = 0;
   if (tid == 0) s_count = 0;
@@ -61,39 +97,44 @@ __global__ void __launch_bounds__(kSelectThreads, 1)
   //    All loads of a round are issued before any is used (one memory latency
   //    per round); 16-byte loads when the row is 16-byte aligned.
   const bool vec = (reinterpret_cast<uintptr_t>(src) & 15u) == 0;
-  const int n_vec = vec ? n / 4 : 0;
+  const int n_vec = vec ? n / V : 0;
   for (int base = 0; base < n_vec; base += kLoadRound * kSelectThreads) {
-    float4 v[kLoadRound];
+    uint4 v[kLoadRound];
 #pragma unroll
     for (int u = 0; u < kLoadRound; ++u) {
       const int i = base + u * kSelectThreads + tid;
-      v[u] = i < n_vec ? __ldg(reinterpret_cast<const float4*>(src) + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+      v[u] = i < n_vec ? __ldg(reinterpret_cast<const uint4*>(src) + i) : make_uint4(0u, 0u, 0u, 0u);
     }
 #pragma unroll
     for (int u = 0; u < kLoadRound; ++u) {
       const int i = base + u * kSelectThreads + tid;
       if (i < n_vec) {
-        const uint4 q = make_uint4(score_key(v[u].x), score_key(v[u].y), score_key(v[u].z), score_key(v[u].w));
-        reinterpret_cast<uint4*>(keys)[i] = q;
-        atomicAdd(&hist[q.x >> 20], 1);
-        atomicAdd(&hist[q.y >> 20], 1);
-        atomicAdd(&hist[q.z >> 20], 1);
-        atomicAdd(&hist[q.w >> 20], 1);
+        float f[V];
+        widen_any<T>(v[u], f);
+        uint32_t q[V];
+#pragma unroll
+        for (int e = 0; e < V; ++e) {
+          q[e] = score_key(make_score<SCORE>(f[e], col_w, V * i + e));
+          atomicAdd(&hist[q[e] >> 20], 1);
+        }
+#pragma unroll
+        for (int e = 0; e < V; e += 4)
+          reinterpret_cast<uint4*>(keys)[(V * i + e) / 4] = make_uint4(q[e], q[e + 1], q[e + 2], q[e + 3]);
       }
     }
   }
-  for (int base = 4 * n_vec; base < n; base += kLoadRound * kSelectThreads) {
+  for (int base = V * n_vec; base < n; base += kLoadRound * kSelectThreads) {
     float v[kLoadRound];
 #pragma unroll
     for (int u = 0; u < kLoadRound; ++u) {
       const int i = base + u * kSelectThreads + tid;
-      v[u] = i < n ? __ldg(src + i) : 0.f;
+      v[u] = i < n ? to_f32<T>(src[i]) : 0.f;
     }
 #pragma unroll
     for (int u = 0; u < kLoadRound; ++u) {
       const int i = base + u * kSelectThreads + tid;
       if (i < n) {
-        const uint32_t key = score_key(v[u]);
+        const uint32_t key = score_key(make_score<SCORE>(v[u], col_w, i));
         keys[i] = key;
         atomicAdd(&hist[key >> 20], 1);
       }
@@ -199,6 +240,10 @@ __global__ void __launch_bounds__(kSelectThreads, 1)
     const int eq_before = run_eq + __popc(b_eq & lt);
     if (is_gt) out[gt_before + min(eq_before, need)] = i;
     else if (is_eq && eq_before < need) out[gt_before + eq_before] = i;
+    if (masked != nullptr && i < seg_hi) {
+      const bool chosen = is_gt || (is_eq && eq_before < need);
+      masked[blockIdx.x * ld_masked + i] = chosen ? src[i] : T(0.f);
+    }
     run_gt += __popc(b_gt);
     run_eq += __popc(b_eq);
   }
@@ -260,12 +305,53 @@ extern "C" int qcc_select_topk(const float* scores, int64_t ld_scores, int batch
   const size_t static_smem = 20 * 1024;  // per-warp histograms, bins, scan scratch
   if (info.max_smem_optin <= 0 || smem + static_smem > static_cast<size_t>(info.max_smem_optin))
     return QCC_ERR_UNSUPPORTED;
-  if (!qcc::ensure_max_dynamic_smem(reinterpret_cast<const void*>(qcc::select_topk_kernel), device))
-    return QCC_ERR_CUDA;
+  auto fn = qcc::select_topk_kernel<float, qcc::kScoreRaw>;
+  if (!qcc::ensure_max_dynamic_smem(reinterpret_cast<const void*>(fn), device)) return QCC_ERR_CUDA;
   qcc::clear_stale_error();
-  qcc::select_topk_kernel<<<batch, qcc::kSelectThreads, smem, stream>>>(scores, ld_scores, n, k, ids_out, ld_ids);
+  fn<<<batch, qcc::kSelectThreads, smem, stream>>>(scores, ld_scores, nullptr, n, k, ids_out, ld_ids, nullptr, 0);
   if (!qcc::launch_ok()) return QCC_ERR_CUDA;
   return QCC_OK;
+}
+
+namespace {
+
+template <typename T>
+int activation_topk(const T* act, int64_t ld_act, int rows, int n, const float* col_weights, int k, int32_t* ids_out,
+                    int64_t ld_ids, T* masked, int64_t ld_masked, cudaStream_t stream) {
+  int device = 0;
+  if (!qcc::cuda_ok(cudaGetDevice(&device))) return QCC_ERR_CUDA;
+  const qcc::DeviceInfo& info = qcc::device_info(device);
+  const size_t smem = static_cast<size_t>(n) * sizeof(uint32_t);
+  const size_t static_smem = 20 * 1024;
+  if (info.max_smem_optin <= 0 || smem + static_smem > static_cast<size_t>(info.max_smem_optin))
+    return QCC_ERR_UNSUPPORTED;
+  auto fn = col_weights != nullptr ? qcc::select_topk_kernel<T, qcc::kScoreAbsScaled>
+                                   : qcc::select_topk_kernel<T, qcc::kScoreAbs>;
+  if (!qcc::ensure_max_dynamic_smem(reinterpret_cast<const void*>(fn), device)) return QCC_ERR_CUDA;
+  qcc::clear_stale_error();
+  fn<<<rows, qcc::kSelectThreads, smem, stream>>>(act, ld_act, col_weights, n, k, ids_out, ld_ids, masked, ld_masked);
+  if (!qcc::launch_ok()) return QCC_ERR_CUDA;
+  return QCC_OK;
+}
+
+}  // namespace
+
+extern "C" int qcc_activation_topk(const void* act, int64_t ld_act, int dtype, int rows, int n, const float* col_weights,
+                                   int k, int32_t* ids_out, int64_t ld_ids, void* masked_out, int64_t ld_masked,
+                                   cudaStream_t stream) {
+  if (!qcc::valid_dtype(dtype)) return QCC_ERR_DTYPE;
+  if (rows < 0 || n < 0 || k < 0 || k > n || ld_act < n || ld_ids < k) return QCC_ERR_SHAPE;
+  if (masked_out != nullptr && ld_masked < n) return QCC_ERR_SHAPE;
+  if (rows == 0 || n == 0) return QCC_OK;
+  if (act == nullptr || ids_out == nullptr) return QCC_ERR_INVALID_ARGUMENT;
+  if (dtype == QCC_DTYPE_BF16)
+    return activation_topk(static_cast<const __nv_bfloat16*>(act), ld_act, rows, n, col_weights, k, ids_out, ld_ids,
+                           static_cast<__nv_bfloat16*>(masked_out), ld_masked, stream);
+  if (dtype == QCC_DTYPE_F16)
+    return activation_topk(static_cast<const __half*>(act), ld_act, rows, n, col_weights, k, ids_out, ld_ids,
+                           static_cast<__half*>(masked_out), ld_masked, stream);
+  return activation_topk(static_cast<const float*>(act), ld_act, rows, n, col_weights, k, ids_out, ld_ids,
+                         static_cast<float*>(masked_out), ld_masked, stream);
 }
 
 extern "C" int qcc_build_union(const int32_t* ids, int64_t ld_ids, int batch, int k, int32_t id_begin,

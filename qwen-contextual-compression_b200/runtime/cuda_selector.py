@@ -64,6 +64,37 @@ def predictor_params(predictor, mean=None, std=None) -> tuple[dict, int, float]:
     return p, KIND_FACTORIZED, 1e-5
 
 
+def params_from_state_dict(state: dict, kind: str, mean=None, std=None) -> tuple[dict, int]:
+    """(weights, kind code) of a predictor ``state_dict`` as the reference's checkpoints store it.
+
+    kind is the reference's architecture name (predictor/models.py:58):
+    "residual_factorized" or "factorized"; keys follow the module attributes
+    (``encoder.weight``, ``residual_fc1.weight`` ...).  mean / std are folded
+    into the encoder as in ``predictor_params``.
+    """
+    if kind not in ("residual_factorized", "factorized"):
+        raise ValueError(f"Unknown predictor architecture: {kind}")
+
+    def get(name):
+        t = state.get(name)
+        return None if t is None else t.detach()
+
+    enc_w = get("encoder.weight").float()
+    enc_b = get("encoder.bias")
+    enc_b = None if enc_b is None else enc_b.float()
+    if std is not None:
+        enc_w = enc_w / std.detach().float().clamp_min(1e-6)[None, :]
+    if mean is not None:
+        shift = -(enc_w @ mean.detach().float())
+        enc_b = shift if enc_b is None else enc_b + shift
+    p = {"enc_w": enc_w, "enc_b": enc_b, "out_w": get("neurons.weight"), "out_b": get("neurons.bias")}
+    if kind == "factorized":
+        return p, KIND_FACTORIZED
+    p.update(fc1_w=get("residual_fc1.weight"), fc1_b=get("residual_fc1.bias"), fc2_w=get("residual_fc2.weight"),
+             fc2_b=get("residual_fc2.bias"), ln_w=get("layer_norm.weight"), ln_b=get("layer_norm.bias"))
+    return p, KIND_RESIDUAL
+
+
 class FusedScoreSelector:
     """Device copy of one predictor plus the fused scores + top-K launch."""
 

@@ -51,6 +51,45 @@ def select_topk(scores: torch.Tensor, k: int, out: torch.Tensor | None = None) -
     return out.squeeze(0) if squeeze else out
 
 
+def activation_topk(act: torch.Tensor, k: int, col_weights: torch.Tensor | None = None, *, masked: bool = False,
+                    out: torch.Tensor | None = None):
+    """Scores made from an activation and their top k, in one launch (``qcc_activation_topk``).
+
+    act [R, N] (or [N]) in bf16 / fp16 / fp32; score = |a| * col_weights
+    (fp32 [N]) or |a|.  Returns ascending int32 ids [R, k] -- and, with
+    ``masked=True``, also act with every unselected entry set to 0.
+    """
+    squeeze = act.ndim == 1
+    if squeeze:
+        act = act.unsqueeze(0)
+    if act.ndim != 2:
+        raise ValueError("act must be [rows, n] or [n]")
+    device = _lib.require_cuda(act, col_weights, out)
+    code = _lib.dtype_code(act.dtype)
+    if act.stride(1) != 1:
+        act = act.contiguous()
+    rows, n = act.shape
+    if not 0 <= k <= n:
+        raise ValueError(f"k must be in [0, {n}]")
+    if col_weights is not None and (col_weights.dtype != torch.float32 or col_weights.numel() != n
+                                    or not col_weights.is_contiguous()):
+        raise ValueError("col_weights must be a contiguous float32 tensor with one weight per column")
+    if out is None:
+        out = torch.empty((rows, k), dtype=torch.int32, device=device)
+    elif out.shape != (rows, k) or out.dtype != torch.int32 or out.stride(1) != 1:
+        raise ValueError("out must be a row-contiguous int32 [rows, k] tensor")
+    sparse = torch.empty_like(act) if masked else None
+    lib = _lib.library()
+    status = lib.qcc_activation_topk(act.data_ptr(), act.stride(0), code, rows, n, _lib.ptr(col_weights), k,
+                                     out.data_ptr(), out.stride(0), _lib.ptr(sparse),
+                                     sparse.stride(0) if sparse is not None else 0, _lib.stream_handle(device))
+    _lib.check(status, "qcc_activation_topk")
+    if squeeze:
+        out = out.squeeze(0)
+        sparse = None if sparse is None else sparse.squeeze(0)
+    return (out, sparse) if masked else out
+
+
 def build_union(ids: torch.Tensor, id_begin: int = 0, id_end: int | None = None, capacity: int | None = None):
     """Union of per-token sorted id rows [B, k] (B <= 8) restricted to [id_begin, id_end).
 

@@ -71,6 +71,23 @@ class HostOffloadLayer:
         self.record_bytes = self.resident.shape[1] * self.resident.element_size()
         self.step = 0
 
+    @classmethod
+    def from_artefact(cls, root, hot_ids: torch.Tensor, capacity: int, max_k: int,
+                      device: torch.device | str = "cuda", checksums: bool = True) -> "HostOffloadLayer":
+        """A layer whose records come from a packed-record artefact (``runtime.artefact``).
+
+        The reference's low-VRAM store loads its layers from a checksummed
+        stream cache (integration/freetoken_qcc/low_vram/host_store.py:29-57);
+        here the artefact's records are read once from disk into host memory,
+        the hot set goes to HBM and the rest into the pinned host store.
+        """
+        from . import artefact
+
+        manifest = artefact.load_manifest(root)
+        artefact.validate_files(root, manifest, checksums)
+        records = artefact.read_records(root, manifest)
+        return cls(records, manifest["hidden"], hot_ids, capacity, max_k, device)
+
     @property
     def cold_bytes(self) -> int:
         return self.cold_host.numel() * self.cold_host.element_size()

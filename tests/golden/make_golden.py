@@ -1,9 +1,9 @@
 """Generate the golden fixtures in this directory by running the REFERENCE itself.
 
-Run in a container where robjlyons/qwen-contextual-compression is checked out
-(default /root/reference, override with QCC_REFERENCE):
+Run where robjlyons/qwen-contextual-compression is checked out, naming the
+checkout in QCC_REFERENCE (required; there is no default location):
 
-    python tests/golden/make_golden.py
+    QCC_REFERENCE=<path to the reference checkout> python tests/golden/make_golden.py
 
 Every expected output below is produced by the reference's own functions
 (runtime.ffn, oracle.importance, oracle.sparse_ffn, end_to_end.oracle_sparse_mlp,
@@ -23,7 +23,9 @@ import numpy as np
 import torch
 
 HERE = Path(__file__).resolve().parent
-REFERENCE = Path(os.environ.get("QCC_REFERENCE", "/root/reference"))
+if not os.environ.get("QCC_REFERENCE"):
+    raise SystemExit("set QCC_REFERENCE to the reference checkout (robjlyons/qwen-contextual-compression)")
+REFERENCE = Path(os.environ["QCC_REFERENCE"])
 sys.path.insert(0, str(REFERENCE))
 sys.path.append(str(HERE.parents[1]))  # after the reference: its `oracle` package shadows this repo's
 

@@ -164,3 +164,37 @@ def test_patched_model_runs_sparse_on_gpu():
     assert patcher.norm_computation_count == 2
     assert patcher.wrappers[0].last_selected_indices.shape == (4, 16)
     patcher.restore()
+
+
+@pytest.mark.gpu
+def test_oracle_mlp_full_layer_size_bf16():
+    """hidden 5120, N 17408, bf16, 6 rows: selection bit-exact on the reference's score formula."""
+    from oracle.select import topk_ids
+
+    torch.manual_seed(5)
+    mlp = TinyFFN(5120, 17408).to(device="cuda", dtype=torch.bfloat16)
+    with torch.no_grad():
+        for lin in (mlp.gate_proj, mlp.up_proj, mlp.down_proj):
+            lin.weight.normal_(0.0, 0.02)
+    wrapper = OracleSparseMLP(mlp, 3, 0.25)
+    wrapper.set_mode(True)
+    x = torch.randn(2, 3, 5120, device="cuda", dtype=torch.bfloat16)
+    with torch.no_grad():
+        y = wrapper(x)
+        a = mlp.act_fn(mlp.gate_proj(x)) * mlp.up_proj(x)
+    norms = wrapper.down_column_norms
+    np.testing.assert_allclose(norms.cpu().numpy(),
+                               torch.linalg.vector_norm(mlp.down_proj.weight.detach().float(), dim=0).cpu().numpy(),
+                               rtol=2e-6)
+    scores = (a.abs().float() * norms).reshape(-1, 17408).cpu().numpy()
+    k = 4352
+    want = topk_ids(scores, k)
+    got = wrapper.last_selected_indices.reshape(-1, k).cpu().numpy()
+    assert np.array_equal(got, want)
+    sparse = torch.zeros_like(a).reshape(-1, 17408)
+    idx = torch.from_numpy(want).long().cuda()
+    sparse.scatter_(1, idx, a.reshape(-1, 17408).gather(1, idx))
+    with torch.no_grad():
+        expected = torch.nn.functional.linear(sparse.reshape(a.shape), mlp.down_proj.weight)
+    assert torch.equal(y, expected)
+    wrapper.close()

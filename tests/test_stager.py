@@ -115,3 +115,38 @@ def test_gather_refuses_pageable_host_memory():
     status = lib.qcc_gather_records(store.data_ptr(), 64, idx.data_ptr(), idx.data_ptr(), None, 1, dst.data_ptr(),
                                     torch.cuda.current_stream().cuda_stream)
     assert status == _lib.ERR_INVALID_ARGUMENT
+
+
+@pytest.mark.gpu
+def test_offload_full_size_eight_layers():
+    """The low-VRAM offload configuration at full size: 8 layers of hidden 5120 x N 17408 (bf16),
+    a quarter of each layer's records hot in HBM, K/N = 0.1 per token (80 % from the hot set, half
+    reused from the previous token), 2048 cache slots.  The cache policy is checked against the
+    oracle's slot cache at every step of every layer, y against the float64 oracle at the first
+    and last token of every layer."""
+    from qcc_b200.runtime.stager import HostOffloadLayer
+
+    hidden, n, layers, tokens, capacity = 5120, 17408, 8, 6, 2048
+    k = workloads.retention_k(n, 0.1)
+    x = workloads.decode_x().cuda()
+    for l in range(layers):
+        packed = workloads.decode_layer(device="cuda", seed=100 + l).packed.cpu()
+        hot = workloads.offload_hot_set(n, seed=11 + l)
+        seqs = workloads.offload_token_ids(n, k, hot, tokens, seed=12 + l)
+        stager = HostOffloadLayer(packed, hidden, hot, capacity=capacity, max_k=k, device="cuda")
+        cache = olru.SlotCache(n, hot.tolist(), capacity)
+        gate, up, down = packed[:, :hidden], packed[:, hidden:2 * hidden], packed[:, 2 * hidden:].t()
+        for t, ids in enumerate(seqs):
+            y = stager(x, ids.cuda())
+            expect = cache.step(ids.tolist(), t)
+            stats = stager.stats()
+            assert stats["overflow"] == 0
+            assert (stats["cache_hits"], stats["misses"], stats["evicted"], stats["hot_hits"]) == (
+                expect["hits"], expect["misses"], expect["evicted"], expect["hot_hits"]), (l, t)
+            assert stager.miss_slot[:stats["misses"]].tolist() == expect["miss_slots"]
+            if t in (0, tokens - 1):
+                assert stager.slot_of.tolist() == cache.slot_of
+                reference = offn.sparse_ffn_f64(x.cpu(), ids, gate, up, down)
+                assert offn.rel_l2(y.double().cpu().numpy(), reference) <= 1e-2, (l, t)
+        del stager, packed
+        torch.cuda.empty_cache()
