@@ -273,6 +273,36 @@ QCC_API int qcc_activation_topk(const void* act, int64_t ld_act, int dtype, int 
                                 cudaStream_t stream);
 
 /*
+ * Block top-K per score row (reference oracle/importance.py:26-35,
+ * block_topk_indices): the row's n scores are cut into ceil(n / block) blocks
+ * of `block` consecutive neurons (zero past the end), each block scored by
+ * the sum of its scores (fp64 in index order, rounded once to fp32), and the
+ * kb = max(1, min(n_blocks, ceil(k / block))) best blocks kept -- ties to
+ * the lower block, the rule of qcc_select_topk -- as kb ascending int32 block
+ * ids in block_ids[b * ld_ids ..].  Block j stands for neurons
+ * [j * block, min(n, (j + 1) * block)), the expansion of
+ * clustering/block_layout.py:61-64.  block_sums (optional) receives the sums.
+ * One launch, one CTA per row.
+ */
+QCC_API int qcc_block_topk(const float* scores, int64_t ld_scores, int rows, int n, int block, int k,
+                           int32_t* block_ids, int64_t ld_ids, float* block_sums, int64_t ld_sums,
+                           cudaStream_t stream);
+
+/*
+ * Per tile of tile_rows consecutive rows of block_ids [rows, kb]: the union
+ * of the rows' block ids, ascending, appended to tile_blocks; tile t's list is
+ * tile_blocks[tile_offsets[t] .. tile_offsets[t + 1]) -- the input of
+ * qcc_indexed_ffn_prefill (tile_rows 128).  tile_blocks must hold
+ * ceil(rows / tile_rows) * n_blocks entries; tile_offsets ceil(rows /
+ * tile_rows) + 1.  Ids outside [0, n_blocks) are skipped and set
+ * QCC_DEV_ID_RANGE in *status when status is not NULL.  One CTA;
+ * n_blocks <= 32768.
+ */
+QCC_API int qcc_tile_block_union(const int32_t* block_ids, int64_t ld_ids, int rows, int kb, int tile_rows,
+                                 int n_blocks, int32_t* tile_blocks, int32_t* tile_offsets, int32_t* status,
+                                 cudaStream_t stream);
+
+/*
  * Union of the per-token sorted id lists ids [batch, k] restricted to
  * [id_begin, id_end), rebased to id_begin: union_ids gets the sorted
  * distinct local ids, token_mask bit b says token b selected it, and

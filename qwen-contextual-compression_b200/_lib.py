@@ -50,6 +50,10 @@ SIGNATURES = {
     "qcc_select_topk": (_c_int, [_c_void_p, _c_int64, _c_int, _c_int, _c_int, _c_void_p, _c_int64, _c_void_p]),
     "qcc_activation_topk": (_c_int, [_c_void_p, _c_int64, _c_int, _c_int, _c_int, _c_void_p, _c_int, _c_void_p,
                                      _c_int64, _c_void_p, _c_int64, _c_void_p]),
+    "qcc_block_topk": (_c_int, [_c_void_p, _c_int64, _c_int, _c_int, _c_int, _c_int, _c_void_p, _c_int64, _c_void_p,
+                                _c_int64, _c_void_p]),
+    "qcc_tile_block_union": (_c_int, [_c_void_p, _c_int64, _c_int, _c_int, _c_int, _c_int, _c_void_p, _c_void_p,
+                                      _c_void_p, _c_void_p]),
     "qcc_ffn_activations": (_c_int, [_c_void_p, _c_int64, _c_int, _c_int, _c_void_p, _c_int64, _c_int, _c_void_p,
                                      _c_void_p, _c_int64, _c_void_p, _c_int64, _c_void_p, _c_size_t, _c_void_p]),
     "qcc_indexed_ffn_down": (_c_int, [_c_void_p, _c_int64, _c_int, _c_int, _c_int, _c_void_p, _c_int64, _c_int,

@@ -48,6 +48,7 @@ constexpr int kLoadRound = 8;                              // loads in flight pe
 constexpr int kScoreRaw = 0;       // the fp32 value itself
 constexpr int kScoreAbs = 1;       // |a|
 constexpr int kScoreAbsScaled = 2;  // |a| * w[i]
+constexpr int kScoreBlockSum = 3;   // element i = sum of the scores of block i (the row holds the blocks)
 
 template <int SCORE>
 __device__ __forceinline__ float make_score(float v, const float* w, int i) {
@@ -70,10 +71,15 @@ __device__ __forceinline__ void widen_any(uint4 raw, float (&f)[16 / sizeof(T)])
   }
 }
 
+// n is the length of the row the selection runs over: the scores themselves,
+// or with kScoreBlockSum the ceil(n_elems / block) block sums of a score row
+// of n_elems entries (zero past its end), summed in fp64 in index order and
+// rounded once; sums (optional) receives them.
 template <typename T, int SCORE>
 __global__ void __launch_bounds__(kSelectThreads, 1)
     select_topk_kernel(const T* __restrict__ scores, int64_t ld_scores, const float* __restrict__ col_w, int n, int k,
-                       int32_t* __restrict__ ids, int64_t ld_ids, T* __restrict__ masked, int64_t ld_masked) {
+                       int32_t* __restrict__ ids, int64_t ld_ids, T* __restrict__ masked, int64_t ld_masked,
+                       int block, int n_elems, float* __restrict__ sums, int64_t ld_sums) {
   extern __shared__ __align__(16) uint32_t keys[];
   // Top-digit histogram; after that digit is chosen the same space holds the
   // candidate keys ([0, kCandidateCap)) and the 10-bit histograms after them.
@@ -96,7 +102,20 @@ __global__ void __launch_bounds__(kSelectThreads, 1)
   // 1. Keys into shared memory, fused with the histogram of the top 12 bits.
   //    All loads of a round are issued before any is used (one memory latency
   //    per round); 16-byte loads when the row is 16-byte aligned.
-  const bool vec = (reinterpret_cast<uintptr_t>(src) & 15u) == 0;
+  if constexpr (SCORE == kScoreBlockSum) {
+    for (int i = tid; i < n; i += kSelectThreads) {
+      const int lo = i * block;
+      const int hi = min(n_elems, lo + block);
+      double acc = 0.0;
+      for (int j = lo; j < hi; ++j) acc += static_cast<double>(to_f32<T>(src[j]));
+      const float s = static_cast<float>(acc);
+      if (sums != nullptr) sums[blockIdx.x * ld_sums + i] = s;
+      const uint32_t key = score_key(s);
+      keys[i] = key;
+      atomicAdd(&hist[key >> 20], 1);
+    }
+  }
+  const bool vec = SCORE != kScoreBlockSum && (reinterpret_cast<uintptr_t>(src) & 15u) == 0;
   const int n_vec = vec ? n / V : 0;
   for (int base = 0; base < n_vec; base += kLoadRound * kSelectThreads) {
     uint4 v[kLoadRound];
@@ -123,7 +142,7 @@ __global__ void __launch_bounds__(kSelectThreads, 1)
       }
     }
   }
-  for (int base = V * n_vec; base < n; base += kLoadRound * kSelectThreads) {
+  for (int base = SCORE == kScoreBlockSum ? n : V * n_vec; base < n; base += kLoadRound * kSelectThreads) {
     float v[kLoadRound];
 #pragma unroll
     for (int u = 0; u < kLoadRound; ++u) {
@@ -289,9 +308,91 @@ __global__ void __launch_bounds__(kUnionThreads, 1)
   if (tid == 0) *count_out = total;
 }
 
+// One CTA: per tile of tile_rows consecutive rows, the union of the rows'
+// block ids as an ascending list, appended at the running offset.  A bitmap
+// of the n_blocks blocks in shared memory, one compaction scan per tile.
+__global__ void __launch_bounds__(kUnionThreads, 1)
+    tile_block_union_kernel(const int32_t* __restrict__ block_ids, int64_t ld_ids, int rows, int kb, int tile_rows,
+                            int n_blocks, int32_t* __restrict__ tile_blocks, int32_t* __restrict__ tile_offsets,
+                            int32_t* __restrict__ status) {
+  extern __shared__ __align__(16) uint32_t bits[];
+  __shared__ int scan_scratch[64];
+  const int tid = threadIdx.x;
+  const int nwords = (n_blocks + 31) / 32;
+  const int n_tiles = (rows + tile_rows - 1) / tile_rows;
+  int written = 0;
+  if (tid == 0) tile_offsets[0] = 0;
+  for (int t = 0; t < n_tiles; ++t) {
+    for (int i = tid; i < nwords; i += blockDim.x) bits[i] = 0u;
+    __syncthreads();
+    const int r0 = t * tile_rows;
+    const int r1 = min(rows, r0 + tile_rows);
+    for (int e = tid; e < (r1 - r0) * kb; e += blockDim.x) {
+      const int r = r0 + e / kb;
+      const int32_t b = __ldg(block_ids + r * ld_ids + e % kb);
+      if (b >= 0 && b < n_blocks) atomicOr(&bits[b >> 5], 1u << (b & 31));
+      else if (status != nullptr) atomicOr(reinterpret_cast<unsigned int*>(status), QCC_DEV_ID_RANGE);
+    }
+    __syncthreads();
+    // Thread i owns word i (32 blocks in order); one exclusive scan of popcounts.
+    const uint32_t w = tid < nwords ? bits[tid] : 0u;
+    int total;
+    int pos = written + block_exclusive_scan(__popc(w), scan_scratch, &total);
+    if (tid < nwords) {
+      uint32_t m = w;
+      while (m != 0u) {
+        const int bit = __ffs(m) - 1;
+        tile_blocks[pos++] = tid * 32 + bit;
+        m &= m - 1u;
+      }
+    }
+    written += total;
+    if (tid == 0) tile_offsets[t + 1] = written;
+    __syncthreads();
+  }
+}
+
 }  // namespace
 
 }  // namespace qcc
+
+extern "C" int qcc_block_topk(const float* scores, int64_t ld_scores, int rows, int n, int block, int k,
+                              int32_t* block_ids, int64_t ld_ids, float* block_sums, int64_t ld_sums,
+                              cudaStream_t stream) {
+  if (rows < 0 || n < 0 || block < 1 || k < 1 || ld_scores < n) return QCC_ERR_SHAPE;
+  const int n_blocks = (n + block - 1) / block;
+  const int kb = std::max(1, std::min(n_blocks, (k + block - 1) / block));
+  if (ld_ids < kb || (block_sums != nullptr && ld_sums < n_blocks)) return QCC_ERR_SHAPE;
+  if (rows == 0 || n == 0) return QCC_OK;
+  if (scores == nullptr || block_ids == nullptr) return QCC_ERR_INVALID_ARGUMENT;
+  int device = 0;
+  if (!qcc::cuda_ok(cudaGetDevice(&device))) return QCC_ERR_CUDA;
+  const qcc::DeviceInfo& info = qcc::device_info(device);
+  const size_t smem = static_cast<size_t>(n_blocks) * sizeof(uint32_t);
+  if (info.max_smem_optin <= 0 || smem + 20 * 1024 > static_cast<size_t>(info.max_smem_optin)) return QCC_ERR_UNSUPPORTED;
+  auto fn = qcc::select_topk_kernel<float, qcc::kScoreBlockSum>;
+  if (!qcc::ensure_max_dynamic_smem(reinterpret_cast<const void*>(fn), device)) return QCC_ERR_CUDA;
+  qcc::clear_stale_error();
+  fn<<<rows, qcc::kSelectThreads, smem, stream>>>(scores, ld_scores, nullptr, n_blocks, kb, block_ids, ld_ids, nullptr,
+                                                  0, block, n, block_sums, ld_sums);
+  if (!qcc::launch_ok()) return QCC_ERR_CUDA;
+  return QCC_OK;
+}
+
+extern "C" int qcc_tile_block_union(const int32_t* block_ids, int64_t ld_ids, int rows, int kb, int tile_rows,
+                                    int n_blocks, int32_t* tile_blocks, int32_t* tile_offsets, int32_t* status,
+                                    cudaStream_t stream) {
+  if (rows < 0 || kb < 0 || ld_ids < kb || tile_rows < 1 || n_blocks < 1) return QCC_ERR_SHAPE;
+  if (n_blocks > 32 * qcc::kUnionThreads) return QCC_ERR_UNSUPPORTED;
+  if (tile_offsets == nullptr || (rows > 0 && kb > 0 && (block_ids == nullptr || tile_blocks == nullptr)))
+    return QCC_ERR_INVALID_ARGUMENT;
+  const size_t smem = (static_cast<size_t>(n_blocks) + 31) / 32 * 4;
+  qcc::clear_stale_error();
+  qcc::tile_block_union_kernel<<<1, qcc::kUnionThreads, smem, stream>>>(block_ids, ld_ids, rows, kb, tile_rows,
+                                                                        n_blocks, tile_blocks, tile_offsets, status);
+  if (!qcc::launch_ok()) return QCC_ERR_CUDA;
+  return QCC_OK;
+}
 
 extern "C" int qcc_select_topk(const float* scores, int64_t ld_scores, int batch, int n, int k, int32_t* ids_out,
                                int64_t ld_ids, cudaStream_t stream) {
@@ -308,7 +409,8 @@ extern "C" int qcc_select_topk(const float* scores, int64_t ld_scores, int batch
   auto fn = qcc::select_topk_kernel<float, qcc::kScoreRaw>;
   if (!qcc::ensure_max_dynamic_smem(reinterpret_cast<const void*>(fn), device)) return QCC_ERR_CUDA;
   qcc::clear_stale_error();
-  fn<<<batch, qcc::kSelectThreads, smem, stream>>>(scores, ld_scores, nullptr, n, k, ids_out, ld_ids, nullptr, 0);
+  fn<<<batch, qcc::kSelectThreads, smem, stream>>>(scores, ld_scores, nullptr, n, k, ids_out, ld_ids, nullptr, 0, 0, 0,
+                                                   nullptr, 0);
   if (!qcc::launch_ok()) return QCC_ERR_CUDA;
   return QCC_OK;
 }
@@ -329,7 +431,8 @@ int activation_topk(const T* act, int64_t ld_act, int rows, int n, const float* 
                                    : qcc::select_topk_kernel<T, qcc::kScoreAbs>;
   if (!qcc::ensure_max_dynamic_smem(reinterpret_cast<const void*>(fn), device)) return QCC_ERR_CUDA;
   qcc::clear_stale_error();
-  fn<<<rows, qcc::kSelectThreads, smem, stream>>>(act, ld_act, col_weights, n, k, ids_out, ld_ids, masked, ld_masked);
+  fn<<<rows, qcc::kSelectThreads, smem, stream>>>(act, ld_act, col_weights, n, k, ids_out, ld_ids, masked, ld_masked,
+                                                  0, 0, nullptr, 0);
   if (!qcc::launch_ok()) return QCC_ERR_CUDA;
   return QCC_OK;
 }

@@ -90,6 +90,59 @@ def activation_topk(act: torch.Tensor, k: int, col_weights: torch.Tensor | None 
     return (out, sparse) if masked else out
 
 
+def block_topk(scores: torch.Tensor, k: int, block: int, *, with_sums: bool = False):
+    """Block top-K of fp32 score rows [R, N] (reference oracle/importance.py:26-35).
+
+    Returns ascending int32 block ids [R, kb], kb = max(1, min(ceil(N / block),
+    ceil(k / block))); block j covers neurons [j * block, min(N, (j+1) * block)).
+    ``with_sums=True`` also returns the fp32 block sums [R, ceil(N / block)].
+    """
+    squeeze = scores.ndim == 1
+    if squeeze:
+        scores = scores.unsqueeze(0)
+    if scores.ndim != 2 or scores.dtype != torch.float32:
+        raise ValueError("scores must be float32 [rows, n] or [n]")
+    if block <= 0:
+        raise ValueError("block_size must be positive")
+    device = _lib.require_cuda(scores)
+    if scores.stride(1) != 1:
+        scores = scores.contiguous()
+    rows, n = scores.shape
+    if not 1 <= k <= n:
+        raise ValueError(f"k must be in [1, {n}]")
+    n_blocks = (n + block - 1) // block
+    kb = max(1, min(n_blocks, (k + block - 1) // block))
+    ids = torch.empty((rows, kb), dtype=torch.int32, device=device)
+    sums = torch.empty((rows, n_blocks), dtype=torch.float32, device=device) if with_sums else None
+    lib = _lib.library()
+    _lib.check(lib.qcc_block_topk(scores.data_ptr(), scores.stride(0), rows, n, block, k, ids.data_ptr(), kb,
+                                  _lib.ptr(sums), n_blocks, _lib.stream_handle(device)), "qcc_block_topk")
+    if squeeze:
+        ids = ids[0]
+        sums = None if sums is None else sums[0]
+    return (ids, sums) if with_sums else ids
+
+
+def tile_block_union(block_ids: torch.Tensor, n_blocks: int, tile_rows: int = 128):
+    """Per tile of ``tile_rows`` rows, the ascending union of the rows' block ids.
+
+    Returns (flat int32 [capacity], offsets int32 [tiles + 1]) on the device --
+    the per-tile block lists ``BlockSparsePrefill`` takes.
+    """
+    if block_ids.ndim != 2 or block_ids.dtype != torch.int32 or block_ids.stride(1) != 1:
+        raise ValueError("block_ids must be a row-contiguous int32 [rows, kb] tensor")
+    device = _lib.require_cuda(block_ids)
+    rows, kb = block_ids.shape
+    tiles = (rows + tile_rows - 1) // tile_rows
+    flat = torch.empty(max(1, tiles * n_blocks), dtype=torch.int32, device=device)
+    offsets = torch.empty(tiles + 1, dtype=torch.int32, device=device)
+    lib = _lib.library()
+    _lib.check(lib.qcc_tile_block_union(block_ids.data_ptr(), block_ids.stride(0), rows, kb, tile_rows, n_blocks,
+                                        flat.data_ptr(), offsets.data_ptr(), None, _lib.stream_handle(device)),
+               "qcc_tile_block_union")
+    return flat, offsets
+
+
 def build_union(ids: torch.Tensor, id_begin: int = 0, id_end: int | None = None, capacity: int | None = None):
     """Union of per-token sorted id rows [B, k] (B <= 8) restricted to [id_begin, id_end).
 

@@ -63,7 +63,20 @@ def _rank(rank: int, world: int, port: int, queue) -> None:
             other_equal = torch.equal(other, y)
         else:
             other_equal = True
-        flags = torch.tensor([int(stable), int(other_equal)], device=device)
+        # Calls alternating batch 4 and batch 1 on one exchange buffer (sized for
+        # batch 4): slots are spaced by the buffer's size, so the batches never
+        # overlap and every call returns what the first call of its batch did.
+        x4 = workloads.decode_x(batch=4, hidden=hidden).to(device)
+        first4, first1 = fused(x4, ids), fused(x4[:1], ids)
+        alternating = True
+        for i in range(8):
+            if i % 2 == 0:
+                alternating = alternating and torch.equal(fused(x4, ids), first4)
+            else:
+                alternating = alternating and torch.equal(fused(x4[:1], ids), first1)
+        torch.cuda.synchronize(device)
+        close = offn.rel_l2(first1.double().cpu().numpy(), first4[:1].double().cpu().numpy()) <= 1e-2
+        flags = torch.tensor([int(stable), int(other_equal), int(alternating), int(close)], device=device)
         dist.all_reduce(flags, op=dist.ReduceOp.MIN)
         fused.engine.check()
         # Gather the full layer on rank 0 for the oracle (small layer).
@@ -100,4 +113,5 @@ def test_two_rank_sharded_layer_matches_oracle():
         p.join(timeout=120)
         assert p.exitcode == 0
     assert err_fused <= 1e-2 and err_nccl <= 1e-2
-    assert flags == [1, 1], "fused sum differs between ranks or between repeated calls"
+    assert flags[:2] == [1, 1], "fused sum differs between ranks or between repeated calls"
+    assert flags[2:] == [1, 1], "calls alternating batch 4 and batch 1 on one exchange buffer disagree"

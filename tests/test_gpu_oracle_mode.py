@@ -114,9 +114,10 @@ def test_down_pass_matches_f64_with_token_bits(dtype, tokens):
         sel = ids[t].cpu().long().numpy()
         want = d[:, sel] @ a[t, sel]
         assert offn.rel_l2(y[t], want) <= 1e-5
-    # Norm weights: ||D[:, j]|| of the packed down parts equals the oracle's fp32 norms.
+    # Norm weights: ||D[:, j]|| of the packed down parts against float64 norms (the
+    # weights' fp32 rounding is the only error left: sums are accumulated in fp64).
     np.testing.assert_allclose(down_column_norms(ffn.weights).cpu().numpy(),
-                               torch.linalg.vector_norm(down.float(), dim=0).numpy(), rtol=1e-6)
+                               np.linalg.norm(down.double().numpy(), axis=0), rtol=1e-7)
 
 
 def test_full_layer_size_weighted():
