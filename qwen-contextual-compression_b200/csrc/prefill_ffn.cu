@@ -9,9 +9,10 @@
 //
 // A call runs groups of up to four tiles (512 tokens); a group is two launches:
 //  plan     one CTA: per-block tile masks from the per-tile block lists; each
-//           tile's ascending block list; the gate/up work units (a tile with
-//           a pair of its blocks) with the prefix of their costs; every CTA's
-//           stream-K ranges.
+//           tile's ascending block list; the gate/up work units (a pair of
+//           blocks against each tile that uses them, the units of one pair
+//           adjacent) with the prefix of their costs; every CTA's stream-K
+//           ranges.
 //  prefill  one persistent CTA per SM (cooperative launch), two phases split by
 //           a grid barrier:
 //   1. gate/up: per unit (a tile and one or two of its blocks),
@@ -55,6 +56,7 @@ constexpr int kBlock = 64;                // records per block
 constexpr int kChunk = 64;                // hidden elements per gate/up K step (one 128-byte swizzled row)
 constexpr int kHRange = 256;              // hidden outputs per down unit (MMA N)
 constexpr int kMaxTiles = 4;
+constexpr int kMasks = (1 << kMaxTiles) - 1;  // non-empty tile masks of a block
 constexpr int kGroupTokens = kTile * kMaxTiles;
 constexpr int kStages = 4;
 // warp 0: weight TMA (first half of a stage's weight boxes), warp 1: MMA,
@@ -72,7 +74,7 @@ constexpr uint32_t kBox128 = 128 * 128;   // [128 rows x 64 elements]: 16 KB
 constexpr uint32_t kStageBytes = 48 * 1024;
 constexpr int kSmemList = 2048;           // down steps staged in shared memory
 constexpr int kPlanUnits = 4096;          // gate/up units the plan kernel keeps in shared memory
-constexpr int kPlanListBlocks = 4096;     // blocks up to which the plan keeps the tile lists in shared memory
+constexpr int kPlanListBlocks = 4096;     // blocks up to which the plan keeps its pairing sequence in shared memory
 constexpr int kMaxPlanGrid = 256;         // prefill CTAs the plan computes ranges for (one per SM)
 constexpr uint32_t kControlBytes = 12 * 1024;
 constexpr uint32_t kSmemBytes = kStages * kStageBytes + kControlBytes + 1024;  // + alignment slack
@@ -131,6 +133,7 @@ struct PrefillArgs {
   const int32_t* units;
   const int32_t* unit_prefix;  // [n_units + 1] exclusive cost prefix
   const int32_t* tile_list;    // [kMaxTiles][n_blocks]
+  const uint8_t* block_masks;  // [n_blocks] bit t: tile t uses the block
   const Ranges* ranges;        // [gridDim.x]
   int n_blocks;
   int n_chunks;                // gate/up K steps
@@ -325,18 +328,18 @@ __device__ bool range_of(int i, int g, Bound bound, Ranges* r, int ph) {
 }
 
 // ---------------------------------------------------------------------------
-// Plan.  Unit word: block << 8 | first tile << 4 | second tile (0xF: none).
-// One CTA: per-block tile masks, the gate/up units and their cost prefix,
-// each tile's ascending block list, then the stream-K ranges of every CTA
-// of the prefill grid (one thread per CTA).
+// Plan.  One CTA: per-block tile masks, each tile's ascending block list, the
+// gate/up units (words as above) and their cost prefix, then the stream-K
+// ranges of every CTA of the prefill grid.
 // ---------------------------------------------------------------------------
 
 __global__ void __launch_bounds__(kPlanThreads)
     prefill_plan_kernel(const int32_t* __restrict__ tile_blocks, const int32_t* __restrict__ tile_offsets,
                         int n_tiles, int n_blocks, int n_chunks, int n_hranges, int grid, int32_t* __restrict__ header,
                         int32_t* __restrict__ units, int32_t* __restrict__ unit_prefix,
-                        int32_t* __restrict__ tile_list, Ranges* __restrict__ ranges) {
-  extern __shared__ __align__(16) uint32_t words[];  // one mask byte per block, then the staged units / prefix
+                        int32_t* __restrict__ tile_list, int32_t* __restrict__ seq_global,
+                        uint32_t* __restrict__ block_masks, Ranges* __restrict__ ranges) {
+  extern __shared__ __align__(16) uint32_t words[];  // one mask byte per block, the staged units / prefix, the pairs
   __shared__ int scratch[64];
   __shared__ int s_down[kMaxDownUnits + 1];
   __shared__ int s_tile_count[kMaxTiles];
@@ -344,6 +347,7 @@ __global__ void __launch_bounds__(kPlanThreads)
   __shared__ int s_fail;
   __shared__ int s_epoch;
   __shared__ int s_bu[2][kMaxPlanGrid + 1], s_bk[2][kMaxPlanGrid + 1];  // stream-K range boundaries
+  __shared__ int s_group[kMasks + 1];  // start of each tile mask's group in the pairing sequence
   // The prefill launch that follows may be scheduled now; it waits for this
   // grid to complete before it reads anything.
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
@@ -352,8 +356,9 @@ __global__ void __launch_bounds__(kPlanThreads)
   const int cap = min(2 * n_blocks + 8, kPlanUnits);
   int* s_units = reinterpret_cast<int*>(words + n_words);
   int* s_prefix = s_units + cap;
-  const bool list_smem = n_blocks <= kPlanListBlocks;
-  int* s_list = s_prefix + cap + 1;  // [kMaxTiles][n_blocks] when list_smem
+  // The pairing sequence of the gate/up units (below): in shared memory up to
+  // kPlanListBlocks blocks, else in the workspace.
+  int* seq = n_blocks <= kPlanListBlocks ? s_prefix + cap + 1 : seq_global;
   for (int i = tid; i < n_words; i += blockDim.x) words[i] = 0u;
   if (tid == 0) {
     s_fail = 0;
@@ -393,6 +398,7 @@ __global__ void __launch_bounds__(kPlanThreads)
   }
   if (bad) atomicOr(header + kHdrStatus, QCC_DEV_ID_RANGE);
   __syncthreads();
+  for (int i = tid; i < n_words; i += blockDim.x) block_masks[i] = words[i];
   const uint8_t* mask = reinterpret_cast<const uint8_t*>(words);
   const int chunk = (n_blocks + blockDim.x - 1) / blockDim.x;
   const int lo = min(n_blocks, tid * chunk);
@@ -417,7 +423,6 @@ __global__ void __launch_bounds__(kPlanThreads)
     for (int t = 0; t < kMaxTiles; ++t)
       if (t < n_tiles && ((m >> t) & 1)) {
         tile_list[t * n_blocks + pos_t[t]] = i;
-        if (list_smem) s_list[t * n_blocks + pos_t[t]] = i;
         ++pos_t[t];
       }
   }
@@ -426,48 +431,101 @@ __global__ void __launch_bounds__(kPlanThreads)
     for (int t = 0; t < kMaxTiles; ++t) s_tile_count[t] = t < n_tiles ? tots[t] : 0;
   }
   __syncthreads();  // tile lists and counts visible to the block
-  const int* lst = list_smem ? s_list : tile_list;
-  // Gate/up units: each tile's blocks in pairs.  Order: pair i of every tile,
-  // then pair i + 1, so units sharing hot blocks run side by side; the cost
-  // prefix follows in closed form (kPairCost per chunk for a pair, kSingleCost for a single).
-  int n_pairs[kMaxTiles], odd[kMaxTiles];
-  int total_units = 0;
-#pragma unroll
-  for (int t = 0; t < kMaxTiles; ++t) {
-    const int c = t < n_tiles ? s_tile_count[t] : 0;
-    n_pairs[t] = (c + 1) / 2;
-    odd[t] = c & 1;
-    total_units += n_pairs[t];
-  }
-  for (int t = 0; t < n_tiles; ++t) {
-    for (int i = tid; i < n_pairs[t]; i += blockDim.x) {
-      int pos = 0, singles = 0;
-#pragma unroll
-      for (int t2 = 0; t2 < kMaxTiles; ++t2) {
-        pos += min(n_pairs[t2], i) + ((t2 < t && n_pairs[t2] > i) ? 1 : 0);
-        const int last = n_pairs[t2] - 1;  // index of t2's single, if it has one
-        singles += (odd[t2] && (last < i || (last == i && t2 < t))) ? 1 : 0;
+  // Gate/up units.  The blocks that any tile uses are put in one sequence,
+  // grouped by their tile mask (the groups in Gray-code order of the mask, so
+  // that neighbouring groups differ in one tile; ascending ids inside a
+  // group), and consecutive blocks of the sequence form the pairs.  A pair
+  // makes one unit for each tile that uses either of its blocks, and those
+  // units are adjacent: the tiles sharing a block run it on neighbouring CTAs a
+  // few K steps apart, so all but the first read its rows from L2.  (Pairing
+  // each tile's own blocks instead re-read shared blocks from DRAM: 329 MB of
+  // gate/up reads against 212 MB unique on a 512-token call.)  A tile that
+  // uses only one block of a pair -- only at a group boundary -- computes the
+  // other block's activations too, which nothing reads.  An odd block left
+  // over makes single-block units at the end.  Warp w counts and then places
+  // the blocks of mask gray(w + 1).
+  {
+    const int warp = tid >> 5, lane = tid & 31;
+    static_assert(kPlanThreads / 32 >= kMasks, "one warp per tile mask");
+    const int mv = (warp + 1) ^ ((warp + 1) >> 1);
+    if (warp < kMasks) {
+      int cnt = 0;
+      for (int b0 = 0; b0 < n_blocks; b0 += 32) {
+        const int b = b0 + lane;
+        cnt += __popc(__ballot_sync(0xffffffffu, b < n_blocks && mask[b] == mv));
       }
-      const int b1 = lst[t * n_blocks + 2 * i];
-      const bool two = 2 * i + 1 < s_tile_count[t];
-      const int b2 = two ? lst[t * n_blocks + 2 * i + 1] : kNoBlock;
+      if (lane == 0) s_group[warp] = cnt;
+    }
+    __syncthreads();
+    if (tid == 0) {
+      int o = 0;
+      for (int g = 0; g < kMasks; ++g) {
+        const int c = s_group[g];
+        s_group[g] = o;
+        o += c;
+      }
+      s_group[kMasks] = o;
+    }
+    __syncthreads();
+    if (warp < kMasks) {
+      int pos = s_group[warp];
+      for (int b0 = 0; b0 < n_blocks; b0 += 32) {
+        const int b = b0 + lane;
+        const bool hit = b < n_blocks && mask[b] == mv;
+        const uint32_t bal = __ballot_sync(0xffffffffu, hit);
+        if (hit) seq[pos + __popc(bal & ((1u << lane) - 1u))] = b;
+        pos += __popc(bal);
+      }
+    }
+    __syncthreads();
+  }
+  const int n_union = s_group[kMasks];
+  const int n_pairs = n_union / 2;
+  const int single_mask = (n_union & 1) ? mask[seq[n_union - 1]] : 0;
+  const int pchunk = (n_pairs + blockDim.x - 1) / blockDim.x;
+  const int p_lo = min(n_pairs, tid * pchunk);
+  const int p_hi = min(n_pairs, p_lo + pchunk);
+  int mine = 0;
+  for (int q = p_lo; q < p_hi; ++q) mine += __popc(mask[seq[2 * q]] | mask[seq[2 * q + 1]]);
+  int pair_units;
+  int pos = block_exclusive_scan(mine, scratch, &pair_units);
+  // Cost prefix: kPairCost per chunk for a pair unit, kSingleCost for a single.
+  for (int q = p_lo; q < p_hi; ++q) {
+    const int b1 = seq[2 * q], b2 = seq[2 * q + 1];
+    const int tm = mask[b1] | mask[b2];
+#pragma unroll
+    for (int t = 0; t < kMaxTiles; ++t) {
+      if (!((tm >> t) & 1)) continue;
       const int word = static_cast<int>((static_cast<uint32_t>(t) << 30) | (static_cast<uint32_t>(b2) << 15) |
                                         static_cast<uint32_t>(b1));
-      const int run = (kPairCost * (pos - singles) + kSingleCost * singles) * n_chunks;
+      const int run = kPairCost * pos * n_chunks;
       units[pos] = word;
       unit_prefix[pos] = run;
       if (pos < cap) {
         s_units[pos] = word;
         s_prefix[pos] = run;
       }
+      ++pos;
     }
   }
-  int total_singles = 0;
-#pragma unroll
-  for (int t = 0; t < kMaxTiles; ++t) total_singles += odd[t];
-  const int total_cost = kPairCost * (total_units - total_singles) + kSingleCost * total_singles;
-  const int total1 = total_cost * n_chunks;
+  const int total_units = pair_units + __popc(single_mask);
+  const int total1 = (kPairCost * pair_units + kSingleCost * (total_units - pair_units)) * n_chunks;
   if (tid == 0) {
+    int q = pair_units;
+    for (int t = 0; t < kMaxTiles; ++t) {
+      if (!((single_mask >> t) & 1)) continue;
+      const int word = static_cast<int>((static_cast<uint32_t>(t) << 30) |
+                                        (static_cast<uint32_t>(kNoBlock) << 15) |
+                                        static_cast<uint32_t>(seq[n_union - 1]));
+      const int run = (kPairCost * pair_units + kSingleCost * (q - pair_units)) * n_chunks;
+      units[q] = word;
+      unit_prefix[q] = run;
+      if (q < cap) {
+        s_units[q] = word;
+        s_prefix[q] = run;
+      }
+      ++q;
+    }
     for (int t = 0; t < kMaxTiles; ++t) header[kHdrTileCount + t] = t < n_tiles ? s_tile_count[t] : 0;
     header[kHdrUnits] = total_units;
     header[kHdrCost] = total1;
@@ -643,6 +701,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     // weight boxes into L2, by TMA or by the other lanes, measured slower: the
     // loads are not waiting on DRAM.)
     if (lane == 0) tma_prefetch_map(&tm_records);
+    // Rows of a block that several tiles use stay in L2 for the other tiles'
+    // units (which run on other CTAs, up to a unit's time apart); rows of a
+    // block that one tile uses are read once.
+    const uint64_t keep = policy_evict_last(), stream = policy_evict_first();
     bool stop = false;
     for (int si = 0, u; !stop && (u = seg_unit(ctl->r, 0, si, n_units)) >= 0; ++si) {
       int ks, ke;
@@ -660,8 +722,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint8_t* st = smem + s * kStageBytes + kBox128;
             mbar_arrive_expect_tx(&ctl->full[s], kBox128);
             const int b = unit_block(unit, 0);
-            tma_load_3d(st, &tm_records, kc * kChunk, 0, b * kBlock, &ctl->full[s]);
-            tma_load_3d(st + kBox64, &tm_records, kc * kChunk, 1, b * kBlock, &ctl->full[s]);
+            const uint64_t pol = __popc(a.block_masks[b]) > 1 ? keep : stream;
+            tma_load_3d_hint(st, &tm_records, kc * kChunk, 0, b * kBlock, &ctl->full[s], pol);
+            tma_load_3d_hint(st + kBox64, &tm_records, kc * kChunk, 1, b * kBlock, &ctl->full[s], pol);
           }
         }
         if (!__shfl_sync(0xffffffffu, ok, 0)) {
@@ -673,20 +736,22 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == kWeightWarp2 && lane == 0) {
     // Second weight loader: the gate and up rows of a pair's second block;
     // for a single-block unit it only arrives.
+    const uint64_t keep = policy_evict_last(), stream = policy_evict_first();
     for (int si = 0, u; (u = seg_unit(ctl->r, 0, si, n_units)) >= 0 && !*abort_flag; ++si) {
       int ks, ke;
       if (!segment(u, ctl->r.lo_u[0], ctl->r.lo_k[0], ctl->r.hi_u[0], ctl->r.hi_k[0], a.n_chunks, &ks, &ke)) continue;
       const int unit = a.units[u];
       const bool pair = unit_blocks(unit) == 2;
       const int b = pair ? unit_block(unit, 1) : 0;
+      const uint64_t pol = __popc(a.block_masks[b]) > 1 ? keep : stream;
       for (int kc = ks; kc < ke; ++kc, ++it) {
         const int s = it % kStages;
         if (!wait_phase(&ctl->empty[s], ((it / kStages) & 1u) ^ 1u, abort_flag, status)) break;
         if (pair) {
           uint8_t* st = smem + s * kStageBytes + 2 * kBox128;
           mbar_arrive_expect_tx(&ctl->full[s], kBox128);
-          tma_load_3d(st, &tm_records, kc * kChunk, 0, b * kBlock, &ctl->full[s]);
-          tma_load_3d(st + kBox64, &tm_records, kc * kChunk, 1, b * kBlock, &ctl->full[s]);
+          tma_load_3d_hint(st, &tm_records, kc * kChunk, 0, b * kBlock, &ctl->full[s], pol);
+          tma_load_3d_hint(st + kBox64, &tm_records, kc * kChunk, 1, b * kBlock, &ctl->full[s], pol);
         } else {
           mbar_arrive(&ctl->full[s]);
         }
@@ -696,6 +761,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // Activation loader: the x box of the unit's tile (A operand).
     tma_prefetch_map(&tm_x);
     tma_prefetch_map(&tm_abuf);
+    const uint64_t keep = policy_evict_last();  // every unit of the tile reads its x
     for (int si = 0, u; (u = seg_unit(ctl->r, 0, si, n_units)) >= 0 && !*abort_flag; ++si) {
       int ks, ke;
       if (!segment(u, ctl->r.lo_u[0], ctl->r.lo_k[0], ctl->r.hi_u[0], ctl->r.hi_k[0], a.n_chunks, &ks, &ke)) continue;
@@ -705,7 +771,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!wait_phase(&ctl->empty[s], ((it / kStages) & 1u) ^ 1u, abort_flag, status)) break;
         uint8_t* st = smem + s * kStageBytes;
         mbar_arrive_expect_tx(&ctl->full[s], kBox128);
-        tma_load_2d(st, &tm_x, kc * kChunk, t * kTile, &ctl->full[s]);
+        tma_load_2d_hint(st, &tm_x, kc * kChunk, t * kTile, &ctl->full[s], keep);
       }
     }
   } else if (warp == 1 && lane == 0) {
@@ -859,6 +925,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   // ------------------------------ phase 2 ------------------------------
   const int staged = min(ctl->n_steps, kSmemList);
   if (warp == 0) {
+    // Down rows of a block that several tiles use are read by each of their
+    // units of the same hidden range: kept in L2, as in phase 1.
+    const uint64_t keep = policy_evict_last(), stream = policy_evict_first();
     bool stop = false;
     int si = 0;  // position in this CTA's step sequence
     for (int sv = 0, v; !stop && (v = seg_unit(ctl->r, 1, sv, n_down)) >= 0; ++sv) {
@@ -878,9 +947,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             // loads the other 128.
             uint8_t* st = smem + s * kStageBytes;
             mbar_arrive_expect_tx(&ctl->full[s], 2 * kBox64);
+            const uint64_t pol = __popc(a.block_masks[b]) > 1 ? keep : stream;
             for (int qq = 0; qq < 2; ++qq)
-              tma_load_3d(st + kBox128 + qq * kBox64, &tm_records, r * kHRange + qq * 64, 2, b * kBlock,
-                          &ctl->full[s]);
+              tma_load_3d_hint(st + kBox128 + qq * kBox64, &tm_records, r * kHRange + qq * 64, 2, b * kBlock,
+                               &ctl->full[s], pol);
           }
         }
         if (!__shfl_sync(0xffffffffu, ok, 0)) {
@@ -891,6 +961,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     if (lane == 0) drain_loads(ctl, it);
   } else if (warp == kWeightWarp2 && lane == 0) {
+    const uint64_t keep = policy_evict_last(), stream = policy_evict_first();
     int si = 0;
     for (int sv = 0, v; (v = seg_unit(ctl->r, 1, sv, n_down)) >= 0 && !*abort_flag; ++sv) {
       const int t = v % a.n_tiles, r = v / a.n_tiles;
@@ -904,11 +975,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!wait_phase(&ctl->empty[s], ((it / kStages) & 1u) ^ 1u, abort_flag, status)) break;
         uint8_t* st = smem + s * kStageBytes;
         mbar_arrive_expect_tx(&ctl->full[s], 2 * kBox64);
+        const uint64_t pol = __popc(a.block_masks[b]) > 1 ? keep : stream;
         for (int qq = 2; qq < 4; ++qq)
-          tma_load_3d(st + kBox128 + qq * kBox64, &tm_records, r * kHRange + qq * 64, 2, b * kBlock, &ctl->full[s]);
+          tma_load_3d_hint(st + kBox128 + qq * kBox64, &tm_records, r * kHRange + qq * 64, 2, b * kBlock,
+                           &ctl->full[s], pol);
       }
     }
   } else if (warp == kActWarp && lane == 0) {
+    const uint64_t keep = policy_evict_last();  // each activation box is read once per hidden range
     int si = 0;
     for (int sv = 0, v; (v = seg_unit(ctl->r, 1, sv, n_down)) >= 0 && !*abort_flag; ++sv) {
       const int t = v % a.n_tiles;
@@ -922,7 +996,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!wait_phase(&ctl->empty[s], ((it / kStages) & 1u) ^ 1u, abort_flag, status)) break;
         uint8_t* st = smem + s * kStageBytes;
         mbar_arrive_expect_tx(&ctl->full[s], kBox128);
-        tma_load_2d(st, &tm_abuf, b * kBlock, t * kTile, &ctl->full[s]);
+        tma_load_2d_hint(st, &tm_abuf, b * kBlock, t * kTile, &ctl->full[s], keep);
       }
     }
   } else if (warp == 1 && lane == 0) {
@@ -1094,7 +1168,8 @@ bool make_map(CUtensorMap* map, int dtype, int rank, const void* base, const uin
 struct PrefillLayout {
   int n_blocks = 0, grid = 0;
   int64_t npad = 0;
-  size_t units = 0, prefix = 0, tile_list = 0, ranges = 0, flags1 = 0, flags2 = 0, abuf = 0, partials = 0, total = 0;
+  size_t units = 0, prefix = 0, tile_list = 0, seq = 0, masks = 0, ranges = 0, flags1 = 0, flags2 = 0, abuf = 0, partials = 0,
+         total = 0;
 };
 
 size_t round_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
@@ -1105,12 +1180,16 @@ PrefillLayout prefill_layout(int64_t n_records, int num_sms) {
   l.grid = num_sms;
   l.npad = static_cast<int64_t>(l.n_blocks) * kBlock;
   size_t off = kHeaderBytes;
-  l.units = off;  // at most one unit per two blocks of each tile, rounded up: 2 * n_blocks + 4
+  l.units = off;  // at most one unit per tile for every pair of blocks, rounded up: 2 * n_blocks + 2
   off = round_up(off + (2 * static_cast<size_t>(l.n_blocks) + 8) * 4, 256);
   l.prefix = off;
   off = round_up(off + (2 * static_cast<size_t>(l.n_blocks) + 9) * 4, 256);
   l.tile_list = off;
   off = round_up(off + static_cast<size_t>(kMaxTiles) * l.n_blocks * 4, 256);
+  l.seq = off;  // the plan's pairing sequence when it does not fit in shared memory
+  off = round_up(off + static_cast<size_t>(l.n_blocks) * 4, 256);
+  l.masks = off;  // one tile-mask byte per block
+  off = round_up(off + static_cast<size_t>(l.n_blocks) + 4, 256);
   l.ranges = off;
   off = round_up(off + static_cast<size_t>(l.grid) * sizeof(Ranges), 256);
   l.flags1 = off;
@@ -1169,6 +1248,7 @@ extern "C" int qcc_indexed_ffn_prefill(const void* x, int64_t ldx, int n_tokens,
   args.units = reinterpret_cast<int32_t*>(ws + l.units);
   args.unit_prefix = reinterpret_cast<int32_t*>(ws + l.prefix);
   args.tile_list = reinterpret_cast<int32_t*>(ws + l.tile_list);
+  args.block_masks = ws + l.masks;
   args.ranges = reinterpret_cast<const Ranges*>(ws + l.ranges);
   args.n_blocks = l.n_blocks;
   args.n_chunks = (hidden + kChunk - 1) / kChunk;
@@ -1206,7 +1286,7 @@ extern "C" int qcc_indexed_ffn_prefill(const void* x, int64_t ldx, int n_tokens,
   const size_t plan_smem =
       round_up(static_cast<size_t>(l.n_blocks), 4) +
       (2 * static_cast<size_t>(std::min(2 * l.n_blocks + 8, kPlanUnits)) + 1) * 4 +
-      (l.n_blocks <= kPlanListBlocks ? static_cast<size_t>(kMaxTiles) * l.n_blocks * 4 : 0);
+      (l.n_blocks <= kPlanListBlocks ? static_cast<size_t>(l.n_blocks) * 4 : 0);
   const uint8_t* xb = static_cast<const uint8_t*>(x);
   uint8_t* yb = static_cast<uint8_t*>(y);
 
@@ -1227,7 +1307,8 @@ extern "C" int qcc_indexed_ffn_prefill(const void* x, int64_t ldx, int n_tokens,
     prefill_plan_kernel<<<1, kPlanThreads, plan_smem, stream>>>(
         tile_blocks, tile_offsets + g0 / kTile, args.n_tiles, l.n_blocks, args.n_chunks, args.n_hranges, l.grid,
         args.header, const_cast<int32_t*>(args.units), const_cast<int32_t*>(args.unit_prefix),
-        const_cast<int32_t*>(args.tile_list), const_cast<Ranges*>(args.ranges));
+        const_cast<int32_t*>(args.tile_list), reinterpret_cast<int32_t*>(ws + l.seq),
+        reinterpret_cast<uint32_t*>(ws + l.masks), const_cast<Ranges*>(args.ranges));
     if (!launch_ok()) return QCC_ERR_CUDA;
     // Every CTA must be resident at once (grid barrier, cross-CTA flags).
     cudaLaunchConfig_t cfg = {};

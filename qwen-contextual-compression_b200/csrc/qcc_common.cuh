@@ -64,6 +64,13 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
   }
 }
 
+// Cache policy for data that later reads of the same kernel should find in L2.
+__device__ __forceinline__ uint64_t policy_evict_last() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+
 // Cache policy for streamed weights: read once, do not keep in L2.
 __device__ __forceinline__ uint64_t policy_evict_first() {
   uint64_t p;
