@@ -483,7 +483,18 @@ def measure_prefill(device, stream, side, cpu_seconds: float) -> dict:
                         "unique_record_bytes": unique,
                         "hbm_gbs_of_unique_bytes": round(unique / (us * 1e-6) / 1e9, 1)},
            "gpu_launches_per_step": 2}
-    del engines, layers
+    del engines
+    # The same call on fp32 records (kind::tf32: the products use the tf32 part
+    # of each operand, sums in fp32); the tf32 dense rate is half the bf16 one.
+    engines = [BlockSparsePrefill(PackedFFNWeights(l.packed.float(), HIDDEN, INTERMEDIATE)) for l in layers]
+    del layers
+    x32, y32 = x.float(), torch.empty(x.shape, dtype=torch.float32, device=device)
+    us32 = graph_time_us(lambda i: engines[i % 2](x32, (flat, offsets), out=y32), steps, stream, side)
+    achieved32 = flops / (us32 * 1e-6) / 1e12
+    out["fp32_records"] = {"us": round(us32, 2), "tflops": round(achieved32, 1),
+                           "frac_of_half_bf16_peak": round(achieved32 / (peak / 2), 4),
+                           "record_bytes_unique": 2 * unique}
+    del engines
     torch.cuda.empty_cache()
     if cpu_seconds > 0:
         out["cpu_baseline"] = prefill_cpu_sample(tiles, cpu_seconds)

@@ -483,9 +483,11 @@ QCC_API int qcc_selector_scores_topk(const void* x, int64_t ldx, int batch, int 
  * tile_offsets[t+1]), device arrays, each block at most once per tile, any
  * order.  For every row r of tile t:
  *   y[r] = sum over records n of t's blocks of silu(g_n . x_r) (u_n . x_r) d_n,
- * fp32 accumulation on the tensor cores; the activation is rounded to the
- * weight type between the two products (as the reference's CUDA path rounds it
- * to fp16, runtime/cuda_indexed.py:28-30).
+ * fp32 accumulation on the tensor cores; for bf16 / fp16 records the
+ * activation is rounded to the weight type between the two products (as the
+ * reference's CUDA path rounds it to fp16, runtime/cuda_indexed.py:28-30).
+ * fp32 records run on kind::tf32: each product uses the tf32 part of its fp32
+ * operands (x, the rows, the fp32 activation), the sums stay fp32.
  * ------------------------------------------------------------------------- */
 
 /* Workspace for qcc_indexed_ffn_prefill on the current device (0 on bad
@@ -495,12 +497,12 @@ QCC_API size_t qcc_prefill_workspace_bytes(int64_t n_records, int hidden);
 /* Byte offset of the int32 status word (QCC_DEV_* bits) in that workspace. */
 QCC_API size_t qcc_prefill_workspace_status_offset(void);
 
-/* x: [n_tokens, hidden] with row stride ldx (elements, ldx * 2 a multiple of
- * 16), bf16 or fp16 like the records; packed: n_records records as packed by
- * qcc_pack_records; tile_offsets: ceil(n_tokens / 128) + 1 entries;
- * y: [n_tokens, hidden], row stride ldy, y_dtype.  fp32 records return
- * QCC_ERR_UNSUPPORTED.  Block ids out of range are skipped and set
- * QCC_DEV_ID_RANGE in the workspace status. */
+/* x: [n_tokens, hidden] with row stride ldx (elements; ldx times the element
+ * size a multiple of 16), in the records' dtype (bf16, fp16 or fp32); packed:
+ * n_records records as packed by qcc_pack_records; tile_offsets:
+ * ceil(n_tokens / 128) + 1 entries; y: [n_tokens, hidden], row stride ldy,
+ * y_dtype.  Block ids out of range are skipped and set QCC_DEV_ID_RANGE in the
+ * workspace status. */
 QCC_API int qcc_indexed_ffn_prefill(const void* x, int64_t ldx, int n_tokens, int hidden, const void* packed,
                                     int64_t n_records, int dtype, const int32_t* tile_blocks,
                                     const int32_t* tile_offsets, void* workspace, size_t workspace_bytes, void* y,

@@ -53,24 +53,24 @@ namespace {
 
 constexpr int kTile = 128;                // tokens per tile (MMA M)
 constexpr int kBlock = 64;                // records per block
-constexpr int kChunk = 64;                // hidden elements per gate/up K step (one 128-byte swizzled row)
+constexpr int kRowBytes = 128;            // one 128-byte swizzled row: a gate/up K step (64 16-bit or 32 fp32 elements)
 constexpr int kHRange = 256;              // hidden outputs per down unit (MMA N)
 constexpr int kMaxTiles = 4;
 constexpr int kMasks = (1 << kMaxTiles) - 1;  // non-empty tile masks of a block
 constexpr int kGroupTokens = kTile * kMaxTiles;
 constexpr int kStages = 4;
-// warp 0: weight TMA (first half of a stage's weight boxes), warp 1: MMA,
-// warps 2-5: TMEM readers, warp 6: activation TMA, warp 7: weight TMA (second
-// half).  One issuing thread reaches only ~5 M tiled TMA copies/s, so a step's
-// boxes are spread over three threads in different warps.
+// warp 1: MMA, warps 2-5: TMEM readers, warps 0, 6 and 7: TMA producers.  A
+// thread issuing tiled TMA copies back to back spends ~0.25 us per ring
+// iteration plus ~0.1 us per box (measured: 6 boxes of 64 rows from L2 in
+// 0.79 us), so each ring iteration is loaded in full by one producer and the
+// three take turns: iteration i belongs to producer i % 3.
 constexpr int kThreads = 256;
-constexpr int kActWarp = 6;
-constexpr int kWeightWarp2 = 7;
+constexpr int kProducerWarp[3] = {0, 6, 7};
+constexpr int kProducers = 3;
 constexpr int kFirstReader = 2, kReaders = 4;  // warps 2-5 read TMEM (warp w: lanes 32*(w%4) .. +31)
-constexpr int kLoaders = 3;                    // arrivals on a stage's full barrier
 constexpr int kPlanThreads = 1024;
-constexpr uint32_t kBox64 = 64 * 128;     // [64 rows x 64 elements] of 16-bit: 8 KB
-constexpr uint32_t kBox128 = 128 * 128;   // [128 rows x 64 elements]: 16 KB
+constexpr uint32_t kBox64 = 64 * 128;     // [64 rows x 128 bytes]: 8 KB
+constexpr uint32_t kBox128 = 128 * 128;   // [128 rows x 128 bytes]: 16 KB
 constexpr uint32_t kStageBytes = 48 * 1024;
 constexpr int kSmemList = 2048;           // down steps staged in shared memory
 constexpr int kPlanUnits = 4096;          // gate/up units the plan kernel keeps in shared memory
@@ -124,8 +124,8 @@ struct Control {
 };
 static_assert(sizeof(Control) <= kControlBytes, "control block");
 static_assert(offsetof(Control, r) % 16 == 0, "the ranges record is copied with 16-byte accesses");
-static_assert(kActWarp >= kFirstReader + kReaders && kActWarp * 32 < kThreads, "warp roles");
-static_assert(kWeightWarp2 >= kFirstReader + kReaders && kWeightWarp2 != kActWarp && kWeightWarp2 * 32 < kThreads,
+static_assert(kProducerWarp[1] >= kFirstReader + kReaders && kProducerWarp[2] > kProducerWarp[1] &&
+                  kProducerWarp[2] * 32 < kThreads && kProducerWarp[0] == 0,
               "warp roles");
 
 struct PrefillArgs {
@@ -141,7 +141,7 @@ struct PrefillArgs {
   int hidden;
   int n_tokens;                // rows of this group
   int n_tiles;
-  uint16_t* abuf;
+  void* abuf;                  // activations: 16-bit, or fp32 for fp32 records
   int64_t ld_abuf;
   float* partials;             // [gridDim.x][kSlotFloats]
   int32_t* flags1;             // [gridDim.x]
@@ -222,6 +222,21 @@ __device__ __forceinline__ void fence_proxy_async_global() {
 __device__ __forceinline__ void epilogue_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 
 __device__ __forceinline__ float silu(float g) { return __fdividef(g, 1.f + __expf(-g)); }
+
+// Per operand format (kFmtF16 / kFmtBF16 / kFmtTF32): element bytes, the
+// elements of a 128-byte row (a gate/up K step, and the records of one down
+// step), and the down rows' boxes per 256-wide hidden range.  fp32 records
+// take the down phase in half blocks: a step of 32 records keeps the stage at
+// 48 KB (16 KB of activations, 32 KB of down rows in eight [32 x 32] boxes).
+template <int kFmt>
+struct Fmt {
+  static constexpr int kEs = kFmt == kFmtTF32 ? 4 : 2;
+  static constexpr int kRow = kRowBytes / kEs;            // 64 or 32
+  static constexpr int kStepsPerBlock = kBlock / kRow;    // down steps per block: 1 or 2
+  static constexpr int kDownBoxes = kHRange / kRow;       // 4 or 8
+  static constexpr uint32_t kDownBox = kRow * kRowBytes;  // bytes of one down box: 8 KB or 4 KB
+  static constexpr int kMmaK = 32 / kEs;                  // elements per MMA K step (32 bytes)
+};
 
 template <bool kBf16>
 __device__ __forceinline__ uint32_t pack2(float a, float b) {
@@ -335,7 +350,8 @@ __device__ bool range_of(int i, int g, Bound bound, Ranges* r, int ph) {
 
 __global__ void __launch_bounds__(kPlanThreads)
     prefill_plan_kernel(const int32_t* __restrict__ tile_blocks, const int32_t* __restrict__ tile_offsets,
-                        int n_tiles, int n_blocks, int n_chunks, int n_hranges, int grid, int32_t* __restrict__ header,
+                        int n_tiles, int n_blocks, int n_chunks, int n_hranges, int steps_per_block, int grid,
+                        int32_t* __restrict__ header,
                         int32_t* __restrict__ units, int32_t* __restrict__ unit_prefix,
                         int32_t* __restrict__ tile_list, int32_t* __restrict__ seq_global,
                         uint32_t* __restrict__ block_masks, Ranges* __restrict__ ranges) {
@@ -543,7 +559,7 @@ __global__ void __launch_bounds__(kPlanThreads)
       tot += s_tile_count[t];
       if (t < part) pre += s_tile_count[t];
     }
-    s_down[v] = (v / n_tiles) * tot + pre;
+    s_down[v] = ((v / n_tiles) * tot + pre) * steps_per_block;
   }
   __syncthreads();
   // Ranges of every CTA of the prefill grid.
@@ -554,7 +570,7 @@ __global__ void __launch_bounds__(kPlanThreads)
   const int n_down = n_hranges * n_tiles;
   const int total2 = s_down[n_down];
   int max_steps = 0;
-  for (int t = 0; t < n_tiles; ++t) max_steps = max(max_steps, s_tile_count[t]);
+  for (int t = 0; t < n_tiles; ++t) max_steps = max(max_steps, s_tile_count[t] * steps_per_block);
   const int g2 = effective_ranges(total2, max_steps, grid);
   // Every range boundary once, in parallel (phase 1 on threads 0..g1, phase 2
   // on threads kPlanThreads/2..): the per-CTA pass below only reads them.
@@ -593,9 +609,12 @@ __global__ void __launch_bounds__(kPlanThreads)
 
 // idx-th unit of a CTA's range in processing order, or -1 past the end: a
 // first segment that continues another CTA's unit goes first (it hands over
-// partial sums), then an unfinished last segment (this CTA completes that
-// unit once the partial sums of the CTAs running its later steps are in),
-// then the units in between.
+// partial sums), then the units in between, then an unfinished last segment
+// (this CTA completes that unit with the partial sums of the CTAs running its
+// later steps, which those CTAs produce first, so they are in by then).
+// Taking the last segment second instead left its epilogue waiting on the
+// partials for the whole of the middle units, and those ran ~40 % slower
+// per step meanwhile.
 __device__ __forceinline__ int seg_unit(const Ranges& r, int ph, int idx, int n_units) {
   const int lo_u = r.lo_u[ph], lo_k = r.lo_k[ph], hi_u = r.hi_u[ph], hi_k = r.hi_k[ph];
   const bool c = lo_k > 0 && lo_u < n_units;
@@ -604,14 +623,11 @@ __device__ __forceinline__ int seg_unit(const Ranges& r, int ph, int idx, int n_
     if (idx == 0) return lo_u;
     --idx;
   }
-  if (h) {
-    if (idx == 0) return hi_u;
-    --idx;
-  }
   const int mid_lo = c ? lo_u + 1 : lo_u;
   const int mid_hi = min(h ? hi_u : hi_u + 1, n_units);
-  const int u = mid_lo + idx;
-  return u < mid_hi ? u : -1;
+  if (idx < mid_hi - mid_lo) return mid_lo + idx;
+  idx -= max(mid_hi - mid_lo, 0);
+  return h && idx == 0 ? hi_u : -1;
 }
 
 // Segment [ks, ke) of unit u inside [lo, hi); returns false if empty.
@@ -625,10 +641,13 @@ __device__ __forceinline__ bool segment(int u, int lo_u, int lo_k, int hi_u, int
 // The prefill kernel.
 // ---------------------------------------------------------------------------
 
-template <bool kBf16>
+template <int kFmt>
 __global__ void __launch_bounds__(kThreads, 1)
-    prefill_kernel(const __grid_constant__ CUtensorMap tm_records, const __grid_constant__ CUtensorMap tm_x,
-                   const __grid_constant__ CUtensorMap tm_abuf, const PrefillArgs a) {
+    prefill_kernel(const __grid_constant__ CUtensorMap tm_records, const __grid_constant__ CUtensorMap tm_down,
+                   const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_abuf,
+                   const PrefillArgs a) {
+  using F = Fmt<kFmt>;
+  constexpr bool kBf16 = kFmt == kFmtBF16;
   // Launched as a programmatic dependent of the plan kernel: the grid may be
   // scheduled while the plan runs, and waits here for it to complete.
   asm volatile("griddepcontrol.wait;" ::: "memory");
@@ -642,7 +661,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
-      mbar_init(&ctl->full[s], kLoaders);  // each loading thread arrives with its bytes
+      mbar_init(&ctl->full[s], 1);  // the iteration's producer arrives with its bytes
       mbar_init(&ctl->empty[s], 1);
     }
     for (int j = 0; j < 2; ++j) {
@@ -678,10 +697,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int si = 0, v; (v = seg_unit(ctl->r, 1, si, n_down)) >= 0; ++si) {
       const int t = v % a.n_tiles;
       int ks, ke;
-      if (!segment(v, ctl->r.lo_u[1], ctl->r.lo_k[1], ctl->r.hi_u[1], ctl->r.hi_k[1], a.header[kHdrTileCount + t], &ks, &ke))
+      if (!segment(v, ctl->r.lo_u[1], ctl->r.lo_k[1], ctl->r.hi_u[1], ctl->r.hi_k[1], a.header[kHdrTileCount + t] * F::kStepsPerBlock, &ks, &ke))
         continue;
       for (int j = ks + lane; j < ke; j += 32)
-        if (n + (j - ks) < kSmemList) ctl->steps[n + (j - ks)] = (v << 16) | a.tile_list[t * a.n_blocks + j];
+        if (n + (j - ks) < kSmemList)
+          ctl->steps[n + (j - ks)] = (v << 16) | a.tile_list[t * a.n_blocks + j / F::kStepsPerBlock];
       n += ke - ks;
     }
     __syncwarp();
@@ -696,89 +716,48 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint32_t ut = 0;  // MMA / TMEM readers: accumulator buffers used
 
   // ------------------------------ phase 1 ------------------------------
-  if (warp == 0) {
-    // Weight loader: lane 0 issues the gate/up boxes.  (Prefetching later
-    // weight boxes into L2, by TMA or by the other lanes, measured slower: the
-    // loads are not waiting on DRAM.)
-    if (lane == 0) tma_prefetch_map(&tm_records);
-    // Rows of a block that several tiles use stay in L2 for the other tiles'
-    // units (which run on other CTAs, up to a unit's time apart); rows of a
-    // block that one tile uses are read once.
+  const int producer = warp == kProducerWarp[0] ? 0 : warp == kProducerWarp[1] ? 1 : warp == kProducerWarp[2] ? 2 : -1;
+  if (producer >= 0 && lane == 0) {
+    // x box of the unit's tile (A) and the gate and up rows of its one or two
+    // blocks (B).  Rows of a block that several tiles use stay in L2 for the
+    // other tiles' units (which run on neighbouring CTAs); rows of a block
+    // that one tile uses are read once.
+    if (producer == 0) {
+      tma_prefetch_map(&tm_records);
+      tma_prefetch_map(&tm_down);
+      tma_prefetch_map(&tm_x);
+      tma_prefetch_map(&tm_abuf);
+    }
     const uint64_t keep = policy_evict_last(), stream = policy_evict_first();
-    bool stop = false;
-    for (int si = 0, u; !stop && (u = seg_unit(ctl->r, 0, si, n_units)) >= 0; ++si) {
+    for (int si = 0, u; (u = seg_unit(ctl->r, 0, si, n_units)) >= 0 && !*abort_flag; ++si) {
       int ks, ke;
       if (!segment(u, ctl->r.lo_u[0], ctl->r.lo_k[0], ctl->r.hi_u[0], ctl->r.hi_k[0], a.n_chunks, &ks, &ke)) continue;
       const int unit = a.units[u];
+      const int t = unit_tile(unit);
       const int nb = unit_blocks(unit);
+      const int b1 = unit_block(unit, 0), b2 = nb == 2 ? unit_block(unit, 1) : b1;
+      const uint64_t pol1 = __popc(a.block_masks[b1]) > 1 ? keep : stream;
+      const uint64_t pol2 = __popc(a.block_masks[b2]) > 1 ? keep : stream;
       for (int kc = ks; kc < ke; ++kc, ++it) {
-        int ok = 1;
-        if (lane == 0) {
-          const int s = it % kStages;
-          ok = wait_phase(&ctl->empty[s], ((it / kStages) & 1u) ^ 1u, abort_flag, status) ? 1 : 0;
-          if (ok) {
-            // B operand: gate and up rows of the unit's first block (128 rows);
-            // warp kWeightWarp2 loads the second block of a pair.
-            uint8_t* st = smem + s * kStageBytes + kBox128;
-            mbar_arrive_expect_tx(&ctl->full[s], kBox128);
-            const int b = unit_block(unit, 0);
-            const uint64_t pol = __popc(a.block_masks[b]) > 1 ? keep : stream;
-            tma_load_3d_hint(st, &tm_records, kc * kChunk, 0, b * kBlock, &ctl->full[s], pol);
-            tma_load_3d_hint(st + kBox64, &tm_records, kc * kChunk, 1, b * kBlock, &ctl->full[s], pol);
-          }
-        }
-        if (!__shfl_sync(0xffffffffu, ok, 0)) {
-          stop = true;
-          break;
-        }
-      }
-    }
-  } else if (warp == kWeightWarp2 && lane == 0) {
-    // Second weight loader: the gate and up rows of a pair's second block;
-    // for a single-block unit it only arrives.
-    const uint64_t keep = policy_evict_last(), stream = policy_evict_first();
-    for (int si = 0, u; (u = seg_unit(ctl->r, 0, si, n_units)) >= 0 && !*abort_flag; ++si) {
-      int ks, ke;
-      if (!segment(u, ctl->r.lo_u[0], ctl->r.lo_k[0], ctl->r.hi_u[0], ctl->r.hi_k[0], a.n_chunks, &ks, &ke)) continue;
-      const int unit = a.units[u];
-      const bool pair = unit_blocks(unit) == 2;
-      const int b = pair ? unit_block(unit, 1) : 0;
-      const uint64_t pol = __popc(a.block_masks[b]) > 1 ? keep : stream;
-      for (int kc = ks; kc < ke; ++kc, ++it) {
-        const int s = it % kStages;
-        if (!wait_phase(&ctl->empty[s], ((it / kStages) & 1u) ^ 1u, abort_flag, status)) break;
-        if (pair) {
-          uint8_t* st = smem + s * kStageBytes + 2 * kBox128;
-          mbar_arrive_expect_tx(&ctl->full[s], kBox128);
-          tma_load_3d_hint(st, &tm_records, kc * kChunk, 0, b * kBlock, &ctl->full[s], pol);
-          tma_load_3d_hint(st + kBox64, &tm_records, kc * kChunk, 1, b * kBlock, &ctl->full[s], pol);
-        } else {
-          mbar_arrive(&ctl->full[s]);
-        }
-      }
-    }
-  } else if (warp == kActWarp && lane == 0) {
-    // Activation loader: the x box of the unit's tile (A operand).
-    tma_prefetch_map(&tm_x);
-    tma_prefetch_map(&tm_abuf);
-    const uint64_t keep = policy_evict_last();  // every unit of the tile reads its x
-    for (int si = 0, u; (u = seg_unit(ctl->r, 0, si, n_units)) >= 0 && !*abort_flag; ++si) {
-      int ks, ke;
-      if (!segment(u, ctl->r.lo_u[0], ctl->r.lo_k[0], ctl->r.hi_u[0], ctl->r.hi_k[0], a.n_chunks, &ks, &ke)) continue;
-      const int t = unit_tile(a.units[u]);
-      for (int kc = ks; kc < ke; ++kc, ++it) {
+        if (static_cast<int>(it % kProducers) != producer) continue;
         const int s = it % kStages;
         if (!wait_phase(&ctl->empty[s], ((it / kStages) & 1u) ^ 1u, abort_flag, status)) break;
         uint8_t* st = smem + s * kStageBytes;
-        mbar_arrive_expect_tx(&ctl->full[s], kBox128);
-        tma_load_2d_hint(st, &tm_x, kc * kChunk, t * kTile, &ctl->full[s], keep);
+        mbar_arrive_expect_tx(&ctl->full[s], (1 + nb) * kBox128);
+        tma_load_2d_hint(st, &tm_x, kc * F::kRow, t * kTile, &ctl->full[s], keep);
+        tma_load_3d_hint(st + kBox128, &tm_records, kc * F::kRow, 0, b1 * kBlock, &ctl->full[s], pol1);
+        tma_load_3d_hint(st + kBox128 + kBox64, &tm_records, kc * F::kRow, 1, b1 * kBlock, &ctl->full[s], pol1);
+        if (nb == 2) {
+          tma_load_3d_hint(st + 2 * kBox128, &tm_records, kc * F::kRow, 0, b2 * kBlock, &ctl->full[s], pol2);
+          tma_load_3d_hint(st + 2 * kBox128 + kBox64, &tm_records, kc * F::kRow, 1, b2 * kBlock, &ctl->full[s], pol2);
+        }
       }
     }
   } else if (warp == 1 && lane == 0) {
-    // One MMA per 16-wide K step: M = 128 tokens, N = 128 per block (256 for a
-    // block pair -- the instruction rate, not the width, bounds tcgen05 here).
-    constexpr uint32_t idesc1 = idesc_f16_f32(128, 128, kBf16, false, false);
-    constexpr uint32_t idesc2 = idesc_f16_f32(128, 256, kBf16, false, false);
+    // One MMA per 32-byte K step: M = 128 tokens, N = 128 per block (256 for a
+    // block pair).
+    constexpr uint32_t idesc1 = idesc_f32acc(128, 128, kFmt, false, false);
+    constexpr uint32_t idesc2 = idesc_f32acc(128, 256, kFmt, false, false);
     for (int si = 0, u; (u = seg_unit(ctl->r, 0, si, n_units)) >= 0 && !*abort_flag; ++si) {
       int ks, ke;
       if (!segment(u, ctl->r.lo_u[0], ctl->r.lo_k[0], ctl->r.hi_u[0], ctl->r.hi_k[0], a.n_chunks, &ks, &ke)) continue;
@@ -799,8 +778,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint64_t a_desc = smem_desc_sw128(st, 16, 1024);            // x tile, K-major
         const uint64_t b_desc = smem_desc_sw128(st + kBox128, 16, 1024);  // gate/up rows, K-major
 #pragma unroll
-        for (int kk = 0; kk < kChunk / 16; ++kk)
-          tc_mma_f16(d0, a_desc + 2u * kk, b_desc + 2u * kk, idesc, (kc > ks || kk > 0) ? 1u : 0u);
+        for (int kk = 0; kk < kRowBytes / 32; ++kk) {
+          if constexpr (kFmt == kFmtTF32)
+            tc_mma_tf32(d0, a_desc + 2u * kk, b_desc + 2u * kk, idesc, (kc > ks || kk > 0) ? 1u : 0u);
+          else
+            tc_mma_f16(d0, a_desc + 2u * kk, b_desc + 2u * kk, idesc, (kc > ks || kk > 0) ? 1u : 0u);
+        }
         tc_commit(&ctl->empty[s]);
       }
       if (!ok) break;
@@ -846,7 +829,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           warp_wait_flags(a.flags1, ctl->r.contrib[0], ctl->r.n_contrib[0], epoch, abort_flag, status);
         for (int i = 0; i < nt; ++i) {
           const int b = unit_block(unit, i);
-          uint16_t* dst = a.abuf + static_cast<int64_t>(t * kTile + row) * a.ld_abuf + static_cast<int64_t>(b) * kBlock;
+          const int64_t dst_off = static_cast<int64_t>(t * kTile + row) * a.ld_abuf + static_cast<int64_t>(b) * kBlock;
 #pragma unroll 1
           for (int c = 0; c < 2; ++c) {
             float g[32], v[32];
@@ -886,13 +869,21 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
               }
             }
-            uint32_t w[16];
+            if constexpr (kFmt == kFmtTF32) {
+              float4* d4 = reinterpret_cast<float4*>(static_cast<float*>(a.abuf) + dst_off + c * 32);
 #pragma unroll
-            for (int e = 0; e < 16; ++e)
-              w[e] = pack2<kBf16>(silu(g[2 * e]) * v[2 * e], silu(g[2 * e + 1]) * v[2 * e + 1]);
-            uint4* d4 = reinterpret_cast<uint4*>(dst + c * 32);
+              for (int e = 0; e < 8; ++e)
+                d4[e] = make_float4(silu(g[4 * e]) * v[4 * e], silu(g[4 * e + 1]) * v[4 * e + 1],
+                                    silu(g[4 * e + 2]) * v[4 * e + 2], silu(g[4 * e + 3]) * v[4 * e + 3]);
+            } else {
+              uint32_t w[16];
 #pragma unroll
-            for (int e = 0; e < 4; ++e) d4[e] = make_uint4(w[4 * e], w[4 * e + 1], w[4 * e + 2], w[4 * e + 3]);
+              for (int e = 0; e < 16; ++e)
+                w[e] = pack2<kBf16>(silu(g[2 * e]) * v[2 * e], silu(g[2 * e + 1]) * v[2 * e + 1]);
+              uint4* d4 = reinterpret_cast<uint4*>(static_cast<uint16_t*>(a.abuf) + dst_off + c * 32);
+#pragma unroll
+              for (int e = 0; e < 4; ++e) d4[e] = make_uint4(w[4 * e], w[4 * e + 1], w[4 * e + 2], w[4 * e + 3]);
+            }
           }
         }
       }
@@ -924,87 +915,42 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   // ------------------------------ phase 2 ------------------------------
   const int staged = min(ctl->n_steps, kSmemList);
-  if (warp == 0) {
-    // Down rows of a block that several tiles use are read by each of their
-    // units of the same hidden range: kept in L2, as in phase 1.
+  if (producer >= 0 && lane == 0) {
+    // The tile's activations of the step's records (A) and their down rows
+    // for the unit's 256 hidden outputs (B).  Down rows of a block that
+    // several tiles use are read by each of their units of the same hidden
+    // range: kept in L2, as in phase 1.
     const uint64_t keep = policy_evict_last(), stream = policy_evict_first();
-    bool stop = false;
     int si = 0;  // position in this CTA's step sequence
-    for (int sv = 0, v; !stop && (v = seg_unit(ctl->r, 1, sv, n_down)) >= 0; ++sv) {
-      const int t = v % a.n_tiles, r = v / a.n_tiles;
-      int ks, ke;
-      if (!segment(v, ctl->r.lo_u[1], ctl->r.lo_k[1], ctl->r.hi_u[1], ctl->r.hi_k[1], a.header[kHdrTileCount + t], &ks,
-                   &ke))
-        continue;
-      for (int step = ks; step < ke; ++step, ++it, ++si) {
-        int ok = 1;
-        if (lane == 0) {
-          const int b = si < staged ? (ctl->steps[si] & 0xFFFF) : a.tile_list[t * a.n_blocks + step];
-          const int s = it % kStages;
-          ok = wait_phase(&ctl->empty[s], ((it / kStages) & 1u) ^ 1u, abort_flag, status) ? 1 : 0;
-          if (ok) {
-            // Down rows, hidden columns [r*256, r*256 + 128); warp kWeightWarp2
-            // loads the other 128.
-            uint8_t* st = smem + s * kStageBytes;
-            mbar_arrive_expect_tx(&ctl->full[s], 2 * kBox64);
-            const uint64_t pol = __popc(a.block_masks[b]) > 1 ? keep : stream;
-            for (int qq = 0; qq < 2; ++qq)
-              tma_load_3d_hint(st + kBox128 + qq * kBox64, &tm_records, r * kHRange + qq * 64, 2, b * kBlock,
-                               &ctl->full[s], pol);
-          }
-        }
-        if (!__shfl_sync(0xffffffffu, ok, 0)) {
-          stop = true;
-          break;
-        }
-      }
-    }
-    if (lane == 0) drain_loads(ctl, it);
-  } else if (warp == kWeightWarp2 && lane == 0) {
-    const uint64_t keep = policy_evict_last(), stream = policy_evict_first();
-    int si = 0;
     for (int sv = 0, v; (v = seg_unit(ctl->r, 1, sv, n_down)) >= 0 && !*abort_flag; ++sv) {
       const int t = v % a.n_tiles, r = v / a.n_tiles;
       int ks, ke;
-      if (!segment(v, ctl->r.lo_u[1], ctl->r.lo_k[1], ctl->r.hi_u[1], ctl->r.hi_k[1], a.header[kHdrTileCount + t], &ks,
-                   &ke))
+      if (!segment(v, ctl->r.lo_u[1], ctl->r.lo_k[1], ctl->r.hi_u[1], ctl->r.hi_k[1],
+                   a.header[kHdrTileCount + t] * F::kStepsPerBlock, &ks, &ke))
         continue;
       for (int step = ks; step < ke; ++step, ++it, ++si) {
-        const int b = si < staged ? (ctl->steps[si] & 0xFFFF) : a.tile_list[t * a.n_blocks + step];
+        if (static_cast<int>(it % kProducers) != producer) continue;
+        const int b = si < staged ? (ctl->steps[si] & 0xFFFF) : a.tile_list[t * a.n_blocks + step / F::kStepsPerBlock];
+        const int r0 = b * kBlock + (step % F::kStepsPerBlock) * F::kRow;  // first record of the step
         const int s = it % kStages;
         if (!wait_phase(&ctl->empty[s], ((it / kStages) & 1u) ^ 1u, abort_flag, status)) break;
         uint8_t* st = smem + s * kStageBytes;
-        mbar_arrive_expect_tx(&ctl->full[s], 2 * kBox64);
+        mbar_arrive_expect_tx(&ctl->full[s], kBox128 + F::kDownBoxes * F::kDownBox);
+        tma_load_2d_hint(st, &tm_abuf, r0, t * kTile, &ctl->full[s], keep);
         const uint64_t pol = __popc(a.block_masks[b]) > 1 ? keep : stream;
-        for (int qq = 2; qq < 4; ++qq)
-          tma_load_3d_hint(st + kBox128 + qq * kBox64, &tm_records, r * kHRange + qq * 64, 2, b * kBlock,
-                           &ctl->full[s], pol);
+        for (int qq = 0; qq < F::kDownBoxes; ++qq)
+          tma_load_3d_hint(st + kBox128 + qq * F::kDownBox, &tm_down, r * kHRange + qq * F::kRow, 2, r0, &ctl->full[s],
+                           pol);
       }
     }
-  } else if (warp == kActWarp && lane == 0) {
-    const uint64_t keep = policy_evict_last();  // each activation box is read once per hidden range
-    int si = 0;
-    for (int sv = 0, v; (v = seg_unit(ctl->r, 1, sv, n_down)) >= 0 && !*abort_flag; ++sv) {
-      const int t = v % a.n_tiles;
-      int ks, ke;
-      if (!segment(v, ctl->r.lo_u[1], ctl->r.lo_k[1], ctl->r.hi_u[1], ctl->r.hi_k[1], a.header[kHdrTileCount + t], &ks,
-                   &ke))
-        continue;
-      for (int step = ks; step < ke; ++step, ++it, ++si) {
-        const int b = si < staged ? (ctl->steps[si] & 0xFFFF) : a.tile_list[t * a.n_blocks + step];
-        const int s = it % kStages;
-        if (!wait_phase(&ctl->empty[s], ((it / kStages) & 1u) ^ 1u, abort_flag, status)) break;
-        uint8_t* st = smem + s * kStageBytes;
-        mbar_arrive_expect_tx(&ctl->full[s], kBox128);
-        tma_load_2d_hint(st, &tm_abuf, b * kBlock, t * kTile, &ctl->full[s], keep);
-      }
-    }
+    // Every copy of the last iterations has landed before the CTA exits.
+    if (producer == 0) drain_loads(ctl, it);
   } else if (warp == 1 && lane == 0) {
-    constexpr uint32_t idesc = idesc_f16_f32(128, 256, kBf16, false, true);
+    constexpr uint32_t idesc = idesc_f32acc(128, 256, kFmt, false, true);
     for (int sv = 0, v; (v = seg_unit(ctl->r, 1, sv, n_down)) >= 0 && !*abort_flag; ++sv) {
       const int t = v % a.n_tiles;
       int ks, ke;
-      if (!segment(v, ctl->r.lo_u[1], ctl->r.lo_k[1], ctl->r.hi_u[1], ctl->r.hi_k[1], a.header[kHdrTileCount + t], &ks, &ke))
+      if (!segment(v, ctl->r.lo_u[1], ctl->r.lo_k[1], ctl->r.hi_u[1], ctl->r.hi_k[1], a.header[kHdrTileCount + t] * F::kStepsPerBlock, &ks, &ke))
         continue;
       const uint32_t j = ut & 1u;
       if (!wait_phase(&ctl->acc_empty[j], ((ut >> 1) & 1u) ^ 1u, abort_flag, status)) break;
@@ -1020,10 +966,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after_sync();
         const uint32_t st = smem_addr(smem + s * kStageBytes);
         const uint64_t a_desc = smem_desc_sw128(st, 16, 1024);          // activations, K-major
-        const uint64_t b_desc = smem_desc_sw128(st + kBox128, kBox64, 1024);  // down rows, hidden-major
+        // Down rows, hidden-major (MN-major B): fp32 rows take the 32-byte-atom swizzle.
+        const uint64_t b_desc = kFmt == kFmtTF32 ? smem_desc_sw128_atom32(st + kBox128, F::kDownBox, 512)
+                                                 : smem_desc_sw128(st + kBox128, F::kDownBox, 1024);
+        constexpr uint32_t kBStep = F::kMmaK * kRowBytes / 16;  // K rows of one MMA, in descriptor units
 #pragma unroll
-        for (int kk = 0; kk < kBlock / 16; ++kk)
-          tc_mma_f16(d0, a_desc + 2u * kk, b_desc + 128u * kk, idesc, (step > ks || kk > 0) ? 1u : 0u);
+        for (int kk = 0; kk < kRowBytes / 32; ++kk) {
+          if constexpr (kFmt == kFmtTF32)
+            tc_mma_tf32(d0, a_desc + 2u * kk, b_desc + kBStep * kk, idesc, (step > ks || kk > 0) ? 1u : 0u);
+          else
+            tc_mma_f16(d0, a_desc + 2u * kk, b_desc + kBStep * kk, idesc, (step > ks || kk > 0) ? 1u : 0u);
+        }
         tc_commit(&ctl->empty[s]);
       }
       if (!ok) break;
@@ -1038,7 +991,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int sv = 0, v; (v = seg_unit(ctl->r, 1, sv, n_down)) >= 0; ++sv) {
       const int t = v % a.n_tiles, r = v / a.n_tiles;
       int ks, ke;
-      const int steps = a.header[kHdrTileCount + t];
+      const int steps = a.header[kHdrTileCount + t] * F::kStepsPerBlock;
       if (!segment(v, ctl->r.lo_u[1], ctl->r.lo_k[1], ctl->r.hi_u[1], ctl->r.hi_k[1], steps, &ks, &ke)) continue;
       const uint32_t j = ut & 1u;
       if (!warp_wait_phase(&ctl->acc_full[j], (ut >> 1) & 1u, abort_flag, status)) break;
@@ -1112,7 +1065,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // Tiles without blocks: their rows are zero.  Spread over the grid by (tile, range).
     for (int v = blockIdx.x; v < n_down; v += gridDim.x) {
       const int t = v % a.n_tiles, r = v / a.n_tiles;
-      if (a.header[kHdrTileCount + t] != 0) continue;
+      if (a.header[kHdrTileCount + t] * F::kStepsPerBlock != 0) continue;
       const int tok = t * kTile + row;
       if (tok >= a.n_tokens) continue;
       for (int h = r * kHRange; h < min(a.hidden, (r + 1) * kHRange); ++h)
@@ -1152,15 +1105,18 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_tiled() {
   return fn;
 }
 
-// 16-bit tensor map with the 128-byte swizzle; dims / strides innermost first.
+// Tensor map (bf16, fp16 or fp32) with the 128-byte swizzle; dims / strides innermost first.
 bool make_map(CUtensorMap* map, int dtype, int rank, const void* base, const uint64_t* dims, const uint64_t* strides,
-              const uint32_t* box) {
+              const uint32_t* box, CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B) {
   auto fn = encode_tiled();
   if (fn == nullptr) return false;
   const uint32_t elem[3] = {1, 1, 1};
-  const CUresult r = fn(map, dtype == QCC_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+  const CUtensorMapDataType type = dtype == QCC_DTYPE_BF16   ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                   : dtype == QCC_DTYPE_F16  ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                                             : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+  const CUresult r = fn(map, type,
                         rank, const_cast<void*>(base), dims, strides, box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }
@@ -1197,7 +1153,7 @@ PrefillLayout prefill_layout(int64_t n_records, int num_sms) {
   l.flags2 = off;
   off = round_up(off + static_cast<size_t>(l.grid) * 4, 1024);
   l.abuf = off;
-  off = round_up(off + static_cast<size_t>(kGroupTokens) * l.npad * 2, 1024);
+  off = round_up(off + static_cast<size_t>(kGroupTokens) * l.npad * 4, 1024);  // fp32 activations at most
   l.partials = off;
   off += static_cast<size_t>(l.grid) * kSlotFloats * 4;
   l.total = round_up(off, 256);
@@ -1223,7 +1179,7 @@ extern "C" int qcc_indexed_ffn_prefill(const void* x, int64_t ldx, int n_tokens,
                                        const int32_t* tile_offsets, void* workspace, size_t workspace_bytes, void* y,
                                        int64_t ldy, int y_dtype, cudaStream_t stream) {
   using namespace qcc;
-  if (dtype != QCC_DTYPE_BF16 && dtype != QCC_DTYPE_F16) return valid_dtype(dtype) ? QCC_ERR_UNSUPPORTED : QCC_ERR_DTYPE;
+  if (dtype != QCC_DTYPE_BF16 && dtype != QCC_DTYPE_F16 && dtype != QCC_DTYPE_F32) return QCC_ERR_DTYPE;
   if (!valid_dtype(y_dtype)) return QCC_ERR_DTYPE;
   if (n_tokens < 0 || hidden <= 0 || n_records <= 0 || ldx < hidden || ldy < hidden) return QCC_ERR_SHAPE;
   if (n_records > static_cast<int64_t>(kMaxBlocks) * kBlock) return QCC_ERR_UNSUPPORTED;
@@ -1233,7 +1189,9 @@ extern "C" int qcc_indexed_ffn_prefill(const void* x, int64_t ldx, int n_tokens,
       y == nullptr)
     return QCC_ERR_INVALID_ARGUMENT;
   // TMA: 16-byte aligned bases and row strides.
-  if (!aligned16(x) || !aligned16(packed) || !aligned16(workspace) || (ldx * 2) % 16 != 0) return QCC_ERR_ALIGNMENT;
+  const int es = dtype_bytes(dtype);
+  const int row_elems = kRowBytes / es;  // elements of a 128-byte row: the boxes' inner extent
+  if (!aligned16(x) || !aligned16(packed) || !aligned16(workspace) || (ldx * es) % 16 != 0) return QCC_ERR_ALIGNMENT;
   int device = 0;
   if (!cuda_ok(cudaGetDevice(&device))) return QCC_ERR_CUDA;
   const DeviceInfo& info = device_info(device);
@@ -1251,10 +1209,10 @@ extern "C" int qcc_indexed_ffn_prefill(const void* x, int64_t ldx, int n_tokens,
   args.block_masks = ws + l.masks;
   args.ranges = reinterpret_cast<const Ranges*>(ws + l.ranges);
   args.n_blocks = l.n_blocks;
-  args.n_chunks = (hidden + kChunk - 1) / kChunk;
+  args.n_chunks = (hidden + row_elems - 1) / row_elems;
   args.n_hranges = (hidden + kHRange - 1) / kHRange;
   args.hidden = hidden;
-  args.abuf = reinterpret_cast<uint16_t*>(ws + l.abuf);
+  args.abuf = ws + l.abuf;
   args.ld_abuf = l.npad;
   args.partials = reinterpret_cast<float*>(ws + l.partials);
   args.flags1 = reinterpret_cast<int32_t*>(ws + l.flags1);
@@ -1264,22 +1222,30 @@ extern "C" int qcc_indexed_ffn_prefill(const void* x, int64_t ldx, int n_tokens,
   const size_t y_es = static_cast<size_t>(dtype_bytes(y_dtype));
   args.y_vec = aligned16(y) && (static_cast<size_t>(ldy) * y_es) % 16 == 0;
 
-  // Records as a 3-D tensor {hidden_pad, segment (gate, up, down), record}.
-  CUtensorMap tm_records, tm_abuf;
+  // Records as a 3-D tensor {hidden_pad, segment (gate, up, down), record}:
+  // gate/up boxes of 64 records, down boxes of one down step's records (read
+  // MN-major by the MMA: fp32 ones with the 32-byte-atom swizzle that
+  // kind::tf32 requires for an MN-major operand).
+  CUtensorMap tm_records, tm_down, tm_abuf;
   {
     const uint64_t dims[3] = {static_cast<uint64_t>(hp), 3, static_cast<uint64_t>(n_records)};
-    const uint64_t strides[2] = {static_cast<uint64_t>(hp) * 2, static_cast<uint64_t>(hp) * 6};
-    const uint32_t box[3] = {64, 1, 64};
-    if (!make_map(&tm_records, dtype, 3, packed, dims, strides, box)) return QCC_ERR_UNSUPPORTED;
+    const uint64_t strides[2] = {static_cast<uint64_t>(hp) * es, static_cast<uint64_t>(hp) * 3 * es};
+    const uint32_t box[3] = {static_cast<uint32_t>(row_elems), 1, 64};
+    const uint32_t down_box[3] = {static_cast<uint32_t>(row_elems), 1, static_cast<uint32_t>(row_elems)};
+    if (!make_map(&tm_records, dtype, 3, packed, dims, strides, box) ||
+        !make_map(&tm_down, dtype, 3, packed, dims, strides, down_box,
+                  dtype == QCC_DTYPE_F32 ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B))
+      return QCC_ERR_UNSUPPORTED;
   }
   {
     const uint64_t dims[2] = {static_cast<uint64_t>(l.npad), static_cast<uint64_t>(kGroupTokens)};
-    const uint64_t strides[1] = {static_cast<uint64_t>(l.npad) * 2};
-    const uint32_t box[2] = {64, 128};
+    const uint64_t strides[1] = {static_cast<uint64_t>(l.npad) * es};
+    const uint32_t box[2] = {static_cast<uint32_t>(row_elems), 128};
     if (!make_map(&tm_abuf, dtype, 2, args.abuf, dims, strides, box)) return QCC_ERR_UNSUPPORTED;
   }
-  const void* kernel = dtype == QCC_DTYPE_BF16 ? reinterpret_cast<const void*>(prefill_kernel<true>)
-                                               : reinterpret_cast<const void*>(prefill_kernel<false>);
+  const void* kernel = dtype == QCC_DTYPE_BF16  ? reinterpret_cast<const void*>(prefill_kernel<kFmtBF16>)
+                       : dtype == QCC_DTYPE_F16 ? reinterpret_cast<const void*>(prefill_kernel<kFmtF16>)
+                                                : reinterpret_cast<const void*>(prefill_kernel<kFmtTF32>);
   if (!ensure_max_dynamic_smem(reinterpret_cast<const void*>(prefill_plan_kernel), device) ||
       !ensure_max_dynamic_smem(kernel, device))
     return QCC_ERR_CUDA;
@@ -1299,13 +1265,14 @@ extern "C" int qcc_indexed_ffn_prefill(const void* x, int64_t ldx, int n_tokens,
     CUtensorMap tm_x;
     {
       const uint64_t dims[2] = {static_cast<uint64_t>(hidden), static_cast<uint64_t>(rows)};
-      const uint64_t strides[1] = {static_cast<uint64_t>(ldx) * 2};
-      const uint32_t box[2] = {64, 128};
-      if (!make_map(&tm_x, dtype, 2, xb + static_cast<size_t>(g0) * ldx * 2, dims, strides, box))
+      const uint64_t strides[1] = {static_cast<uint64_t>(ldx) * es};
+      const uint32_t box[2] = {static_cast<uint32_t>(row_elems), 128};
+      if (!make_map(&tm_x, dtype, 2, xb + static_cast<size_t>(g0) * ldx * es, dims, strides, box))
         return QCC_ERR_UNSUPPORTED;
     }
     prefill_plan_kernel<<<1, kPlanThreads, plan_smem, stream>>>(
-        tile_blocks, tile_offsets + g0 / kTile, args.n_tiles, l.n_blocks, args.n_chunks, args.n_hranges, l.grid,
+        tile_blocks, tile_offsets + g0 / kTile, args.n_tiles, l.n_blocks, args.n_chunks, args.n_hranges,
+        kBlock / row_elems, l.grid,
         args.header, const_cast<int32_t*>(args.units), const_cast<int32_t*>(args.unit_prefix),
         const_cast<int32_t*>(args.tile_list), reinterpret_cast<int32_t*>(ws + l.seq),
         reinterpret_cast<uint32_t*>(ws + l.masks), const_cast<Ranges*>(args.ranges));
@@ -1325,7 +1292,7 @@ extern "C" int qcc_indexed_ffn_prefill(const void* x, int64_t ldx, int n_tokens,
     attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 2;
-    void* kargs[] = {&tm_records, &tm_x, &tm_abuf, &args};
+    void* kargs[] = {&tm_records, &tm_down, &tm_x, &tm_abuf, &args};
     if (!cuda_ok(cudaLaunchKernelExC(&cfg, kernel, kargs))) return QCC_ERR_CUDA;
   }
   return QCC_OK;

@@ -1,10 +1,10 @@
 // Tensor-core (tcgen05 / TMEM) and tiled-TMA helpers for sm_100a kernels.
 //
 // Conventions used by the kernels of this library:
-// * operands are 16-bit (bf16 or fp16), staged in shared memory by tiled TMA
-//   loads with the 128-byte swizzle: a box row is 64 elements = 128 bytes and
-//   rows come in 1024-byte groups of eight; every operand tile starts on a
-//   1024-byte boundary;
+// * operands are bf16 / fp16 (kind::f16) or fp32 (kind::tf32), staged in
+//   shared memory by tiled TMA loads with the 128-byte swizzle: a box row is
+//   128 bytes (64 16-bit or 32 fp32 elements) and rows come in 1024-byte
+//   groups of eight; every operand tile starts on a 1024-byte boundary;
 // * one MMA is M = 128 x N x K = 16, single CTA (cta_group::1), fp32
 //   accumulation in tensor memory (TMEM), lane = row of D, column = column of D;
 // * no multicast: every TMA load fills only this CTA's shared memory.
@@ -106,6 +106,18 @@ __device__ __forceinline__ void tc_mma_f16(uint32_t d_tmem, uint64_t a_desc, uin
       : "memory");
 }
 
+// The same with kind::tf32: A and B hold fp32 values, of which the MMA uses
+// the tf32 part (K = 8 per instruction, 32 bytes of a row as for kind::f16).
+__device__ __forceinline__ void tc_mma_tf32(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // 32 consecutive fp32 columns of this thread's TMEM lane (32x32b shape: warp
 // w reads lanes 32*(w%4) .. +31).  The wait is inside the same statement, so
 // the registers are valid when it returns.
@@ -144,12 +156,35 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t addr, uint32_t lbo,
   return d;
 }
 
-// Instruction descriptor of tcgen05.mma kind::f16 with fp32 accumulation.
-__host__ __device__ constexpr uint32_t idesc_f16_f32(int m, int n, bool bf16, bool a_mn_major, bool b_mn_major) {
-  return (1u << 4) |                                          // D format: f32
-         ((bf16 ? 1u : 0u) << 7) | ((bf16 ? 1u : 0u) << 10) |  // A, B format: bf16 (1) or f16 (0)
+// Operand formats of kind::f16 and kind::tf32 (A and B use the same one).
+constexpr int kFmtF16 = 0, kFmtBF16 = 1, kFmtTF32 = 2;
+
+// The same for an MN-major fp32 operand of kind::tf32, which takes the
+// 128-byte swizzle with 32-byte atoms (TMA CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B):
+// 32 MN elements per 128-byte row, K rows 128 bytes apart in groups of four,
+// `sbo` bytes between the groups of four (512 for a dense tile), `lbo` bytes
+// between consecutive 32-element MN groups.
+__device__ __forceinline__ uint64_t smem_desc_sw128_atom32(uint32_t addr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((addr >> 4) & 0x3FFFu);
+  d |= static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16;
+  d |= static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32;
+  d |= 1ull << 46;  // descriptor version for sm_100
+  d |= 1ull << 61;  // 128-byte swizzle, 32-byte atoms
+  return d;
+}
+
+// Instruction descriptor of tcgen05.mma kind::f16 / kind::tf32 with fp32
+// accumulation; `fmt` is one of the formats above.
+__host__ __device__ constexpr uint32_t idesc_f32acc(int m, int n, int fmt, bool a_mn_major, bool b_mn_major) {
+  return (1u << 4) |                                                          // D format: f32
+         (static_cast<uint32_t>(fmt) << 7) | (static_cast<uint32_t>(fmt) << 10) |  // A, B format
          ((a_mn_major ? 1u : 0u) << 15) | ((b_mn_major ? 1u : 0u) << 16) |
          (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(m >> 4) << 24);
+}
+
+__host__ __device__ constexpr uint32_t idesc_f16_f32(int m, int n, bool bf16, bool a_mn_major, bool b_mn_major) {
+  return idesc_f32acc(m, n, bf16 ? kFmtBF16 : kFmtF16, a_mn_major, b_mn_major);
 }
 
 }  // namespace qcc

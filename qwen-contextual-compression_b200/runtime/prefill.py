@@ -6,8 +6,12 @@ In the reference a prefill selection comes in whole blocks: block top-K
 tile of tokens then runs ``TorchDynamicSparseFFN`` (``runtime/ffn.py:20-39``)
 on its expanded ids.  :class:`BlockSparsePrefill` takes the block ids of every
 tile and runs the whole prefill as tensor-core GEMMs over the packed records
-(``qcc_indexed_ffn_prefill``): a block used by several tiles is read once per
-pair of tiles instead of once per tile.
+(``qcc_indexed_ffn_prefill``).  The units of a block pair shared by several
+tiles run side by side and keep its rows in L2, so DRAM sees it about once.
+
+bf16 and fp16 records run on ``tcgen05.mma kind::f16``; fp32 records run on
+``kind::tf32``: the products use the tf32 part of each fp32 operand (x, the
+gate / up / down rows and the intermediate activations), the sums are fp32.
 """
 from __future__ import annotations
 
@@ -70,11 +74,11 @@ class PrefillWorkspace:
 
 
 class BlockSparsePrefill:
-    """Prefill of one packed FFN layer (bf16 or fp16 records) over per-tile block selections."""
+    """Prefill of one packed FFN layer (bf16, fp16 or fp32 records) over per-tile block selections."""
 
     def __init__(self, weights: PackedFFNWeights):
-        if weights.dtype not in (torch.bfloat16, torch.float16):
-            raise ValueError(f"expected bf16 or fp16 records for the tensor-core prefill, got {weights.dtype}")
+        if weights.dtype not in (torch.bfloat16, torch.float16, torch.float32):
+            raise ValueError(f"expected bf16, fp16 or fp32 records for the tensor-core prefill, got {weights.dtype}")
         _lib.require_cuda(weights.packed)
         self.weights = weights
         self._code = _lib.dtype_code(weights.dtype)

@@ -97,6 +97,63 @@ def test_prefill_reference_rounding_and_fp32_output():
     assert offn.rel_l2(y.double().cpu().numpy(), ref.double().numpy()) <= PREFILL_TOL
 
 
+def tf32(a: np.ndarray) -> np.ndarray:
+    """fp32 values cut to tf32 (10 explicit mantissa bits, the low 13 bits dropped)."""
+    return (np.asarray(a, dtype=np.float32).view(np.uint32) & np.uint32(0xFFFFE000)).view(np.float32)
+
+
+def oracle_prefill_tf32(x, tiles, gate, up, down):
+    """The prefill in float64 on tf32 operands, the activations cut to tf32 again before the down product."""
+    n = gate.shape[0]
+    xs, g, u, d = (tf32(t.numpy()).astype(np.float64) for t in (x, gate, up, down))
+    y = np.zeros((x.shape[0], gate.shape[1]))
+    for t, blocks in enumerate(tiles):
+        rows = slice(t * TILE_TOKENS, min((t + 1) * TILE_TOKENS, x.shape[0]))
+        ids = expand(blocks, n).numpy()
+        if ids.size:
+            gv, uv = xs[rows] @ g[ids].T, xs[rows] @ u[ids].T
+            a = (gv / (1.0 + np.exp(-gv)) * uv).astype(np.float32)
+            y[rows] = tf32(a).astype(np.float64) @ d[:, ids].T
+    return y
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("tokens,hidden,n,density", [
+    (128, 256, 512, 0.5),
+    (100, 200, 130, 0.7),      # partial tile, hidden not a multiple of 32, partial last block
+    (300, 1024, 1024, 0.3),
+    (640, 512, 768, 0.4),      # two groups of tiles
+    (257, 5120, 2048, 0.3),
+])
+def test_prefill_fp32_records_on_tf32(tokens, hidden, n, density):
+    """fp32 records run on kind::tf32, which reads the tf32 part of each fp32
+    operand (the low 13 mantissa bits dropped, not rounded).
+
+    * Against float64 on the same tf32 operands: rel-L2 <= 1e-4.  What remains
+      is the fp32 accumulation, and activations within an fp32 rounding of a
+      tf32 boundary that the kernel and float64 cut to neighbouring tf32 values.
+    * Against the exact fp32 layer: rel-L2 <= 5e-3 (measured 2.2e-3 to 2.3e-3),
+      the tf32 cut of three operand streams.
+    """
+    gen = torch.Generator().manual_seed(tokens * 5 + hidden + n)
+    gate = torch.randn(n, hidden, generator=gen) * 0.05
+    up = torch.randn(n, hidden, generator=gen) * 0.05
+    down = torch.randn(hidden, n, generator=gen) * 0.05
+    x = torch.randn(tokens, hidden, generator=gen)
+    n_blocks = (n + BLOCK_RECORDS - 1) // BLOCK_RECORDS
+    tiles = random_tiles(n_blocks, (tokens + TILE_TOKENS - 1) // TILE_TOKENS, gen, density)
+    dev = torch.device("cuda", 0)
+    engine = BlockSparsePrefill(pack_neuron_major(gate.to(dev), up.to(dev), down.to(dev)))
+    y = engine(x.to(dev), tiles)
+    torch.cuda.synchronize()
+    engine.check()
+    assert y.dtype == torch.float32
+    got = y.double().cpu().numpy()
+    assert offn.rel_l2(got, oracle_prefill_tf32(x, tiles, gate, up, down)) <= 1e-4
+    assert offn.rel_l2(got, oracle_prefill(x, tiles, gate, up, down)) <= 5e-3
+    assert torch.equal(engine(x.to(dev), tiles), y)
+
+
 @pytest.mark.gpu
 def test_prefill_empty_tiles_and_out_of_range_blocks():
     hidden, n, tokens = 256, 512, 384
@@ -193,12 +250,15 @@ def test_prefill_workload_density():
     assert flops == sum(2 * 128 * 3 * 5120 * 64 * t.numel() for t in tiles)
 
 
-def test_prefill_abi_rejects_fp32_and_bad_shapes():
+def test_prefill_abi_rejects_bad_dtypes_and_shapes():
     lib = _lib.library()
     dummy = 256
-    status = lib.qcc_indexed_ffn_prefill(dummy, 64, 4, 64, dummy, 64, _lib.DTYPE_F32, dummy, dummy, dummy, 1 << 20,
+    status = lib.qcc_indexed_ffn_prefill(dummy, 64, 4, 64, dummy, 64, 99, dummy, dummy, dummy, 1 << 20,
                                          dummy, 64, _lib.DTYPE_F32, None)
-    assert status == _lib.ERR_UNSUPPORTED
+    assert status == _lib.ERR_DTYPE
+    status = lib.qcc_indexed_ffn_prefill(dummy, 64, 4, 64, dummy, 64, _lib.DTYPE_F32, dummy, dummy, dummy, 1 << 20,
+                                         dummy, 64, 99, None)
+    assert status == _lib.ERR_DTYPE
     status = lib.qcc_indexed_ffn_prefill(dummy, 32, 4, 64, dummy, 64, _lib.DTYPE_BF16, dummy, dummy, dummy, 1 << 20,
                                          dummy, 64, _lib.DTYPE_BF16, None)
     assert status == _lib.ERR_SHAPE
