@@ -303,20 +303,28 @@ def measure_selector(engine, x, device, stream, side) -> dict:
         engine(x, ids1[0], out=y1)
 
     out["select_ffn_us_batch1"] = round(graph_time_us(step1, steps, stream, side), 2)
-    batch = 8
-    scores8 = [workloads.selector_scores(batch, seed=40 + i).to(device) for i in range(steps)]
-    ids8 = torch.empty((batch, k), dtype=torch.int32, device=device)
-    x8 = workloads.decode_x(batch=batch).to(device)
-    y8 = torch.empty((batch, HIDDEN), dtype=torch.bfloat16, device=device)
+    # Batches of 2, 4 and 8 tokens with their own selections: selector, union of
+    # the ids with per-token bits, one decode over the union (8 tokens: two
+    # launches of 4 over the same union and mask).  union_gbs: the union's
+    # record bytes (+ x, ids, y) over the step time.
+    for batch in (2, 4, 8):
+        scores_b = [workloads.selector_scores(batch, seed=40 + i).to(device) for i in range(steps)]
+        ids_b = torch.empty((batch, k), dtype=torch.int32, device=device)
+        x_b = workloads.decode_x(batch=batch).to(device)
+        y_b = torch.empty((batch, HIDDEN), dtype=torch.bfloat16, device=device)
 
-    def step8(i):
-        select_topk(scores8[i], k, out=ids8)
-        union, mask, count = build_union(ids8, 0, INTERMEDIATE)
-        engine(x8, union, token_mask=mask, n_ids_dev=count, out=y8)
+        def step_b(i, scores_b=scores_b, ids_b=ids_b, x_b=x_b, y_b=y_b):
+            select_topk(scores_b[i], k, out=ids_b)
+            union, mask, count = build_union(ids_b, 0, INTERMEDIATE)
+            engine(x_b, union, token_mask=mask, n_ids_dev=count, out=y_b)
 
-    out["select_union_ffn_us_batch8"] = round(graph_time_us(step8, steps, stream, side), 2)
-    union, _, count = build_union(select_topk(scores8[0], k), 0, INTERMEDIATE)
-    out["union_records_batch8"] = int(count.item())
+        us = graph_time_us(step_b, steps, stream, side)
+        records = float(torch.stack([build_union(select_topk(scores_b[i], k), 0, INTERMEDIATE)[2]
+                                     for i in range(steps)]).float().mean().item())
+        union_bytes = records * 3 * HIDDEN * 2 + batch * HIDDEN * 2 * 2 + records * 4
+        out[f"select_union_ffn_us_batch{batch}"] = round(us, 2)
+        out[f"union_records_batch{batch}"] = round(records, 1)
+        out[f"union_gbs_batch{batch}"] = round(union_bytes / (us * 1e-6) / 1e9, 1)
     out["score_select"] = measure_score_select(engine, x, device, stream, side)
     return out
 

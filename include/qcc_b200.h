@@ -60,6 +60,13 @@ extern "C" {
  * qcc_selector_scores_topk on the same stream. */
 #define QCC_IDS_READY 0x100
 
+/* OR-ed into the index type of the decode entry points, QCC_MASK_SHIFT(s),
+ * s in 0..7: token b of the call uses bit s + b of each token_mask byte (and
+ * s + batch <= 8).  A host that splits a batch of up to 8 tokens into calls of
+ * qcc_decode_max_batch tokens passes the same mask with the chunk's first token
+ * as s instead of a shifted copy. */
+#define QCC_MASK_SHIFT(s) (((s) & 7) << 12)
+
 /* Host-side status codes. */
 #define QCC_OK 0
 #define QCC_ERR_INVALID_ARGUMENT 1 /* null pointer, negative size, bad enum */
@@ -143,14 +150,16 @@ QCC_API int qcc_workspace_init(void* workspace, size_t workspace_bytes, cudaStre
  *   x          : [batch, hidden] in `dtype`, row stride ldx elements
  *   packed     : qcc_pack_records layout, n_records records
  *   ids        : n_ids selected record indices (ids_dtype QCC_INDEX_I32 or
- *                _I64, optionally | QCC_IDS_READY); any order, duplicates
+ *                _I64, optionally | QCC_IDS_READY | QCC_MASK_SHIFT(s)); any
+ *                order, duplicates
  *                count twice (as index_select does); out-of-range ids
  *                contribute nothing and raise QCC_DEV_ID_RANGE
  *   n_ids_dev  : optional device int32 count; when non-null the kernel uses
  *                min(*n_ids_dev, n_ids) ids (output of qcc_build_union)
- *   token_mask : optional [n_ids] bytes; bit b set = token b uses record j.
- *                Null means every token uses every record (the reference's
- *                one shared 1-D id list, runtime/ffn.py:20-23).
+ *   token_mask : optional [n_ids] bytes; bit b set = token b uses record j
+ *                (bit s + b with QCC_MASK_SHIFT(s) in ids_dtype).  Null
+ *                means every token uses every record (the reference's one
+ *                shared 1-D id list, runtime/ffn.py:20-23).
  *   y_out      : [batch, hidden] in y_dtype (dtype or QCC_DTYPE_F32)
  *   y_in       : optional fp32 [batch, hidden] (row stride ld_in) added to
  *                the sum before the final rounding: a residual, or the

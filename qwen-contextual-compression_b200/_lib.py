@@ -19,6 +19,11 @@ DTYPE_BF16, DTYPE_F16, DTYPE_F32 = 0, 1, 2
 INDEX_I32, INDEX_I64 = 0, 1
 IDS_READY = 0x100  # OR-ed into the index type: the ids are not written by an earlier qcc launch on the stream
 
+
+def mask_shift(s: int) -> int:
+    """QCC_MASK_SHIFT(s): OR-ed into the index type, token b of the call reads bit s + b of the token mask."""
+    return (s & 7) << 12
+
 OK = 0
 ERR_INVALID_ARGUMENT, ERR_SHAPE, ERR_DTYPE, ERR_ALIGNMENT, ERR_UNSUPPORTED, ERR_WORKSPACE, ERR_CUDA = range(1, 8)
 DEV_ID_RANGE, DEV_TIMEOUT = 1, 2

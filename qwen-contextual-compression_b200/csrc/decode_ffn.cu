@@ -109,6 +109,7 @@ struct DecodeArgs {
   int ids64;
   int ids_ready;  // ids / count / mask may be read before the preceding launches finish
   const uint8_t* token_mask;
+  int mask_shift;  // token b uses bit mask_shift + b of its token_mask byte
   int n_ids;
   const int32_t* n_ids_dev;
   unsigned int* status;
@@ -294,7 +295,8 @@ __global__ void __launch_bounds__(kMaxThreads, 1) indexed_ffn_decode_kernel(cons
     const bool in_range = id >= 0 && id < a.n_records;
     if (!in_range) atomicOr(a.status, QCC_DEV_ID_RANGE);
     s_ids[i] = in_range ? static_cast<int32_t>(id) : -1;
-    s_bits[i] = a.token_mask ? __ldg(a.token_mask + begin + i) : static_cast<uint8_t>(0xFFu);
+    s_bits[i] = a.token_mask ? static_cast<uint8_t>(__ldg(a.token_mask + begin + i) >> a.mask_shift)
+                             : static_cast<uint8_t>(0xFFu);
   };
 
   float xr[B][VPT][8];
@@ -898,11 +900,13 @@ int launch_decode(const DecodeRequest& q) {
   if (q.world < 1 || q.world > kMaxRanks || q.rank < 0 || q.rank >= q.world) return QCC_ERR_SHAPE;
   if (q.id_lo >= 0 && q.id_hi < q.id_lo) return QCC_ERR_SHAPE;
   if (mode != kModeGateUp && q.y_dtype != q.dtype && q.y_dtype != QCC_DTYPE_F32) return QCC_ERR_DTYPE;
-  if ((q.ids_kind & ~(0xFF | QCC_IDS_READY)) != 0) return QCC_ERR_DTYPE;
+  if ((q.ids_kind & ~(0xFF | QCC_IDS_READY | QCC_MASK_SHIFT(7))) != 0) return QCC_ERR_DTYPE;
+  const int mask_shift = (q.ids_kind >> 12) & 7;
   const int ids_dtype = q.ids_kind & 0xFF;
   if (ids_dtype != QCC_INDEX_I32 && ids_dtype != QCC_INDEX_I64) return QCC_ERR_DTYPE;
   if (mode == kModeDown && !valid_dtype(q.act_in_dtype)) return QCC_ERR_DTYPE;
   if (q.batch < 1 || q.hidden < 1 || q.n_records < 0 || q.n_ids < 0) return QCC_ERR_SHAPE;
+  if (mask_shift + q.batch > 8) return QCC_ERR_SHAPE;  // the tokens' bits must lie in the mask byte
   if (q.batch > decode_max_batch(q.hidden, q.dtype)) return QCC_ERR_UNSUPPORTED;
   if (mode != kModeDown && q.ldx < q.hidden) return QCC_ERR_SHAPE;
   if (mode != kModeGateUp && q.ldy < q.hidden) return QCC_ERR_SHAPE;
@@ -992,6 +996,7 @@ int launch_decode(const DecodeRequest& q) {
   args.ids64 = ids_dtype == QCC_INDEX_I64;
   args.ids_ready = (q.ids_kind & QCC_IDS_READY) != 0;
   args.token_mask = q.token_mask;
+  args.mask_shift = mask_shift;
   args.n_ids = n_ids;
   args.n_ids_dev = q.n_ids_dev;
   args.status = reinterpret_cast<unsigned int*>(ws);

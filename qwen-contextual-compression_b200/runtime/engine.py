@@ -166,11 +166,8 @@ class IndexedSparseFFN:
         for start in range(0, batch, self.max_batch):
             chunk = min(self.max_batch, batch - start)
             a_ptr = None if activation is None else activation.data_ptr() + start * activation.stride(0) * plan.esize_x
-            if token_mask is not None and start > 0:
-                # Token bits start.. moved down to bit 0.  The temporary comes from
-                # the caching allocator on this stream, so its reuse is ordered
-                # after the kernel that reads it.
-                mask_ptr = torch.bitwise_right_shift(token_mask, start).data_ptr()
+            # The chunk's tokens read bits start.. of the same mask (QCC_MASK_SHIFT).
+            chunk_code = ids_code | (_lib.mask_shift(start) if token_mask is not None else 0)
             acc_ptr = None if accumulate is None else accumulate.data_ptr() + start * acc_row
             if exchange is not None or id_range is not None:
                 if a_ptr is not None:
@@ -181,7 +178,7 @@ class IndexedSparseFFN:
                 world, rank = (exchange.world, exchange.rank) if exchange is not None else (1, 0)
                 status = lib.qcc_indexed_ffn_decode_allreduce(
                     x_ptr + start * x_row, x.stride(0), chunk, plan.hidden, plan.packed_ptr, plan.n_records,
-                    plan.code, ids.data_ptr(), ids_code, n_ids, count_ptr, mask_ptr, ws.ptr, ws.nbytes,
+                    plan.code, ids.data_ptr(), chunk_code, n_ids, count_ptr, mask_ptr, ws.ptr, ws.nbytes,
                     out_ptr + start * out_row, out.stride(0), plan.y_code, acc_ptr, acc_ld, id_begin, id_end,
                     exchange.pointers if exchange is not None else None,
                     exchange.nbytes if exchange is not None else 0, world, rank, stream)
@@ -190,7 +187,7 @@ class IndexedSparseFFN:
                 continue
             status = lib.qcc_indexed_ffn_decode(
                 x_ptr + start * x_row, x.stride(0), chunk, plan.hidden, plan.packed_ptr, plan.n_records, plan.code,
-                ids.data_ptr(), ids_code, n_ids, count_ptr, mask_ptr, ws.ptr, ws.nbytes,
+                ids.data_ptr(), chunk_code, n_ids, count_ptr, mask_ptr, ws.ptr, ws.nbytes,
                 out_ptr + start * out_row, out.stride(0), plan.y_code, acc_ptr, acc_ld, a_ptr, n_ids if a_ptr else 0,
                 stream)
             if status:
@@ -225,6 +222,8 @@ class IndexedSparseFFN:
             raise ValueError("selected IDs must be contiguous one-dimensional int32 or int64")
         device = _lib.require_cuda(x, ids, w.packed, token_mask, n_ids_dev, out, activation)
         batch, n_ids = x.shape[0], ids.shape[0]
+        if token_mask is not None and batch > 8:
+            raise ValueError("a token_mask holds 8 tokens per byte: batch must be <= 8 with a token_mask")
         if token_mask is not None and (token_mask.dtype != torch.uint8 or token_mask.numel() < n_ids
                                        or not token_mask.is_contiguous()):
             raise ValueError("token_mask must be a contiguous uint8 tensor with one byte per id")

@@ -75,6 +75,13 @@ def test_argument_validation_happens_before_any_cuda_call():
     args[8] = _lib.INDEX_I32 | _lib.IDS_READY
     args[2] = 0
     assert lib.qcc_indexed_ffn_decode(*args) == _lib.ERR_SHAPE  # the flag is accepted, batch 0 is not
+    # QCC_MASK_SHIFT(s): the call's tokens must fit bits s .. s + batch - 1 of the mask byte.
+    args[2] = 4
+    args[8] = _lib.INDEX_I32 | _lib.mask_shift(5)
+    assert lib.qcc_indexed_ffn_decode(*args) == _lib.ERR_SHAPE
+    args[8] = _lib.INDEX_I32 | 0x8000  # the bit above the shift field
+    assert lib.qcc_indexed_ffn_decode(*args) == _lib.ERR_DTYPE
+    args[2], args[8] = 1, _lib.INDEX_I32
     # Cross-rank sum: the exchange buffers must hold three slots of this batch for every rank.
     need = int(lib.qcc_exchange_bytes(2, 1, 8, _lib.DTYPE_BF16))
     assert need == 256 + 3 * 2 * 2 * 16
