@@ -81,7 +81,7 @@ constexpr uint32_t kSmemBytes = kStages * kStageBytes + kControlBytes + 1024;  /
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kAccCols = 256;        // one accumulator buffer
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
-constexpr int kMaxBlocks = 1 << 15;        // block ids fit the 15-bit fields of a unit word
+constexpr int kMaxBlocks = (1 << 15) - 1;  // block ids fit the 15-bit fields of a unit word (0x7FFF: none)
 constexpr int kMaxDownUnits = 512;        // tiles x 256-wide hidden ranges (hidden <= 32768)
 constexpr size_t kSlotFloats = 128 * 256; // one CTA's partial accumulators
 constexpr int kMaxContrib = 16;           // CTAs that may hand partial sums to one unit's finishing CTA
@@ -262,9 +262,9 @@ __device__ __forceinline__ int unit_blocks(int unit) { return ((unit >> 15) & 0x
 // ---------------------------------------------------------------------------
 
 // Phase 1: (unit, chunk) at cost position p.  A chunk of a block pair costs
-// kPairCost, a chunk of a single block kSingleCost: measured per-step times
-// of 0.154 and 0.202 us (a single block's N = 128 MMA takes as long as a
-// pair's N = 256 one, and the per-step overhead is the same).
+// kPairCost, a chunk of a single block kSingleCost: per-CTA stamps measured
+// 0.154 and 0.202 us per ring iteration (the ring is latency-bound, so a
+// single block's iteration is not cheaper than a pair's).
 __device__ void locate_gate_up(const int* units, const int* prefix, int n_units, int total, int64_t p, int* u,
                                int* k) {
   if (p >= total || n_units == 0) {
@@ -421,7 +421,7 @@ __global__ void __launch_bounds__(kPlanThreads)
   const int hi = min(n_blocks, lo + chunk);
   // Each tile's blocks in ascending order: the four tiles' counts go through
   // two scans, two tiles per 32-bit word (a count fits 16 bits: n_blocks <=
-  // kMaxBlocks = 2^15).
+  // kMaxBlocks < 2^15).
   static_assert(kMaxTiles == 4 && kMaxBlocks <= 65535, "packed tile counts");
   int c01 = 0, c23 = 0;
   for (int i = lo; i < hi; ++i) {
