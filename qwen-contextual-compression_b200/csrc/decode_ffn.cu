@@ -210,8 +210,14 @@ __device__ __forceinline__ float warp_reduce_multi(float (&v)[V], int lane) {
 // Shared-memory layout after the record ring (host mirrors it in tail_bytes):
 //   mbarriers [kMaxStages] | warp partials [2][VP][32] f32 | flag [4] i32 |
 //   ids [id_cap] i32 | token bits [id_cap] u8
-template <typename T, int B, int VPT, int R, int MODE>
+// DN (whole records only): the down slices are read from the ring when the
+// group is finished, one iteration later, and the group's slots are refilled
+// after that (instead of holding the slices in registers and refilling at
+// once).  Frees the registers that two records per group need at 3-4 tokens,
+// at the cost of R fewer records in flight.
+template <typename T, int B, int VPT, int R, int MODE, bool DN>
 __global__ void __launch_bounds__(kMaxThreads, 1) indexed_ffn_decode_kernel(const DecodeArgs a) {
+  static_assert(!DN || MODE == kModeFull, "down slices from the ring: whole records only");
   extern __shared__ __align__(128) uint8_t smem[];
   constexpr int kVals = 2 * R * B;          // partial sums per group: (gate, up) x records x tokens
   constexpr int VP = next_pow2(kVals);      // padded to a power of two for the butterfly
@@ -383,6 +389,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1) indexed_ffn_decode_kernel(cons
   int rn_prev = 0;
   int buf = 0;
   int stage0 = 0;    // ring slot of the group's first record
+  int stage_prev = 0;  // ring slot of the previous group's first record (DN)
   uint32_t phase0 = 0;
   int consumed = 0;
   bool aborted = false;
@@ -424,7 +431,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1) indexed_ffn_decode_kernel(cons
           for (int k = 0; k < VPT; ++k) {
             const int v = tid + k * nthreads;
             if (v < nslots) {
-              if constexpr (MODE == kModeFull) dn_cur[r][k] = load_pack8(rec + 2 * seg + 8 * v);
+              if constexpr (MODE == kModeFull && !DN) dn_cur[r][k] = load_pack8(rec + 2 * seg + 8 * v);
               if constexpr (MODE == kModeDown) dn_cur[r][k] = load_pack8(rec + 8 * v);
               if constexpr (MODE == kModeDown) continue;
               const Pack8<T> gr = load_pack8(rec + 8 * v);
@@ -496,7 +503,15 @@ __global__ void __launch_bounds__(kMaxThreads, 1) indexed_ffn_decode_kernel(cons
                 const int v = tid + k * nthreads;
                 if (v < nslots) {
                   float df[8];
-                  widen(dn_prev[r][k], df);
+                  if constexpr (DN) {
+                    int st = stage_prev + r;
+                    if (st >= S) st -= S;
+                    widen(load_pack8(reinterpret_cast<const T*>(smem + static_cast<size_t>(st) * a.copy_bytes) +
+                                     2 * seg + 8 * v),
+                          df);
+                  } else {
+                    widen(dn_prev[r][k], df);
+                  }
 #pragma unroll
                   for (int e = 0; e < 8; ++e) yr[b][k][e] = fmaf(act, df[e], yr[b][k][e]);
                 }
@@ -512,12 +527,16 @@ __global__ void __launch_bounds__(kMaxThreads, 1) indexed_ffn_decode_kernel(cons
       consumed = g0;
       break;
     }
-    // Every thread has its down slices of this group in registers: refill.
+    // Every thread has its down slices of this group in registers (of the
+    // previous group, with DN: finished above): refill those slots.
     if (tid == 0) {
-      for (int r = 0; r < rn; ++r) {
-        const int i = g0 + r + S;
+      const int gr = DN ? g0 - R : g0;  // first record of the freed group
+      const int n_free = DN ? rn_prev : rn;
+      const int st0 = DN ? stage_prev : stage0;
+      for (int r = 0; r < n_free; ++r) {
+        const int i = gr + r + S;
         if (i < cnt) {
-          int stage = stage0 + r;
+          int stage = st0 + r;
           if (stage >= S) stage -= S;
           issue(i, stage);
           issued = i + 1;
@@ -535,6 +554,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1) indexed_ffn_decode_kernel(cons
     }
     rn_prev = rn;
     buf ^= 1;
+    stage_prev = stage0;
     stage0 += R;
     if (stage0 >= S) {
       stage0 -= S;
@@ -712,9 +732,17 @@ constexpr int group_records() {
   return (sizeof(T) == 2 && B <= 2) ? 2 : 1;
 }
 
+// Whole records at 3-4 tokens of 16-bit weights: two records per group with the
+// down slices read from the ring (DN), which fits the registers.
+template <typename T, int B, int MODE>
+constexpr bool down_from_ring() {
+  return MODE == kModeFull && sizeof(T) == 2 && B >= 3;
+}
+
 template <typename T, int B, int VPT, int MODE>
 KernelFn kernel_for() {
-  return indexed_ffn_decode_kernel<T, B, VPT, group_records<T, B>(), MODE>;
+  constexpr bool dn = down_from_ring<T, B, MODE>();
+  return indexed_ffn_decode_kernel<T, B, VPT, dn ? 2 : group_records<T, B>(), MODE, dn>;
 }
 
 // Slots of 8 hidden elements per thread: 1, 2 or 4 (hidden <= 2560, 5120,
