@@ -39,6 +39,7 @@ namespace {
 
 constexpr int kSelectThreads = 1024;
 constexpr int kUnionThreads = 1024;
+constexpr int kUnionLoads = 8;  // id loads in flight per thread in build_union_kernel
 constexpr int kDigit1Bins = 1 << 12;                       // key bits 31..20
 constexpr int kDigitBins = 1 << 10;                        // key bits 19..10, then 9..0
 constexpr int kCandidateCap = kDigit1Bins - kDigitBins;   // candidate keys that fit beside a 10-bit histogram
@@ -278,13 +279,23 @@ __global__ void __launch_bounds__(kUnionThreads, 1)
   const int tid = threadIdx.x;
   for (int i = tid; i < nwords; i += blockDim.x) words[i] = 0u;
   __syncthreads();
-  for (int b = 0; b < batch; ++b) {
-    const int32_t* row = ids + b * ld_ids;
-    for (int j = tid; j < k; j += blockDim.x) {
-      const int32_t id = __ldg(row + j);
-      if (id >= id_begin && id < id_end) {
-        const int local = id - id_begin;
-        atomicOr(&words[local >> 2], (1u << b) << (8 * (local & 3)));
+  // All rows' ids as one range of batch * k elements, kUnionLoads loads in
+  // flight per thread before their atomics (row by row, one load at a time,
+  // this phase was a chain of ~30 dependent L2 round trips at batch 8).
+  const int total_ids = batch * k;
+  for (int base = tid; base < total_ids; base += static_cast<int>(blockDim.x) * kUnionLoads) {
+    int32_t v[kUnionLoads];
+#pragma unroll
+    for (int u = 0; u < kUnionLoads; ++u) {
+      const int e = base + u * static_cast<int>(blockDim.x);
+      v[u] = e < total_ids ? __ldg(ids + static_cast<int64_t>(e / k) * ld_ids + e % k) : 0;
+    }
+#pragma unroll
+    for (int u = 0; u < kUnionLoads; ++u) {
+      const int e = base + u * static_cast<int>(blockDim.x);
+      if (e < total_ids && v[u] >= id_begin && v[u] < id_end) {
+        const int local = v[u] - id_begin;
+        atomicOr(&words[local >> 2], (1u << (e / k)) << (8 * (local & 3)));
       }
     }
   }
