@@ -49,7 +49,8 @@ constexpr int kMaxGrid = 160;          // decode CTAs (one per SM) whose partial
 constexpr int kRowLoads = (kMaxGrid + 31) / 32;  // partial rows per lane in the reduce
 constexpr int kMaxStages = 16;      // ring slots (mbarriers) for the gate|up-only and down-only passes
 constexpr int kMaxStagesFull = 8;   // ring slots when whole records stream (registers of the first ids)
-constexpr int kMaxThreads = 320;  // 10 warps; hidden 5120 = two 8-element slots per thread
+constexpr int kMaxThreads = 320;  // compute threads: 10 warps; hidden 5120 = two 8-element slots per thread
+constexpr int kMaxBlock = kMaxThreads + 32;  // plus the producer warp
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s bound on any bulk-copy wait, default exchange bound
 constexpr int kMaxRanks = 8;
 // Cross-rank exchange buffer: a 256-byte header -- the launches that used
@@ -210,13 +211,28 @@ __device__ __forceinline__ float warp_reduce_multi(float (&v)[V], int lane) {
 // Shared-memory layout after the record ring (host mirrors it in tail_bytes):
 //   mbarriers [kMaxStages] | warp partials [2][VP][32] f32 | flag [4] i32 |
 //   ids [id_cap] i32 | token bits [id_cap] u8
+// Barrier 1 over the first n threads of the CTA (the compute warps; the
+// producer warp does not take part) that also ORs a predicate across them.
+__device__ __forceinline__ bool compute_barrier_or(bool v, int n) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 q, %1, 0;\n\t"
+      "bar.red.or.pred p, 1, %2, q;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(r)
+      : "r"(v ? 1u : 0u), "r"(n)
+      : "memory");
+  return r != 0;
+}
+
 // DN (whole records only): the down slices are read from the ring when the
 // group is finished, one iteration later, and the group's slots are refilled
 // after that (instead of holding the slices in registers and refilling at
 // once).  Frees the registers that two records per group need at 3-4 tokens,
 // at the cost of R fewer records in flight.
 template <typename T, int B, int VPT, int R, int MODE, bool DN>
-__global__ void __launch_bounds__(kMaxThreads, 1) indexed_ffn_decode_kernel(const DecodeArgs a) {
+__global__ void __launch_bounds__(kMaxBlock, 1) indexed_ffn_decode_kernel(const DecodeArgs a) {
   static_assert(!DN || MODE == kModeFull, "down slices from the ring: whole records only");
   extern __shared__ __align__(128) uint8_t smem[];
   constexpr int kVals = 2 * R * B;          // partial sums per group: (gate, up) x records x tokens
@@ -225,14 +241,18 @@ __global__ void __launch_bounds__(kMaxThreads, 1) indexed_ffn_decode_kernel(cons
   const int tid = threadIdx.x;
   const int lane = tid & 31;
   const int warp = tid >> 5;
-  const int nthreads = blockDim.x;
+  // The last warp is the producer: it issues the record copies, the others
+  // (nthreads compute threads) consume them.
+  const int nthreads = blockDim.x - 32;
   const int nwarps = nthreads >> 5;
+  const bool producer = warp == nwarps;
   const int S = a.stages;
   const int seg = a.hidden_pad;
   const int nslots = seg >> 3;
 
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + a.ring_bytes);
-  float* s_red = reinterpret_cast<float*>(bars + kMaxStages);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + a.ring_bytes);   // slot filled
+  uint64_t* empty = bars + kMaxStages;                                  // slot consumed
+  float* s_red = reinterpret_cast<float*>(empty + kMaxStages);
   int* s_flag = reinterpret_cast<int*>(s_red + 2 * VP * 32);
   int32_t* s_ids = s_flag + 4;
   uint8_t* s_bits = reinterpret_cast<uint8_t*>(s_ids + a.id_cap);
@@ -253,7 +273,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1) indexed_ffn_decode_kernel(cons
     // [#ids < id_lo, #ids < id_hi): count both in one coalesced pass (every
     // load in flight at once) and a block reduction.
     unsigned int below_lo = 0, below_hi = 0;
-    for (int i = tid; i < n; i += nthreads) {
+    for (int i = tid; i < n && !producer; i += nthreads) {
       const int64_t id = load_id(a, i);
       below_lo += id < a.id_lo ? 1u : 0u;
       below_hi += id < a.id_hi ? 1u : 0u;
@@ -261,7 +281,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1) indexed_ffn_decode_kernel(cons
     below_lo = __reduce_add_sync(0xffffffffu, below_lo);
     below_hi = __reduce_add_sync(0xffffffffu, below_hi);
     unsigned int* s_count = reinterpret_cast<unsigned int*>(s_red);  // free until the pipeline starts
-    if (lane == 0) {
+    if (lane == 0 && !producer) {
       s_count[2 * warp] = below_lo;
       s_count[2 * warp + 1] = below_hi;
     }
@@ -280,12 +300,12 @@ __global__ void __launch_bounds__(kMaxThreads, 1) indexed_ffn_decode_kernel(cons
   const int cnt = end - begin;
 
   const uint64_t policy = policy_evict_first();
-  int issued = 0;  // meaningful in thread 0 only
+  int issued = 0;  // meaningful in the producer's lane 0 only
   // Source of the streamed part of record id (read from the kernel parameters
   // at each use, so that no pointer stays live in a register).
   auto part_src = [&](int32_t id) { return a.packed + a.copy_offset + static_cast<int64_t>(id) * a.record_bytes; };
 
-  auto issue = [&](int i, int stage) {  // thread 0: start the bulk copy of local record i
+  auto issue = [&](int i, int stage) {  // producer: start the bulk copy of local record i
     const int32_t id = s_ids[i];
     uint64_t* bar = &bars[stage];
     if (id >= 0) {
@@ -336,25 +356,31 @@ __global__ void __launch_bounds__(kMaxThreads, 1) indexed_ffn_decode_kernel(cons
   // are in the memory system before any record copy (loads issued after the
   // copies queue behind ~30 MB of record traffic).  With it, x may only be
   // read after the wait for the preceding launches, so the ids and the first
-  // record copies go first and x follows the wait.  Thread 0 fetches the first
-  // S ids itself and starts their copies without waiting for the block
+  // record copies go first and x follows the wait.  The producer fetches the
+  // first S ids itself and starts their copies without waiting for the block
   // barrier.
   const int pre = min(S, cnt);
-  if (!a.ids_ready) load_x();
-  // Thread 0's first S ids are loaded into registers together with the
+  if (!a.ids_ready && !producer) load_x();
+  // The producer's first S ids are loaded into registers together with the
   // cache loads, so one memory latency covers both.
   constexpr int kFirst = MODE == kModeFull ? kMaxStagesFull : kMaxStages;
   int32_t first_ids[kFirst];
-  if (tid == 0) {
+  const bool issuer = producer && lane == 0;
+  if (issuer) {
 #pragma unroll
     for (int i = 0; i < kFirst; ++i) {
       const int64_t id = i < pre ? load_id(a, begin + i) - rebase : -1;
       first_ids[i] = (id >= 0 && id < a.n_records) ? static_cast<int32_t>(id) : -1;
     }
   }
-  for (int i = tid; i < cnt; i += nthreads) cache_id(i);
-  if (tid == 0) {
-    for (int s = 0; s < S; ++s) mbar_init(&bars[s], 1);
+  if (!producer)
+    for (int i = tid; i < cnt; i += nthreads) cache_id(i);
+  if (issuer) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&bars[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    s_flag[0] = 0;  // set by the consumers when they give up
     fence_barrier_init();
 #pragma unroll
     for (int i = 0; i < kFirst; ++i) {
@@ -372,11 +398,39 @@ __global__ void __launch_bounds__(kMaxThreads, 1) indexed_ffn_decode_kernel(cons
     }
     issued = pre;
   }
-  if (a.ids_ready) {
+  if (a.ids_ready && !producer) {
     asm volatile("griddepcontrol.wait;" ::: "memory");
     load_x();
   }
   __syncthreads();
+
+  if (producer) {
+    // Refill each slot as soon as the consumers free it (they arrive on
+    // empty[slot] after the barrier of the group that used it): record i goes
+    // to slot i % S after its (i / S)-th release.  Its copy-issue time (about
+    // 0.2 us per two records) is no longer on the compute warps' path.
+    if (issuer) {
+      for (int i = pre; i < cnt; ++i) {
+        const int stage = i % S;
+        const uint32_t parity = ((i / S) & 1u) ^ 1u;
+        bool ok = mbar_try_wait(&empty[stage], parity);
+        if (!ok) {
+          const uint64_t start = global_timer_ns();
+          while (!(ok = mbar_try_wait(&empty[stage], parity))) {
+            if (*reinterpret_cast<volatile int*>(s_flag) != 0 || global_timer_ns() - start > kWaitLimitNs) break;
+          }
+        }
+        if (!ok) break;
+        issue(i, stage);
+        issued = i + 1;
+      }
+      // After a give-up (or with every record issued): the copies of the last
+      // S issued records have landed before the CTA exits.
+      for (int i = max(0, issued - S); i < issued; ++i)
+        (void)mbar_wait_bounded(&bars[i % S], (i / S) & 1, kWaitLimitNs);
+    }
+    return;
+  }
 
   // Software pipeline, one barrier per group of R records:
   //   iteration g: wait for group g, partial dot products of group g -> warp
@@ -391,7 +445,6 @@ __global__ void __launch_bounds__(kMaxThreads, 1) indexed_ffn_decode_kernel(cons
   int stage0 = 0;    // ring slot of the group's first record
   int stage_prev = 0;  // ring slot of the previous group's first record (DN)
   uint32_t phase0 = 0;
-  int consumed = 0;
   bool aborted = false;
   for (int g0 = 0;; g0 += R) {
     const int rn = min(R, cnt - g0);
@@ -522,25 +575,21 @@ __global__ void __launch_bounds__(kMaxThreads, 1) indexed_ffn_decode_kernel(cons
       }
     }
     if (rn <= 0) break;
-    if (__syncthreads_or(!ok)) {
+    if (compute_barrier_or(!ok, nthreads)) {
       aborted = true;
-      consumed = g0;
+      if (tid == 0) *reinterpret_cast<volatile int*>(s_flag) = 1;  // the producer stops refilling
       break;
     }
     // Every thread has its down slices of this group in registers (of the
-    // previous group, with DN: finished above): refill those slots.
+    // previous group, with DN: finished above): release those slots to the
+    // producer.
     if (tid == 0) {
-      const int gr = DN ? g0 - R : g0;  // first record of the freed group
       const int n_free = DN ? rn_prev : rn;
       const int st0 = DN ? stage_prev : stage0;
       for (int r = 0; r < n_free; ++r) {
-        const int i = gr + r + S;
-        if (i < cnt) {
-          int stage = st0 + r;
-          if (stage >= S) stage -= S;
-          issue(i, stage);
-          issued = i + 1;
-        }
+        int stage = st0 + r;
+        if (stage >= S) stage -= S;
+        mbar_arrive(&empty[stage]);
       }
     }
 #pragma unroll
@@ -562,12 +611,8 @@ __global__ void __launch_bounds__(kMaxThreads, 1) indexed_ffn_decode_kernel(cons
     }
   }
 
-  if (aborted && tid == 0) {
-    // Drain this CTA's bulk copies still in flight (bounded) before the CTA
-    // exits and its shared memory goes to another CTA.
-    atomicOr(a.status, QCC_DEV_TIMEOUT);
-    for (int i = consumed; i < issued; ++i) (void)mbar_wait_bounded(&bars[i % S], (i / S) & 1, kWaitLimitNs);
-  }
+  // After a give-up the producer drains the copies in flight (above).
+  if (aborted && tid == 0) atomicOr(a.status, QCC_DEV_TIMEOUT);
   if constexpr (MODE == kModeGateUp) return;  // activations only: no partial y
 
   // Every CTA (also one with no records) stores its partial y row.  The row
@@ -786,8 +831,8 @@ struct LaunchShape {
 };
 
 size_t tail_bytes(int id_cap) {
-  // mbarriers, warp partials (at most 2 * 32 values x 32 warps), flag, id cache, token bits
-  return kMaxStages * sizeof(uint64_t) + 2 * 32 * 32 * sizeof(float) + 4 * sizeof(int) +
+  // mbarriers (filled, consumed), warp partials (at most 2 * 32 values x 32 warps), flag, id cache, token bits
+  return 2 * kMaxStages * sizeof(uint64_t) + 2 * 32 * 32 * sizeof(float) + 4 * sizeof(int) +
          static_cast<size_t>(id_cap) * sizeof(int32_t) + (static_cast<size_t>(id_cap) + 15) / 16 * 16;
 }
 
@@ -997,7 +1042,8 @@ int launch_decode(const DecodeRequest& q) {
     fn = pick_kernel_mode<float>(mode, q.batch, shape.vpt);
   if (fn == nullptr) return QCC_ERR_UNSUPPORTED;
 
-  const int nb = blocks_per_sm(fn, device, shape.threads, shape.smem);
+  const int block = shape.threads + 32;  // compute threads and the producer warp
+  const int nb = blocks_per_sm(fn, device, block, shape.smem);
   if (nb <= 0) return QCC_ERR_CUDA;
   // At most one CTA per SM (the workspace holds kMaxGrid partial rows); no
   // CTA waits for another, so residency of the whole grid is not required.
@@ -1051,7 +1097,7 @@ int launch_decode(const DecodeRequest& q) {
   args.act_in_dtype = q.act_in_dtype;
 
   clear_stale_error();
-  if (!launch_dependent(fn, args, static_cast<unsigned>(grid), static_cast<unsigned>(shape.threads), shape.smem,
+  if (!launch_dependent(fn, args, static_cast<unsigned>(grid), static_cast<unsigned>(block), shape.smem,
                         q.stream))
     return QCC_ERR_CUDA;
   if (mode == kModeGateUp) return QCC_OK;  // no partial rows to reduce
