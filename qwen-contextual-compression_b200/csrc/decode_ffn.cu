@@ -23,11 +23,12 @@
 // QCC_IDS_READY the next decode starts its record copies right away, before
 // it waits for the launches ahead of it; only x is read after that wait.
 //
-// Thread t of a CTA owns the 8-element hidden slots v = t + k * blockDim.x
-// (k < VPT): it holds x[b, 8v:8v+8] and the partial y[b, 8v:8v+8] in
-// registers, reads the matching 16-byte pieces of every staged record, and
-// all partial dot products meet in one warp-shuffle + shared-memory
-// reduction per group of R records (one __syncthreads per group).
+// Compute thread t of a CTA owns the 8-element hidden slots v = t + k * n
+// (k < VPT, n compute threads): it holds x[b, 8v:8v+8] and the partial
+// y[b, 8v:8v+8] in registers, reads the matching 16-byte pieces of every
+// staged record, and all partial dot products meet in one warp-shuffle +
+// shared-memory reduction per group of R records (one named barrier of the
+// compute warps per group).  A producer warp issues the record copies.
 
 #include <cuda_runtime.h>
 
@@ -208,9 +209,6 @@ __device__ __forceinline__ float warp_reduce_multi(float (&v)[V], int lane) {
   return v[0];
 }
 
-// Shared-memory layout after the record ring (host mirrors it in tail_bytes):
-//   mbarriers [kMaxStages] | warp partials [2][VP][32] f32 | flag [4] i32 |
-//   ids [id_cap] i32 | token bits [id_cap] u8
 // Barrier 1 over the first n threads of the CTA (the compute warps; the
 // producer warp does not take part) that also ORs a predicate across them.
 __device__ __forceinline__ bool compute_barrier_or(bool v, int n) {
@@ -226,6 +224,11 @@ __device__ __forceinline__ bool compute_barrier_or(bool v, int n) {
   return r != 0;
 }
 
+// Shared-memory layout after the record ring (host mirrors it in tail_bytes):
+//   filled mbarriers [kMaxStages] | consumed mbarriers [kMaxStages] |
+//   warp partials [2][VP][32] f32 | flag [4] i32 (flag[0]: the consumers gave
+//   up) | ids [id_cap] i32 | token bits [id_cap] u8
+//
 // DN (whole records only): the down slices are read from the ring when the
 // group is finished, one iteration later, and the group's slots are refilled
 // after that (instead of holding the slices in registers and refilling at
