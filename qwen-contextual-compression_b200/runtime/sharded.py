@@ -141,34 +141,41 @@ class ShardedIndexedFFN:
         return self.engine(x2, local, token_mask=mask if per_token else None, n_ids_dev=count,
                            out_dtype=torch.float32)
 
-    def __call__(self, x: torch.Tensor, ids: torch.Tensor, ids_ready: bool = False) -> torch.Tensor:
-        return self.forward(x, ids, ids_ready=ids_ready)
+    def __call__(self, x: torch.Tensor, ids: torch.Tensor, ids_ready: bool = False,
+                 out: torch.Tensor | None = None) -> torch.Tensor:
+        return self.forward(x, ids, ids_ready=ids_ready, out=out)
 
-    def forward(self, x: torch.Tensor, ids: torch.Tensor, ids_ready: bool = False) -> torch.Tensor:
+    def forward(self, x: torch.Tensor, ids: torch.Tensor, ids_ready: bool = False,
+                out: torch.Tensor | None = None) -> torch.Tensor:
         """y of the whole layer on every rank; ``ids_ready`` as in ``IndexedSparseFFN.forward``
-        (used with one shared 1-D id list and the fused sum)."""
+        (used with one shared 1-D id list and the fused sum).  ``out``: optional [B, hidden] (or
+        [hidden]) tensor in the weight dtype that receives y."""
+        x2 = x if x.ndim == 2 else x.unsqueeze(0)
+        out2 = None if out is None else (out if out.ndim == 2 else out.unsqueeze(0))
         if self.allreduce == "fused" and ids.ndim == 1:
             # One id list for every token: the kernel finds this shard's run.
-            x2 = x if x.ndim == 2 else x.unsqueeze(0)
-            y = self.engine(x2, ids, exchange=self.exchange, id_range=(self.begin, self.end), ids_ready=ids_ready)
+            y = self.engine(x2, ids, exchange=self.exchange, id_range=(self.begin, self.end), ids_ready=ids_ready,
+                            out=out2)
             return y if x.ndim == 2 else y.squeeze(0)
         if self.allreduce == "fused":
             rows = ids if ids.ndim == 2 else ids.unsqueeze(0)
             if rows.dtype != torch.int32:
                 rows = rows.to(torch.int32)
             local, mask, count = build_union(rows.contiguous(), self.begin, self.end)
-            x2 = x if x.ndim == 2 else x.unsqueeze(0)
             y = self.engine(x2, local, token_mask=mask if ids.ndim == 2 else None, n_ids_dev=count,
-                            exchange=self.exchange)
+                            exchange=self.exchange, out=out2)
             return y if x.ndim == 2 else y.squeeze(0)
         y32 = self.partial(x, ids)
         if self.group is not None:
             torch.distributed.all_reduce(y32, group=self.group)
-        out = torch.empty(y32.shape, dtype=self.weights.dtype, device=y32.device)
+        if out2 is None:
+            out2 = torch.empty(y32.shape, dtype=self.weights.dtype, device=y32.device)
+        elif out2.shape != y32.shape or out2.dtype != self.weights.dtype or not out2.is_contiguous():
+            raise ValueError("out must be a contiguous [batch, hidden] tensor in the weight dtype")
         lib = _lib.library()
-        _lib.check(lib.qcc_cast_f32(y32.data_ptr(), out.data_ptr(), y32.numel(), _lib.dtype_code(out.dtype),
+        _lib.check(lib.qcc_cast_f32(y32.data_ptr(), out2.data_ptr(), y32.numel(), _lib.dtype_code(out2.dtype),
                                     _lib.stream_handle(y32.device)), "qcc_cast_f32")
-        return out if x.ndim == 2 else out.squeeze(0)
+        return out2 if x.ndim == 2 else out2.squeeze(0)
 
     def check(self) -> None:
         """Raise if a call since the last check flagged a device-side error (host sync).

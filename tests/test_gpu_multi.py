@@ -55,8 +55,12 @@ def _rank(rank: int, world: int, port: int, queue) -> None:
         y = fused(x, ids)
         y_nccl = nccl(x, ids)
         ys = [fused(x, ids) for _ in range(50)]  # rotating exchange slots, graph-free loop
+        # The caller's output buffer (out=), fused and NCCL paths.
+        y_out, y_nccl_out = torch.empty_like(y), torch.empty_like(y_nccl)
+        fused(x, ids, out=y_out)
+        nccl(x, ids, out=y_nccl_out)
         torch.cuda.synchronize(device)
-        stable = all(torch.equal(y, yi) for yi in ys)
+        stable = all(torch.equal(y, yi) for yi in ys) and torch.equal(y_out, y) and torch.equal(y_nccl_out, y_nccl)
         other = torch.empty_like(y)
         dist.broadcast(other if rank else y.clone(), src=0)
         if rank:
