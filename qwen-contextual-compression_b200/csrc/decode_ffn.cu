@@ -454,9 +454,9 @@ __global__ void __launch_bounds__(kMaxBlock, 1) indexed_ffn_decode_kernel(const 
     Pack8<T> dn_cur[R][VPT];
     float act_cur[R][B];
     bool ok = true;
-    // Finishing group g-1 needs nothing of group g.  At batch 1 it goes first and
-    // runs while group g's records may still be arriving (27.6 against 28.4 us per
-    // layer); at 3-4 tokens the other order measured slightly faster.
+    // Finishing group g-1 needs nothing of group g.  At 1-2 tokens it goes first
+    // and runs while group g's records may still be arriving (27.6 against 28.4 us
+    // per layer at batch 1); at 3-4 tokens the other order measured slightly faster.
     auto finish_prev = [&]() {
       if (rn_prev > 0) {
         // Block totals of group g-1: value q = lane / kLanesPer summed over warps.
@@ -584,7 +584,7 @@ __global__ void __launch_bounds__(kMaxBlock, 1) indexed_ffn_decode_kernel(const 
         }
       }
     };
-    if constexpr (B == 1) {
+    if constexpr (B <= 2) {
       finish_prev();
       dot_group();
     } else {
