@@ -787,15 +787,16 @@ __global__ void __launch_bounds__(1024) decode_reduce_kernel(const ReduceArgs a)
 
 using KernelFn = void (*)(const DecodeArgs);
 
-// Records per barrier group: two for 16-bit weights and up to two tokens,
-// else one (keeps the down slices of two groups in registers).
-template <typename T, int B>
+// Records per barrier group: two for 16-bit weights (every mode and batch),
+// one for fp32, whose records are twice the bytes.
+template <typename T>
 constexpr int group_records() {
-  return (sizeof(T) == 2 && B <= 2) ? 2 : 1;
+  return sizeof(T) == 2 ? 2 : 1;
 }
 
-// Whole records at 3-4 tokens of 16-bit weights: two records per group with the
-// down slices read from the ring (DN), which fits the registers.
+// Whole records at 3-4 tokens of 16-bit weights read their down slices from
+// the ring (DN) instead of holding them in registers, so that two records per
+// group fit the register budget.
 template <typename T, int B, int MODE>
 constexpr bool down_from_ring() {
   return MODE == kModeFull && sizeof(T) == 2 && B >= 3;
@@ -803,8 +804,7 @@ constexpr bool down_from_ring() {
 
 template <typename T, int B, int VPT, int MODE>
 KernelFn kernel_for() {
-  constexpr bool dn = down_from_ring<T, B, MODE>();
-  return indexed_ffn_decode_kernel<T, B, VPT, dn ? 2 : group_records<T, B>(), MODE, dn>;
+  return indexed_ffn_decode_kernel<T, B, VPT, group_records<T>(), MODE, down_from_ring<T, B, MODE>()>;
 }
 
 // Slots of 8 hidden elements per thread: 1, 2 or 4 (hidden <= 2560, 5120,
