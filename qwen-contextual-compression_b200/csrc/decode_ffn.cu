@@ -34,10 +34,12 @@
 
 #include <algorithm>
 #include <mutex>
+#include <type_traits>
 #include <unordered_map>
 
 #include "qcc_common.cuh"
 #include "qcc_host.h"
+#include "qcc_tc.cuh"
 
 namespace qcc {
 
@@ -781,6 +783,8 @@ __global__ void __launch_bounds__(1024) decode_reduce_kernel(const ReduceArgs a)
   }
 }
 
+#include "decode_tc.cuh"
+
 // ---------------------------------------------------------------------------
 // Host side
 // ---------------------------------------------------------------------------
@@ -890,7 +894,8 @@ struct OccHash {
 
 // Blocks per SM for a kernel configuration (after raising the kernel's
 // dynamic shared-memory limit to the device maximum).  0 on failure.
-int blocks_per_sm(KernelFn fn, int device, int threads, size_t smem) {
+template <typename Fn>
+int blocks_per_sm(Fn fn, int device, int threads, size_t smem) {
   static std::mutex mu;
   static std::unordered_map<OccKey, int, OccHash> cache;
   const OccKey key{reinterpret_cast<const void*>(fn), device, threads, smem};
@@ -910,8 +915,8 @@ int blocks_per_sm(KernelFn fn, int device, int threads, size_t smem) {
 // Both launches are programmatic dependents of what precedes them on the
 // stream: the reduce launch is scheduled while the decode CTAs run (it waits
 // for them at entry), and the next decode is scheduled while this reduce runs.
-template <typename Fn, typename Args>
-bool launch_dependent(Fn fn, const Args& args, unsigned grid, unsigned threads, size_t smem, cudaStream_t stream) {
+template <typename Fn, typename... Args>
+bool launch_dependent(Fn fn, unsigned grid, unsigned threads, size_t smem, cudaStream_t stream, const Args&... args) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(threads);
@@ -922,13 +927,20 @@ bool launch_dependent(Fn fn, const Args& args, unsigned grid, unsigned threads, 
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cuda_ok(cudaLaunchKernelEx(&cfg, fn, args));
+  return cuda_ok(cudaLaunchKernelEx(&cfg, fn, args...));
 }
 
 }  // namespace
 
 int decode_max_batch(int hidden, int dtype) {
-  const int vpt = vpt_for(hidden_pad(hidden, dtype));
+  // Eight tokens per launch on the tensor cores when every mode fits (227 KB
+  // of shared memory, a typical id share); else the CUDA-core kernel's limit.
+  const int hp = hidden_pad(hidden, dtype);
+  TcShape s;
+  if (tc_plan(kModeFull, 8, hp, dtype, 232448, 256, &s) && tc_plan(kModeGateUp, 8, hp, dtype, 232448, 256, &s) &&
+      tc_plan(kModeDown, 8, hp, dtype, 232448, 256, &s))
+    return 8;
+  const int vpt = vpt_for(hp);
   return (vpt == 1 || vpt == 2) ? 4 : (vpt == 4 ? 1 : 0);
 }
 
@@ -1045,23 +1057,36 @@ int launch_decode(const DecodeRequest& q) {
   const int n_ids = q.n_ids;
   const int id_cap = std::max(1, (n_ids + std::min(info.num_sms, std::max(1, n_ids)) - 1) /
                                      std::min(info.num_sms, std::max(1, n_ids)));
-  LaunchShape shape;
-  if (!plan_launch(hp, copy_bytes, info.max_smem_optin, id_cap, mode == kModeFull ? kMaxStagesFull : kMaxStages,
-                   &shape))
-    return QCC_ERR_UNSUPPORTED;
-
+  // 2-8 tokens of 16-bit records run on the tensor cores; one token, fp32
+  // records and hidden sizes that are not a multiple of 128 on the CUDA cores.
+  TcShape tc_shape;
+  const bool use_tc = tc_plan(mode, q.batch, hp, q.dtype, info.max_smem_optin, id_cap, &tc_shape);
+  LaunchShape shape = {};
   KernelFn fn = nullptr;
-  if (q.dtype == QCC_DTYPE_BF16)
-    fn = pick_kernel_mode<__nv_bfloat16>(mode, q.batch, shape.vpt);
-  else if (q.dtype == QCC_DTYPE_F16)
-    fn = pick_kernel_mode<__half>(mode, q.batch, shape.vpt);
-  else
-    fn = pick_kernel_mode<float>(mode, q.batch, shape.vpt);
-  if (fn == nullptr) return QCC_ERR_UNSUPPORTED;
-
-  const int block = shape.threads + 32;  // compute threads and the producer warp
-  const int nb = blocks_per_sm(fn, device, block, shape.smem);
-  if (nb <= 0) return QCC_ERR_CUDA;
+  TcKernelFn tc_fn = nullptr;
+  int block = 0;
+  size_t smem = 0;
+  if (use_tc) {
+    tc_fn = q.dtype == QCC_DTYPE_BF16 ? pick_tc_kernel<__nv_bfloat16>(mode, q.batch) : pick_tc_kernel<__half>(mode, q.batch);
+    if (tc_fn == nullptr) return QCC_ERR_UNSUPPORTED;
+    block = kTcThreads;
+    smem = tc_smem_bytes(tc_shape, id_cap);
+    if (blocks_per_sm(tc_fn, device, block, smem) <= 0) return QCC_ERR_CUDA;
+  } else {
+    if (!plan_launch(hp, copy_bytes, info.max_smem_optin, id_cap, mode == kModeFull ? kMaxStagesFull : kMaxStages,
+                     &shape))
+      return QCC_ERR_UNSUPPORTED;
+    if (q.dtype == QCC_DTYPE_BF16)
+      fn = pick_kernel_mode<__nv_bfloat16>(mode, q.batch, shape.vpt);
+    else if (q.dtype == QCC_DTYPE_F16)
+      fn = pick_kernel_mode<__half>(mode, q.batch, shape.vpt);
+    else
+      fn = pick_kernel_mode<float>(mode, q.batch, shape.vpt);
+    if (fn == nullptr) return QCC_ERR_UNSUPPORTED;
+    block = shape.threads + 32;  // compute threads and the producer warp
+    smem = shape.smem;
+    if (blocks_per_sm(fn, device, block, smem) <= 0) return QCC_ERR_CUDA;
+  }
   // At most one CTA per SM (the workspace holds kMaxGrid partial rows); no
   // CTA waits for another, so residency of the whole grid is not required.
   int64_t grid = std::min<int64_t>(info.num_sms, kMaxGrid);
@@ -1114,9 +1139,11 @@ int launch_decode(const DecodeRequest& q) {
   args.act_in_dtype = q.act_in_dtype;
 
   clear_stale_error();
-  if (!launch_dependent(fn, args, static_cast<unsigned>(grid), static_cast<unsigned>(block), shape.smem,
-                        q.stream))
-    return QCC_ERR_CUDA;
+  const bool launched = use_tc ? launch_dependent(tc_fn, static_cast<unsigned>(grid), static_cast<unsigned>(block),
+                                                  smem, q.stream, args, tc_shape)
+                               : launch_dependent(fn, static_cast<unsigned>(grid), static_cast<unsigned>(block), smem,
+                                                  q.stream, args);
+  if (!launched) return QCC_ERR_CUDA;
   if (mode == kModeGateUp) return QCC_OK;  // no partial rows to reduce
 
   ReduceArgs red;
@@ -1142,8 +1169,8 @@ int launch_decode(const DecodeRequest& q) {
                                : nullptr;
   for (int r = 0; r < kMaxRanks; ++r)
     red.xchg[r] = r < q.world && q.world > 1 ? static_cast<uint8_t*>(q.xchg[r]) + kXchgHeader : nullptr;
-  if (!launch_dependent(decode_reduce_kernel, red, static_cast<unsigned>(slices),
-                        static_cast<unsigned>(reduce_threads), 0, q.stream))
+  if (!launch_dependent(decode_reduce_kernel, static_cast<unsigned>(slices), static_cast<unsigned>(reduce_threads), 0,
+                        q.stream, red))
     return QCC_ERR_CUDA;
   return QCC_OK;
 }

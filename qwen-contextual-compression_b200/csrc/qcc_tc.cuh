@@ -137,9 +137,39 @@ __device__ __forceinline__ void tmem_load32(uint32_t taddr, float (&v)[32]) {
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// 16 consecutive fp32 columns of this thread's TMEM lane, waited for.
+__device__ __forceinline__ void tmem_load16(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15}, [%16];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr)
+      : "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
 // ---------------------------------------------------------------------------
 // Descriptors.
 // ---------------------------------------------------------------------------
+
+// Shared-memory matrix descriptor for an operand without swizzle, built from
+// 128-byte core matrices (8 rows of 16 bytes).  For both majors `sbo` is the
+// byte distance between core matrices adjacent in M (or N) and `lbo` the
+// distance between core matrices adjacent in K.  K-major: a core matrix is 8
+// M rows x 8 K elements (rows 16 bytes apart); MN-major: 8 K rows x 8 M
+// elements (K rows 16 bytes apart).
+__device__ __forceinline__ uint64_t smem_desc_none(uint32_t addr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((addr >> 4) & 0x3FFFu);
+  d |= static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16;
+  d |= static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32;
+  d |= 1ull << 46;  // descriptor version for sm_100; layout type 0: no swizzle
+  return d;
+}
 
 // Shared-memory matrix descriptor for a 128-byte-swizzled operand tile.
 // K-major: rows of 128 bytes, groups of 8 rows `sbo` bytes apart (1024 for a

@@ -1,7 +1,9 @@
 """The fused indexed gated-FFN engine (one packed layer on one GPU).
 
 ``IndexedSparseFFN(weights)(x, ids)`` computes, in one call of the C ABI
-(a record-streaming launch and a reduce launch) per chunk of <= 4 tokens,
+(a record-streaming launch and a reduce launch) per chunk of up to
+``max_batch`` tokens (8 for 16-bit records whose hidden size is a multiple
+of 128, which run on the tensor cores; else 4, or 1 above hidden 5120),
 
     y[b] = sum_j mask[j, b] * silu(G[ids_j] . x[b]) * (U[ids_j] . x[b]) * D[:, ids_j]
 
