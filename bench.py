@@ -304,9 +304,9 @@ def measure_selector(engine, x, device, stream, side) -> dict:
 
     out["select_ffn_us_batch1"] = round(graph_time_us(step1, steps, stream, side), 2)
     # Batches of 2, 4 and 8 tokens with their own selections: selector, union of
-    # the ids with per-token bits, one decode over the union (8 tokens: two
-    # launches of 4 over the same union and mask).  union_gbs: the union's
-    # record bytes (+ x, ids, y) over the step time.
+    # the ids with per-token bits, one decode over the union (2-8 tokens: one
+    # tensor-core launch and its reduce).  union_gbs: the union's record bytes
+    # (+ x, ids, y) over the step time.
     for batch in (2, 4, 8):
         scores_b = [workloads.selector_scores(batch, seed=40 + i).to(device) for i in range(steps)]
         ids_b = torch.empty((batch, k), dtype=torch.int32, device=device)
@@ -446,7 +446,8 @@ def measure_dense_and_oracle(device, stream, side, sparse_us: float) -> dict:
         torch_us = graph_time_us(torch_step, steps, stream, side)
         out[f"oracle_mode_tokens{rows}"] = {
             "us": round(us, 2), "algorithmic_bytes": nbytes, "gbs": round(nbytes / (us * 1e-6) / 1e9, 1),
-            "union_records": union, "k": k, "launches": 4 * ((rows + 3) // 4) + 1,
+            "union_records": union, "k": k,
+            "launches": 4 * ((rows + engines[0].max_batch - 1) // engines[0].max_batch) + 1,
             "reference_formulation_torch_us": round(torch_us, 2)}
         for e in engines:
             e.check()

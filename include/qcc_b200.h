@@ -120,8 +120,12 @@ QCC_API int qcc_pack_records(const void* gate, const void* up, int64_t ld_gu, co
 /* Fused indexed gated FFN (decode / small batch)                          */
 /* ---------------------------------------------------------------------- */
 
-/* Largest batch one qcc_indexed_ffn_decode call accepts: 4 for hidden <=
- * 5120, 1 for hidden <= 10240 (four hidden slots per thread), 0 beyond. */
+/* Largest batch one qcc_indexed_ffn_decode call accepts (the same bound
+ * holds for qcc_ffn_activations and qcc_indexed_ffn_down).  bf16 / fp16
+ * records whose hidden size rounded up to 8 is a multiple of 128 run 2 or
+ * more tokens on the tensor cores: 8 up to hidden 6144, 6 up to 8192, 4 up
+ * to 10240.  Otherwise (fp32, other sizes) 4 for hidden <= 5120 and 1 for
+ * hidden <= 10240; 0 beyond 10240. */
 QCC_API int qcc_decode_max_batch(int hidden, int dtype);
 
 /* Bytes of workspace qcc_indexed_ffn_decode needs for this batch/hidden. */

@@ -933,15 +933,21 @@ bool launch_dependent(Fn fn, unsigned grid, unsigned threads, size_t smem, cudaS
 }  // namespace
 
 int decode_max_batch(int hidden, int dtype) {
-  // Eight tokens per launch on the tensor cores when every mode fits (227 KB
-  // of shared memory, a typical id share); else the CUDA-core kernel's limit.
+  // The CUDA-core kernel's limit (4 tokens with <= 2 hidden slots per thread,
+  // 1 with 4, none beyond), raised to the largest batch <= 8 that the
+  // tensor-core kernel plans in every mode (227 KB of shared memory, a typical
+  // id share): 8 up to hidden 6144, 6 up to 8192, 4 up to 10240.
   const int hp = hidden_pad(hidden, dtype);
-  TcShape s;
-  if (tc_plan(kModeFull, 8, hp, dtype, 232448, 256, &s) && tc_plan(kModeGateUp, 8, hp, dtype, 232448, 256, &s) &&
-      tc_plan(kModeDown, 8, hp, dtype, 232448, 256, &s))
-    return 8;
   const int vpt = vpt_for(hp);
-  return (vpt == 1 || vpt == 2) ? 4 : (vpt == 4 ? 1 : 0);
+  const int cuda_cores = (vpt == 1 || vpt == 2) ? 4 : (vpt == 4 ? 1 : 0);
+  if (cuda_cores == 0) return 0;
+  for (int b = 8; b > cuda_cores; --b) {
+    TcShape s;
+    if (tc_plan(kModeFull, b, hp, dtype, 232448, 256, &s) && tc_plan(kModeGateUp, b, hp, dtype, 232448, 256, &s) &&
+        tc_plan(kModeDown, b, hp, dtype, 232448, 256, &s))
+      return b;
+  }
+  return cuda_cores;
 }
 
 size_t decode_workspace_bytes(int batch, int hidden, int dtype) {

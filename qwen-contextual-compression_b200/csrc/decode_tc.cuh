@@ -460,56 +460,74 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_decode_kernel(const DecodeAr
         *s_abort = 1;
         if (lane == 0) atomicOr(a.status, QCC_DEV_TIMEOUT);
       }
-      if constexpr (kDN) {
-        // This CTA's y -> its partial row ([B][seg], slice-major float4 columns
-        // as the reduce launch reads them).  A CTA with no records stores zeros.
-        bool yok = cnt > 0 && tc_wait_warp(y_full, 0, s_abort, lane);
-        if (cnt > 0 && !yok && lane == 0) atomicOr(a.status, QCC_DEV_TIMEOUT);
-        tc_fence_after_sync();
-        const int per = a.part_per;
-        const int grid = gridDim.x;
-        const int nvec = B * seg / 4;
-        const uint32_t t_y = tmem + (kGU ? 2 * N : 0);
-        // Tile by tile through shared memory (the ring is idle now): lane
-        // (g, m) of token t holds y_t[1024 j + 64 g + 8 kk + m], kk < 8; the
-        // four warps write the tile's [B][1024] fp32 rows, then store them as
-        // float4 columns in the slice-major partial-row layout.
-        float* stage = reinterpret_cast<float*>(ring);
-        for (int j = 0; j < L.n_tiles; ++j) {
-          const int hrow = 64 * (row >> 3) + (row & 7);
+    }
+  }
+
+  if constexpr (kDN) {
+    // This CTA's y -> its partial row ([B][seg] fp32, slice-major float4
+    // columns as the reduce launch reads them), tile by tile through the idle
+    // ring: the epilogue warps move the tile from TMEM (lane (g, m) of token
+    // t holds y_t[1024 j + 64 g + 8 kk + m], kk < 8) into rows of 1152 floats
+    // (8 padding floats after every 64 keep the stores free of bank
+    // conflicts), then all warps store it as float4 columns.  A CTA with no
+    // records stores zeros.
+    __syncwarp();
+    const bool epi = warp >= 3;
+    bool yok = false;
+    if (epi) {
+      yok = cnt > 0 && tc_wait_warp(y_full, 0, s_abort, lane);
+      if (cnt > 0 && !yok && lane == 0) atomicOr(a.status, QCC_DEV_TIMEOUT);
+      tc_fence_after_sync();
+    }
+    constexpr int kRow = kTcTile + 128;
+    const int quarter = warp & 3;
+    const int row = 32 * quarter + lane;
+    const int hrow = 64 * (row >> 3) + (row & 7) + 8 * (row >> 3);  // padded position of kk = 0
+    const uint32_t t_y = tmem + (kGU ? 2 * N : 0) + (static_cast<uint32_t>(32 * quarter) << 16);
+    const int per = a.part_per;
+    const float inv_per = 1.f / static_cast<float>(per);
+    const int grid = gridDim.x;
+    const int nvec = B * seg / 4;
+    float* stage = reinterpret_cast<float*>(ring);
+    for (int j = 0; j < L.n_tiles; ++j) {
+      if (epi) {
+        constexpr int kPiece = N % 32 == 0 ? 32 : 16;
 #pragma unroll
-          for (int t2 = 0; t2 < TP; t2 += 2) {
-            float v[16];
-            if (yok) {
-              tmem_load16(t_y + (static_cast<uint32_t>(32 * quarter) << 16) + j * N + 8 * t2, v);
-            } else {
+        for (int c0 = 0; c0 < N; c0 += kPiece) {
+          float v[kPiece];
+          if (yok) {
+            if constexpr (kPiece == 32)
+              tmem_load32(t_y + j * N + c0, v);
+            else
+              tmem_load16(t_y + j * N + c0, v);
+          } else {
 #pragma unroll
-              for (int e = 0; e < 16; ++e) v[e] = 0.f;
-            }
-#pragma unroll
-            for (int tt = 0; tt < 2; ++tt)
-              if (t2 + tt < B) {
-#pragma unroll
-                for (int kk = 0; kk < 8; ++kk) stage[(t2 + tt) * kTcTile + hrow + 8 * kk] = v[tt * 8 + kk];
-              }
+            for (int e = 0; e < kPiece; ++e) v[e] = 0.f;
           }
-          asm volatile("bar.sync 2, 128;" ::: "memory");
-          const int tile_el = min(kTcTile, seg - j * kTcTile);
-          const int n4 = B * (tile_el / 4);
-          for (int w = row; w < n4; w += 128) {
-            const int t = w / (tile_el / 4);
-            const int h4 = w - t * (tile_el / 4);
-            const float4 val = reinterpret_cast<const float4*>(stage + t * kTcTile)[h4];
-            const int c = (t * seg + j * kTcTile) / 4 + h4;
-            const int blk = c / per;
-            const int width = min(per, nvec - blk * per);
-            __stcg(a.partials + static_cast<int64_t>(blk) * grid * per + static_cast<int64_t>(blockIdx.x) * width +
-                       (c - blk * per),
-                   val);
+#pragma unroll
+          for (int e = 0; e < kPiece; ++e) {
+            const int t = (c0 + e) >> 3;
+            const int kk = (c0 + e) & 7;
+            if (t < B) stage[t * kRow + hrow + 8 * kk] = v[e];
           }
-          asm volatile("bar.sync 2, 128;" ::: "memory");
         }
       }
+      asm volatile("bar.sync 2, %0;" ::"r"(kTcThreads) : "memory");
+      const int q4 = min(kTcTile, seg - j * kTcTile) / 4;
+      for (int w = tid; w < B * q4; w += kTcThreads) {
+        const int t = w / q4;
+        const int h = 4 * (w - t * q4);
+        const float4 val = *reinterpret_cast<const float4*>(stage + t * kRow + h + 8 * (h >> 6));
+        const int c = (t * seg + j * kTcTile + h) / 4;
+        int blk = __float2int_rz(static_cast<float>(c) * inv_per);
+        if (blk * per > c) --blk;
+        if ((blk + 1) * per <= c) ++blk;
+        const int width = min(per, nvec - blk * per);
+        __stcg(a.partials + static_cast<int64_t>(blk) * grid * per + static_cast<int64_t>(blockIdx.x) * width +
+                   (c - blk * per),
+               val);
+      }
+      asm volatile("bar.sync 2, %0;" ::"r"(kTcThreads) : "memory");
     }
   }
   __syncwarp();

@@ -2,8 +2,8 @@
 
 ``IndexedSparseFFN(weights)(x, ids)`` computes, in one call of the C ABI
 (a record-streaming launch and a reduce launch) per chunk of up to
-``max_batch`` tokens (8 for 16-bit records whose hidden size is a multiple
-of 128, which run on the tensor cores; else 4, or 1 above hidden 5120),
+``max_batch`` tokens (``qcc_decode_max_batch``: 8 at hidden 5120 for 16-bit
+records, whose 2-8 token chunks run on the tensor cores),
 
     y[b] = sum_j mask[j, b] * silu(G[ids_j] . x[b]) * (U[ids_j] . x[b]) * D[:, ids_j]
 

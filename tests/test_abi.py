@@ -42,9 +42,16 @@ def test_pure_host_queries_without_gpu():
     assert lib.qcc_hidden_pad(5, _lib.DTYPE_F32) == 8
     assert lib.qcc_record_bytes(5120, _lib.DTYPE_BF16) == 30720
     assert lib.qcc_record_bytes(5120, _lib.DTYPE_F32) == 61440
-    assert lib.qcc_decode_max_batch(5120, _lib.DTYPE_BF16) == 4
-    assert lib.qcc_decode_max_batch(8192, _lib.DTYPE_BF16) == 1
-    assert lib.qcc_decode_max_batch(2560, _lib.DTYPE_BF16) == 4
+    # 2-8 tokens of 16-bit records with hidden % 128 == 0 run on the tensor cores.
+    assert lib.qcc_decode_max_batch(5120, _lib.DTYPE_BF16) == 8
+    assert lib.qcc_decode_max_batch(5120, _lib.DTYPE_F16) == 8
+    assert lib.qcc_decode_max_batch(2560, _lib.DTYPE_BF16) == 8
+    assert lib.qcc_decode_max_batch(8192, _lib.DTYPE_BF16) == 6
+    assert lib.qcc_decode_max_batch(10240, _lib.DTYPE_BF16) == 4
+    # fp32 records and other sizes: the CUDA-core kernel's limits.
+    assert lib.qcc_decode_max_batch(5120, _lib.DTYPE_F32) == 4
+    assert lib.qcc_decode_max_batch(5000, _lib.DTYPE_BF16) == 4
+    assert lib.qcc_decode_max_batch(8192, _lib.DTYPE_F32) == 1
     assert lib.qcc_decode_max_batch(20480, _lib.DTYPE_BF16) == 0
     # status / counters header + one fp32 partial row per CTA (up to 160 CTAs)
     assert lib.qcc_decode_workspace_bytes(1, 5120, _lib.DTYPE_BF16) == 256 + 160 * 5120 * 4
