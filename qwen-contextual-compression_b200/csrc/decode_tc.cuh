@@ -470,13 +470,14 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_decode_kernel(const DecodeAr
     // t holds y_t[1024 j + 64 g + 8 kk + m], kk < 8) into rows of 1152 floats
     // (8 padding floats after every 64 keep the stores free of bank
     // conflicts), then all warps store it as float4 columns.  A CTA with no
-    // records stores zeros.
+    // records (or a layer with none) stores zeros.
     __syncwarp();
     const bool epi = warp >= 3;
     bool yok = false;
     if (epi) {
-      yok = cnt > 0 && tc_wait_warp(y_full, 0, s_abort, lane);
-      if (cnt > 0 && !yok && lane == 0) atomicOr(a.status, QCC_DEV_TIMEOUT);
+      // y is in TMEM only if some group ran (no records: an empty shard).
+      yok = n_groups > 0 && tc_wait_warp(y_full, 0, s_abort, lane);
+      if (n_groups > 0 && !yok && lane == 0) atomicOr(a.status, QCC_DEV_TIMEOUT);
       tc_fence_after_sync();
     }
     constexpr int kRow = kTcTile + 128;

@@ -101,6 +101,20 @@ def test_ids_outside_the_records_are_flagged_and_skipped():
     assert offn.rel_l2(y.double().cpu().numpy(), expected) <= 1e-4
 
 
+def test_empty_shard_at_four_tokens():
+    # A layer slice with no records: every id is outside it, y is zero and the ids are flagged.
+    layer = workloads.decode_layer(hidden=1024, intermediate=2048, device="cuda", seed=13)
+    empty = IndexedSparseFFN(PackedFFNWeights(layer.packed[:0], 1024, 0, 0, 2048))
+    x = workloads.decode_x(batch=4, hidden=1024).cuda()
+    ids = torch.arange(0, 600, dtype=torch.int32, device="cuda")
+    y = empty(x, ids, out_dtype=torch.float32)
+    assert torch.count_nonzero(y) == 0
+    with pytest.raises(ValueError, match="range"):
+        empty.check()
+    assert torch.count_nonzero(empty(x, ids, id_range=(0, 0), out_dtype=torch.float32)) == 0
+    empty.check()
+
+
 def test_activation_output_at_three_tokens():
     h, n, batch = 1024, 900, 3
     gate, up, down = _layer(h, n, torch.bfloat16, seed=21)
