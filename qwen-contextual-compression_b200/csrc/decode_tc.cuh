@@ -31,9 +31,10 @@
 // records.  Warp 0 streams each group's records into a ring of 32 KB stages
 // with one 2 KB bulk copy per record and stage (its lanes issue them): the
 // gate parts in chunks of 1024 elements, then the up parts, then the down
-// parts in tiles of 1024 elements.  (The bulk-copy unit costs about 40 ns per
-// copy, so copies of 1 KB held a stage to ~25 GB/s per SM; 16-byte cp.async
-// pieces from two warps were slower still.)  Warp 2 holds the
+// parts in tiles of 1024 elements.  (A bulk copy costs about 20 ns plus its
+// bytes at ~52 GB/s per SM: copies of 1 KB held a stage to ~25 GB/s per SM,
+// 2 KB copies reach ~38 GB/s; 16-byte cp.async pieces, alone or beside the
+// bulk copies, were slower.)  Warp 1 only joins the block barriers.  Warp 2 holds the
 // tensor memory and issues the MMAs (gate and up accumulators of 8 x tokens
 // columns, y accumulators of the same width per 1024-element tile), releasing
 // each stage with tcgen05.commit.  Warps 3-6 (one per TMEM lane quarter) read the
@@ -46,8 +47,8 @@ constexpr int kTcChunk = 1024;       // gate or up elements per record and stage
 constexpr int kTcTile = 1024;        // hidden elements per y tile (M = 128 = 16 x 64)
 constexpr int kTcStageBytes = 32768;
 constexpr int kTcMaxStages = 6;
-constexpr int kTcThreads = 224;      // two producer warps, MMA warp, four epilogue warps
-constexpr int kTcProducers = 64;
+constexpr int kTcThreads = 224;      // producer warp, idle warp, MMA warp, four epilogue warps
+constexpr int kTcProducers = 64;     // warps 0-1; the x rows are staged by warps 2-6
 constexpr int kTcTailFixed = 256;    // mbarriers, TMEM address, give-up flag, counts
 
 struct TcShape {
