@@ -82,6 +82,17 @@ def test_argument_validation_happens_before_any_cuda_call():
     args[8] = _lib.INDEX_I32 | _lib.IDS_READY
     args[2] = 0
     assert lib.qcc_indexed_ffn_decode(*args) == _lib.ERR_SHAPE  # the flag is accepted, batch 0 is not
+    # Batches beyond qcc_decode_max_batch: 5 tokens of fp32 records (limit 4), 7 at hidden 8192 (limit 6); more
+    # than 8 tokens never fit the token-mask byte.
+    args[8] = _lib.INDEX_I32
+    args[2], args[3], args[6], args[16] = 5, 5120, _lib.DTYPE_F32, _lib.DTYPE_F32
+    args[1], args[15] = 5120, 5120
+    assert lib.qcc_indexed_ffn_decode(*args) == _lib.ERR_UNSUPPORTED
+    args[2], args[3], args[6], args[16] = 7, 8192, _lib.DTYPE_BF16, _lib.DTYPE_BF16
+    args[1], args[15] = 8192, 8192
+    assert lib.qcc_indexed_ffn_decode(*args) == _lib.ERR_UNSUPPORTED
+    args[2] = 9
+    assert lib.qcc_indexed_ffn_decode(*args) == _lib.ERR_SHAPE
     # QCC_MASK_SHIFT(s): the call's tokens must fit bits s .. s + batch - 1 of the mask byte.
     args[2] = 4
     args[8] = _lib.INDEX_I32 | _lib.mask_shift(5)
