@@ -20,6 +20,7 @@ in float64 and check that they compute the gated FFN:
 from __future__ import annotations
 
 import numpy as np
+import pytest
 import torch
 
 GROUP, CHUNK, TILE = 16, 1024, 1024  # records per group, gate|up elements per stage, hidden elements per y tile
@@ -54,19 +55,22 @@ def _setup(seed, hidden, tokens):
     return gate, up, down, x
 
 
-def test_gate_up_diagonal_sums_are_the_dot_products():
-    hidden, tp = 2048, 4
+@pytest.mark.parametrize("hidden", [2048, 3584])
+def test_gate_up_diagonal_sums_are_the_dot_products(hidden):
+    # 3584: the last gate / up chunk holds 512 elements (four K steps of 128 instead of eight).
+    tp = 4
     n = 8 * tp
     gate, up, _, x = _setup(0, hidden, tp)
     xs = x.reshape(-1)  # token rows hidden * 2 bytes apart (the kernel's x staging)
     accs = []
     for part in (gate, up):
         acc = np.zeros((128, n))
-        for c in range(hidden // CHUNK):
-            stage = np.zeros(GROUP * TILE)  # record r's chunk at r * 2 KB
+        for c in range((hidden + CHUNK - 1) // CHUNK):
+            el = min(CHUNK, hidden - c * CHUNK)
+            stage = np.full(GROUP * TILE, np.nan)  # record r's chunk at r * 2 KB; the rest is never read
             for r in range(GROUP):
-                stage[r * TILE:r * TILE + CHUNK] = part[r, c * CHUNK:(c + 1) * CHUNK]
-            for k in range(CHUNK // 128):
+                stage[r * TILE:r * TILE + el] = part[r, c * CHUNK:c * CHUNK + el]
+            for k in range(el // 128):
                 a = _kmajor(stage, 256 * k, 128, CHUNK * 2, 128)
                 b = _kmajor(xs, (c * CHUNK + 128 * k) * 2, 128, hidden * 2, n)
                 acc += a @ b.T
@@ -79,8 +83,13 @@ def test_gate_up_diagonal_sums_are_the_dot_products():
         np.testing.assert_allclose(diag[1], up @ x[t], rtol=1e-12, atol=1e-12)
 
 
-def test_down_tiles_with_split_activations_give_y():
-    hidden, tp, rn = 2048, 4, 13  # an odd group: the last pair repeats record 12 with a zero activation
+@pytest.mark.parametrize("hidden", [2048, 3584])
+@pytest.mark.parametrize("rn", [1, 13, 16])
+def test_down_tiles_with_split_activations_give_y(hidden, rn):
+    # rn records in the group; an odd group's last MMA step repeats its last record with a zero
+    # activation.  3584: the last tile holds 512 elements; rows past them read unwritten memory
+    # and are not stored.
+    tp = 4
     n = 8 * tp
     _, _, down, _ = _setup(1, hidden, tp)
     act = np.random.default_rng(2).standard_normal((tp, GROUP)) * 3.0
@@ -94,11 +103,12 @@ def test_down_tiles_with_split_activations_give_y():
             for i in range(8):  # element t * 1024 + r * 64 + 9 i: the diagonal of block (t, r)
                 bhi[t * 1024 + r * 64 + 9 * i] = hi[t, r]
                 blo[t * 1024 + r * 64 + 9 * i] = lo[t, r]
-    y = np.zeros((tp, hidden))
-    for j in range(hidden // TILE):
-        stage = np.full(GROUP * TILE, np.nan)  # slots past the group stay unread
-        for s in range(rn + (rn & 1)):
-            stage[s * TILE:(s + 1) * TILE] = down[min(s, rn - 1), j * TILE:(j + 1) * TILE]
+    y = np.full((tp, hidden), np.nan)
+    for j in range((hidden + TILE - 1) // TILE):
+        el = min(TILE, hidden - j * TILE)
+        stage = np.full(GROUP * TILE, np.nan)  # slots past the group and past el stay unwritten
+        for s_ in range(rn + (rn & 1)):
+            stage[s_ * TILE:s_ * TILE + el] = down[min(s_, rn - 1), j * TILE:j * TILE + el]
         acc = np.zeros((128, n))
         for p in range((rn + 1) // 2):
             a = _mnmajor(stage, p * 2 * TILE * 2, TILE * 2, 128, 128)
@@ -107,7 +117,9 @@ def test_down_tiles_with_split_activations_give_y():
         lane = np.arange(128)[:, None]
         col = np.arange(n)[None, :]
         h = j * TILE + 64 * (lane // 8) + 8 * (col % 8) + lane % 8
-        y[col // 8, h] = acc
+        keep = np.broadcast_to(h < hidden, acc.shape)
+        tok = np.broadcast_to(col // 8, acc.shape)
+        y[tok[keep], h[keep]] = acc[keep]
     expected = act @ down  # y_t = sum_r a[t, r] D[:, r]
     # The high and low parts carry the activation to ~2^-17 relative.
     np.testing.assert_allclose(y, expected, rtol=0, atol=1e-5 * np.abs(expected).max())
